@@ -1,0 +1,603 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200-native attention / Gated DeltaNet hot path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload attn_c5|attn_c1|attn_c2|gdn_decode|gdn_prefill]
+
+One JSON line on stdout (rank 0).  The headline workload is the long-context
+causal GQA attention config (B4 Hq32 Hkv8 S16384 D128 bf16), the config the
+reference's metric is sharded across 1/2/4/8 GPUs on; GDN decode (GB/s) and
+GDN prefill (tok/s) are reported in the same line under "secondary".
+
+Multi-GPU: one process per GPU (torchrun), units sharded across ranks with no
+data-path collective -- attention by (batch, kv-head) with its q-heads, GDN
+decode by sequence, GDN prefill by v-head.  Timing: CUDA events on the stream
+the kernels are launched on, barrier + synchronize around the timed region,
+MAX over ranks.  The optional NCCL all-gather of attention outputs is timed
+separately ("allgather").
+
+--impl reference: the CPU implementation of the path timed on this host's
+cores (the reference has no CPU attention, so the fp64 restatement of its
+naive kernel in oracle/ stands in), on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "turing-sm75_b200"))
+sys.path.insert(0, ROOT)
+
+BASELINE_METRIC = "attn fwd TFLOP/s, GDN prefill tok/s, GDN decode GB/s; % roofline @1/2/4/8 GPU"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+# ----------------------------------------------------------------------------
+# small utilities
+# ----------------------------------------------------------------------------
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return {k: float(d[k]) for k in FALLBACK_PEAKS}, "measured"
+    except Exception:
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def profile_traffic(name):
+    """Per-launch DRAM bytes of the dominant kernel, read from the committed ncu
+    summary profiles/<name>.md (line `traffic_bytes_per_launch: <float>`)."""
+    path = os.path.join(ROOT, "profiles", f"{name}.md")
+    try:
+        for line in open(path):
+            if line.strip().startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].strip().split()[0])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML while running."""
+
+    NAMES = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+        0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+        0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+        0x100: "display_clock_setting",
+    }
+
+    def __init__(self, torch_device, period_s=0.05):
+        self.period = period_s
+        self.samples = []
+        self.max_mhz = None
+        self.err = None
+        self._stop = threading.Event()
+        self._t = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            import torch
+            uuid = "GPU-" + str(torch.cuda.get_device_properties(torch_device).uuid)
+            self.h = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+            self.nv = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # NVML missing: report, do not fail the bench
+            self.h = None
+            self.err = repr(e)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                mhz = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
+                rs = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.samples.append((mhz, rs))
+            except Exception as e:
+                self.err = repr(e)
+            self._stop.wait(self.period)
+
+    def __enter__(self):
+        if self.h is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t:
+            self._t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0,
+                    "note": self.err or "no samples"}
+        busy = [s for s in self.samples if not (s[1] & 0x1)] or self.samples
+        reasons = set()
+        for _, r in busy:
+            for bit, name in self.NAMES.items():
+                if r & bit and bit != 0x1:
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(m for m, _ in busy), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(busy)}
+
+
+# ----------------------------------------------------------------------------
+# distributed plumbing
+# ----------------------------------------------------------------------------
+class Dist:
+    def __init__(self, want_gpus):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        if self.world != want_gpus:
+            raise SystemExit(f"--gpus {want_gpus} but WORLD_SIZE={self.world}")
+        self.pg = None
+
+    def init(self):
+        import torch
+        torch.cuda.set_device(self.local)
+        if self.world > 1:
+            import datetime
+            import torch.distributed as dist
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier()
+
+    def max(self, x):
+        if not self.pg:
+            return x
+        import torch
+        t = torch.tensor([float(x)], device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+def split_units(total, world, rank):
+    if total % world:
+        raise SystemExit(f"{total} units do not split over {world} GPUs")
+    n = total // world
+    return rank * n, n
+
+
+# ----------------------------------------------------------------------------
+# workloads (ours)
+# ----------------------------------------------------------------------------
+def attn_shard(cfg, world, rank):
+    """(batch, kv-head) units with their q-heads; returns the local (B, Hq, Hkv)."""
+    units = cfg["B"] * cfg["Hkv"]
+    u0, n = split_units(units, world, rank)
+    group = cfg["Hq"] // cfg["Hkv"]
+    if n >= cfg["Hkv"]:
+        return n // cfg["Hkv"], cfg["Hq"], cfg["Hkv"]
+    return 1, n * group, n
+
+
+def attn_flops(B, Hq, S, D, causal):
+    return (2.0 * B * Hq * S * (S + 1) * D) if causal else (4.0 * B * Hq * S * S * D)
+
+
+def bench_attention(name, cfg, args, dist, peaks):
+    import torch
+    import b200lab
+    import workloads
+
+    B, Hq, Hkv = attn_shard(cfg, dist.world, dist.rank)
+    S, D, causal, dtype = cfg["S"], cfg["D"], cfg["causal"], cfg["dtype"]
+    dev = torch.device("cuda", dist.local)
+    Q, K, V = workloads.attn_inputs(B, Hq, Hkv, S, D, dtype, seed=42 + dist.rank, device=dev)
+    O = torch.empty_like(Q)
+    stream = torch.cuda.current_stream()
+    flops_local = attn_flops(B, Hq, S, D, causal)
+    flops_total = attn_flops(cfg["B"], cfg["Hq"], S, D, causal)
+    in_bytes = (Q.numel() + K.numel() + V.numel()) * Q.element_size()
+
+    def step():
+        b200lab.attn_fwd(Q, K, V, causal=causal, out=O, stream=stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    n0 = b200lab.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    launches = b200lab.launch_count() - n0
+    dist.barrier()
+    torch.cuda.synchronize()
+    ms_local = e0.elapsed_time(e1) / args.steps
+    ms = dist.max(ms_local)
+    status = b200lab.device_status()
+    if status != b200lab.OK:
+        raise RuntimeError(f"device status {status}: {b200lab.strerror(status)}")
+
+    # end to end: pinned host inputs -> device, kernel, result -> pinned host
+    Qh, Kh, Vh = (t.cpu().pin_memory() for t in (Q, K, V))
+    Oh = torch.empty(O.shape, dtype=O.dtype, pin_memory=True)
+    e2e_steps = max(3, min(args.steps, 10))
+
+    def e2e_step():
+        Q.copy_(Qh, non_blocking=True)
+        K.copy_(Kh, non_blocking=True)
+        V.copy_(Vh, non_blocking=True)
+        b200lab.attn_fwd(Q, K, V, causal=causal, out=O, stream=stream)
+        Oh.copy_(O, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = dist.max(e0.elapsed_time(e1) / e2e_steps)
+
+    # optional NCCL all-gather of the output shards (timed on its own)
+    allgather = None
+    if dist.world > 1:
+        import torch.distributed as tdist
+        gathered = torch.empty((dist.world,) + tuple(O.shape), dtype=O.dtype, device=dev)
+        for _ in range(2):
+            tdist.all_gather_into_tensor(gathered, O)
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0.record(stream)
+        for _ in range(3):
+            tdist.all_gather_into_tensor(gathered, O)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ag_ms = dist.max(e0.elapsed_time(e1) / 3)
+        allgather = {"ms": ag_ms, "bytes_per_rank_out": O.numel() * O.element_size(),
+                     "kernel_plus_allgather_ms": ms + ag_ms}
+        del gathered
+
+    tflops = flops_total / (ms * 1e-3) / 1e12
+    achieved = flops_local / (ms_local * 1e-3) / 1e12
+    peak = peaks["bf16_tflops"]
+    traffic = profile_traffic(f"attn_fwd_{name}")
+    res = {
+        "metric": BASELINE_METRIC if name == "attn_c5" else f"attn fwd TFLOP/s ({name})",
+        "value": tflops, "unit": "TFLOP/s", "ms_per_step": ms,
+        "flops_per_step": flops_total, "flop_convention": "causal-exec 2*B*H*S*(S+1)*D"
+        if causal else "4*B*H*S^2*D",
+        "dtype": "bf16" if dtype == torch.bfloat16 else "fp16",
+        "config": {"workload": name, "B": cfg["B"], "Hq": cfg["Hq"], "Hkv": cfg["Hkv"], "S": S,
+                   "D": D, "causal": causal, "sharding": "(batch, kv-head) units",
+                   "local_shape": [B, Hq, Hkv, S, D],
+                   "l2": f"inputs larger than L2 ({in_bytes / 1e6:.0f} MB per GPU)"
+                   if in_bytes > 126e6 else "inputs smaller than L2 (back to back)"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak,
+                     # profiles/ records DRAM bytes of one full-config launch (N=1);
+                     # a shard moves its units' share
+                     "traffic": None if traffic is None else traffic * flops_local / flops_total},
+        "e2e": {"value": flops_total / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": O.numel() * O.element_size()},
+        "gpu_launches": int(launches),
+        "clocks": clk.summary(),
+    }
+    if allgather:
+        res["allgather"] = allgather
+    del Q, K, V, O, Qh, Kh, Vh, Oh
+    torch.cuda.empty_cache()
+    return res
+
+
+def bench_gdn_decode(cfg, args, dist, peaks):
+    import torch
+    import b200lab
+    import workloads
+
+    u0, Bl = split_units(cfg["B"], dist.world, dist.rank)
+    Hqk, Hv, d, T = cfg["Hqk"], cfg["Hv"], cfg["d"], cfg["steps"]
+    dtype = cfg["dtype"]
+    dev = torch.device("cuda", dist.local)
+    state = workloads.gdn_state(Bl, Hv, d, std=0.02, seed=3 + dist.rank, device=dev)
+    steps_in = [workloads.gdn_decode_inputs(Bl, Hqk, Hv, d, dtype, seed=1000 * dist.rank + t,
+                                            device=dev) for t in range(T)]
+    out = torch.empty((T, Bl, Hv, d), dtype=dtype, device=dev)
+    stream = torch.cuda.current_stream()
+    esz = torch.tensor([], dtype=dtype).element_size()
+    bytes_step_local = (Bl * Hv * d * d * 4 * 2 + Bl * Hqk * d * esz * 2 + Bl * Hv * d * esz * 2
+                        + Bl * Hv * 4 * 2)
+
+    def run_all():
+        for t in range(T):
+            q, k, v, g, b = steps_in[t]
+            b200lab.gdn_decode(q, k, v, g, b, state, out=out[t], stream=stream)
+
+    run_all()  # warm-up: one pass of the 256-step sequence
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    n0 = b200lab.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev) as clk:
+        e0.record(stream)
+        run_all()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    launches = b200lab.launch_count() - n0
+    ms_local = e0.elapsed_time(e1) / T
+    ms = dist.max(ms_local)
+    gbs = bytes_step_local * dist.world / (ms * 1e-3) / 1e9
+    achieved = bytes_step_local / (ms_local * 1e-3) / 1e9
+    traffic = profile_traffic("gdn_decode_c4")
+    res = {"metric": "GDN decode GB/s", "value": gbs, "unit": "GB/s", "us_per_step": ms * 1e3,
+           "steps": T, "bytes_per_step": bytes_step_local * dist.world,
+           "config": {"workload": "gdn_decode_c4", "B": cfg["B"], "Hqk": Hqk, "Hv": Hv, "d": d,
+                      "state": "fp32 [B,Hv,128,128] in place", "sharding": "sequences",
+                      "l2": "state larger than L2 (134 MB at N=1), 256 consecutive steps"},
+           "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                        "frac": achieved / peaks["hbm_gbs"], "traffic": traffic},
+           "gpu_launches": int(launches), "clocks": clk.summary()}
+    del state, steps_in, out
+    torch.cuda.empty_cache()
+    return res
+
+
+def bench_gdn_prefill(cfg, args, dist, peaks):
+    import torch
+    import b200lab
+    import workloads
+
+    T, Hqk, Hv, d, dtype = cfg["T"], cfg["Hqk"], cfg["Hv"], cfg["d"], cfg["dtype"]
+    h0, Hv_l = split_units(Hv, dist.world, dist.rank)
+    Hqk_l = min(Hqk, Hv_l)
+    dev = torch.device("cuda", dist.local)
+    q, k, v, g, b = workloads.gdn_inputs(1, T, Hqk_l, Hv_l, d, dtype, seed=7 + dist.rank, device=dev)
+    state = torch.zeros((1, Hv_l, d, d), dtype=torch.float32, device=dev)
+    out = torch.empty((1, T, Hv_l, d), dtype=dtype, device=dev)
+    stream = torch.cuda.current_stream()
+    ws_bytes = b200lab.gdn_prefill_workspace_bytes(1, T, Hqk_l, Hv_l, d, d)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+
+    def step():
+        b200lab.gdn_prefill(q, k, v, g, b, state, out=out, workspace=ws, stream=stream)
+
+    try:
+        step()
+    except b200lab.B200LabError as e:
+        return {"metric": "GDN prefill tok/s", "status": str(e)}
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    n0 = b200lab.launch_count()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    with ClockSampler(dev) as clk:
+        for e0, e1 in evs:
+            flush.zero_()  # inputs (106 MB) fit in L2: flush it between timed launches
+            e0.record(stream)
+            step()
+            e1.record(stream)
+        torch.cuda.synchronize()
+    launches = b200lab.launch_count() - n0
+    ms_local = sum(e0.elapsed_time(e1) for e0, e1 in evs) / args.steps
+    ms = dist.max(ms_local)
+    esz = q.element_size()
+    bytes_local = ((q.numel() + k.numel() + v.numel() + out.numel()) * esz
+                   + (g.numel() + b.numel()) * 4 + state.numel() * 4 * 2)
+    flops_local = Hv_l * T * (6 * 64 * d + 6 * d * d) + Hqk_l * T * 4 * 64 * d
+    achieved = bytes_local / (ms_local * 1e-3) / 1e9
+    res = {"metric": "GDN prefill tok/s", "value": T / (ms * 1e-3), "unit": "tok/s",
+           "us_per_step": ms * 1e3,
+           "config": {"workload": "gdn_prefill_c3", "B": 1, "T": T, "Hqk": Hqk, "Hv": Hv, "d": d,
+                      "chunk": 64, "sharding": "v-heads", "l2": "L2 flushed between launches"},
+           "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                        "frac": achieved / peaks["hbm_gbs"], "traffic": profile_traffic("gdn_prefill_c3"),
+                        "tensor_tflops": flops_local / (ms_local * 1e-3) / 1e12},
+           "gpu_launches": int(launches), "clocks": clk.summary()}
+    del q, k, v, g, b, state, out, ws, flush
+    torch.cuda.empty_cache()
+    return res
+
+
+# ----------------------------------------------------------------------------
+# CPU side: the fp64 oracle restatement timed on this host
+# ----------------------------------------------------------------------------
+def cpu_attention_sample(cfg, budget_s, threads=0):
+    """Times the oracle on rows of one (b, h) head; returns (TFLOP/s, cores, description)."""
+    import numpy as np
+    import torch
+    import oracle
+    import workloads
+
+    S, D = cfg["S"], cfg["D"]
+    Q, K, V = workloads.attn_inputs(1, 1, 1, S, D, cfg["dtype"], seed=42, device="cpu")
+    q, k, v = (t.float().numpy() for t in (Q, K, V))
+    cores = threads or oracle.default_threads()
+
+    def rows_flops(rows):
+        if cfg["causal"]:
+            return float(sum(4.0 * (r + 1) * D for r in rows))
+        return 4.0 * len(rows) * S * D
+
+    probe = list(range(0, S, max(1, S // 256)))
+    t0 = time.perf_counter()
+    oracle.attn_fwd(q, k, v, 1 / math.sqrt(D), cfg["causal"], rows=probe, nthreads=threads)
+    rate = rows_flops(probe) / max(time.perf_counter() - t0, 1e-6)
+    full = rows_flops(range(S))
+    frac = min(1.0, budget_s * rate / full)
+    stride = max(1, int(round(1 / frac)))
+    rows = list(range(0, S, stride))
+    t0 = time.perf_counter()
+    oracle.attn_fwd(q, k, v, 1 / math.sqrt(D), cfg["causal"], rows=rows, nthreads=threads)
+    dt = time.perf_counter() - t0
+    fl = rows_flops(rows)
+    desc = (f"fp64 oracle (restated naive_attn_kernel), 1 of {cfg['B'] * cfg['Hq']} heads, "
+            f"{len(rows)} of {S} query rows (every {stride}th), {fl:.3g} FLOP in {dt:.1f} s")
+    return fl / dt / 1e12, cores, desc, rows, q, k, v
+
+
+def cpu_gdn_prefill(cfg, threads=0):
+    import numpy as np
+    import oracle
+    import workloads
+    T, Hqk, Hv, d = cfg["T"], cfg["Hqk"], cfg["Hv"], cfg["d"]
+    q, k, v, g, b = workloads.gdn_inputs(1, T, Hqk, Hv, d, cfg["dtype"], seed=7)
+    arr = [t.float().numpy() for t in (q, k, v, g, b)]
+    t0 = time.perf_counter()
+    oracle.gdn_recurrent(*arr, np.zeros((1, Hv, d, d)), 1 / math.sqrt(d), 0, nthreads=threads)
+    dt = time.perf_counter() - t0
+    return {"value": T / dt, "unit": "tok/s", "cores": threads or oracle.default_threads(),
+            "kind": "port", "sample": f"full config, fp64 serial recurrence, {dt:.2f} s"}
+
+
+def cpu_gdn_decode(cfg, threads=0):
+    import numpy as np
+    import oracle
+    import workloads
+    B, Hqk, Hv, d = cfg["B"], cfg["Hqk"], cfg["Hv"], cfg["d"]
+    q, k, v, g, b = workloads.gdn_decode_inputs(B, Hqk, Hv, d, cfg["dtype"], seed=11)
+    arr = [t.float().numpy()[:, None] for t in (q, k, v, g, b)]
+    S = workloads.gdn_state(B, Hv, d).double().numpy()
+    t0 = time.perf_counter()
+    oracle.gdn_recurrent(*arr, S, 1 / math.sqrt(d), 0, nthreads=threads)
+    dt = time.perf_counter() - t0
+    nbytes = B * Hv * d * d * 4 * 2 + B * Hqk * d * 4 + B * Hv * d * 4 + B * Hv * 8
+    return {"value": nbytes / dt / 1e9, "unit": "GB/s (fp32-state bytes)",
+            "cores": threads or oracle.default_threads(), "kind": "port",
+            "sample": f"1 of 256 steps, fp64 serial recurrence, {dt:.2f} s"}
+
+
+# ----------------------------------------------------------------------------
+# arms
+# ----------------------------------------------------------------------------
+def run_reference(args):
+    """CPU implementation of the path on this host, same config/metric as our arm."""
+    import workloads
+    if int(os.environ.get("RANK", "0")) != 0:
+        return None
+    cfg = workloads.CONFIGS[args.workload if args.workload.startswith("attn") else "attn_c5"]
+    budget = max(0.5, args.cpu_budget_s / max(1, args.steps + args.warmup))
+    vals = []
+    desc = cores = None
+    for i in range(args.warmup + args.steps):
+        v, cores, desc, *_ = cpu_attention_sample(cfg, budget)
+        if i >= args.warmup:
+            vals.append(v)
+    value = statistics.mean(vals)
+    return {"metric": BASELINE_METRIC, "value": value, "unit": "TFLOP/s", "impl": "reference",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic", "config": {"workload": args.workload, "B": cfg["B"],
+                                            "Hq": cfg["Hq"], "Hkv": cfg["Hkv"], "S": cfg["S"],
+                                            "D": cfg["D"], "causal": cfg["causal"]},
+            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                             "sample": desc},
+            "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+            "note": "the reference has no CPU attention; its naive_attn_kernel "
+                    "(src/attn_sm75.cu:55-94) restated in fp64 C (oracle/) runs on the host cores"}
+
+
+def run_ours(args):
+    import torch
+    import workloads
+
+    dist = Dist(args.gpus)
+    dist.init()
+    peaks, peaks_src = load_peaks()
+    name = args.workload
+    cfgname = {"attn_c2": "attn_c2_d128", "gdn_decode": "gdn_decode_c4",
+               "gdn_prefill": "gdn_prefill_c3"}.get(name, name)
+    cfg = dict(workloads.CONFIGS[cfgname])
+    if args.attn_shape:
+        # smaller instance of the same kernel, for ncu captures that must stay small
+        cfg["B"], cfg["Hq"], cfg["Hkv"], cfg["S"], cfg["D"] = (int(x) for x in args.attn_shape.split(","))
+        name = name + "_custom"
+    if name.startswith("attn"):
+        main = bench_attention(name, cfg, args, dist, peaks)
+    elif name == "gdn_decode":
+        main = bench_gdn_decode(cfg, args, dist, peaks)
+    else:
+        main = bench_gdn_prefill(cfg, args, dist, peaks)
+
+    secondary = {}
+    if args.secondary and name == "attn_c5" and not args.attn_shape:
+        for key, fn, c in (("gdn_decode", bench_gdn_decode, workloads.CONFIGS["gdn_decode_c4"]),
+                           ("gdn_prefill", bench_gdn_prefill, workloads.CONFIGS["gdn_prefill_c3"])):
+            try:
+                secondary[key] = fn(c, args, dist, peaks)
+            except Exception as e:  # report, keep the headline line
+                secondary[key] = {"status": f"error: {e!r}"}
+
+    line = None
+    if dist.rank == 0:
+        line = {"metric": main.pop("metric"), "value": main.pop("value"), "unit": main.pop("unit"),
+                "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup}
+        line["ms_per_step"] = main.pop("ms_per_step", None) or main.get("us_per_step", 0) / 1e3
+        line.update({"higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                     "data": "synthetic (seeded torch.Generator, config distributions)"})
+        line.update(main)
+        line["roofline"]["peak_source"] = f"{peaks_src} (MEASURED_PEAKS.json)" \
+            if peaks_src == "measured" else "fallback (recipe constants)"
+        if dist.world == 1 and name.startswith("attn") and not args.no_cpu:
+            v, cores, desc, *_ = cpu_attention_sample(cfg, args.cpu_budget_s / 4)
+            line["cpu_baseline"] = {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                                    "sample": desc}
+        if secondary:
+            if dist.world == 1 and not args.no_cpu:
+                for key, fn, c in (("gdn_decode", cpu_gdn_decode, workloads.CONFIGS["gdn_decode_c4"]),
+                                   ("gdn_prefill", cpu_gdn_prefill, workloads.CONFIGS["gdn_prefill_c3"])):
+                    if "value" in secondary.get(key, {}):
+                        try:
+                            secondary[key]["cpu_baseline"] = fn(c)
+                        except Exception as e:
+                            secondary[key]["cpu_baseline"] = {"status": repr(e)}
+            line["secondary"] = secondary
+    dist.close()
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="attn_c5",
+                    choices=["attn_c5", "attn_c1", "attn_c2", "gdn_decode", "gdn_prefill"])
+    ap.add_argument("--no-secondary", dest="secondary", action="store_false")
+    ap.add_argument("--attn-shape", default=None, metavar="B,Hq,Hkv,S,D",
+                    help="override the attention shape (profiling a smaller case)")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline legs")
+    ap.add_argument("--cpu-budget-s", type=float, default=60.0,
+                    help="approximate CPU seconds for the reference arm / cpu_baseline")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    line = run_reference(args) if args.impl == "reference" else run_ours(args)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

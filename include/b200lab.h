@@ -1,0 +1,130 @@
+/*
+ * b200lab.h -- C ABI of the B200-native (sm_100a) attention and Gated
+ * DeltaNet kernels.
+ *
+ * The reference (cookys/turing-sm75) has no library; its drop-in surface is
+ * the raw __global__ signatures called from each binary's main() and the
+ * per-binary CLI.  Each entry point below replaces one of those kernel
+ * families; the comment on each names the reference interface (file:line).
+ *
+ * Conventions shared by every entry point:
+ *   - All tensor pointers are DEVICE pointers owned by the caller.  Nothing
+ *     is allocated; scratch space, where an entry needs it, is passed in
+ *     through (workspace, ws_bytes) and sized by the matching *_workspace()
+ *     query.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default
+ *     stream).  Each call enqueues its launches on that stream and returns
+ *     without synchronising.  The caller selects the device (cudaSetDevice).
+ *   - The return value is a status code (B200LAB_OK or a negative error);
+ *     the library never prints and never exits.  Arguments are validated
+ *     before anything is launched, so an error return means nothing ran
+ *     (except B200LAB_ERR_CUDA, which reports a failed launch).
+ *   - Device-side bounded waits that run out set a device error word instead
+ *     of hanging; b200lab_device_status() reads and clears it.
+ *   - Entry points are stateless and re-entrant apart from that error word.
+ */
+#ifndef B200LAB_H
+#define B200LAB_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define B200LAB_OK               0
+#define B200LAB_ERR_INVALID     -1  /* null pointer or inconsistent shape     */
+#define B200LAB_ERR_UNSUPPORTED -2  /* well-formed but not built (e.g. D=96)  */
+#define B200LAB_ERR_CUDA        -3  /* a CUDA runtime call / launch failed    */
+#define B200LAB_ERR_TIMEOUT     -4  /* a device-side bounded wait ran out     */
+#define B200LAB_ERR_WORKSPACE   -5  /* workspace missing or too small         */
+#define B200LAB_ERR_DEVICE      -6  /* current device is not sm_100 (B200)    */
+
+/* ---- element types ----------------------------------------------------- */
+#define B200LAB_F16  0
+#define B200LAB_BF16 1
+#define B200LAB_F32  2
+
+/* ---- softmax attention forward ------------------------------------------
+ * Replaces flash_attn_sm75_wmma<D> / flash_attn_sm75_ffma<D>
+ * (src/attn_sm75.cu:107-112, 239-244) and their launchers launch_wmma /
+ * launch_ffma (src/attn_sm75.cu:421-440):
+ *   (const half* Q, const half* K, const half* V, half* O, int S,
+ *    float scale, int causal), grid (ceil(S/16), B*H).
+ * Generalised with GQA (Hkv divides Hq; q-head h reads kv-head h/(Hq/Hkv)),
+ * separate query / key lengths and a bf16 variant.
+ *   Q, O : [B][Hq ][Sq ][D]  dtype (F16 or BF16)
+ *   K, V : [B][Hkv][Skv][D]  dtype
+ *   D    : 64 or 128.  fp32 accumulation; O = softmax(scale*Q K^T [+mask]) V.
+ *   causal: key j is visible to query i iff j <= i + (Skv - Sq); with
+ *           Sq == Skv this is the reference's k <= q (src/attn_sm75.cu:69).
+ *           A query row that sees no key is written as 0 (the reference's
+ *           l == 0 rule, src/attn_sm75.cu:372).
+ *   Base pointers must be 16-byte aligned.
+ *   workspace: may be NULL when attn_fwd_sm100_workspace() returns 0. */
+int attn_fwd_sm100(const void* Q, const void* K, const void* V, void* O,
+                   int B, int Hq, int Hkv, int Sq, int Skv, int D,
+                   float scale, int causal, int dtype,
+                   void* workspace, size_t ws_bytes, void* stream);
+size_t attn_fwd_sm100_workspace(int B, int Hq, int Hkv, int Sq, int Skv, int D,
+                                int causal);
+
+/* ---- Gated DeltaNet chunked prefill --------------------------------------
+ * Replaces the chunked GDN kernels gdn_wmma_kernel (src/gdn_sm75.cu:361-369)
+ * and gdn_prep_kernel + gdn_apply_kernel (src/gdn_sm75.cu:896-905, 981-992):
+ *   (const float* q, k, v, g_log, beta, float* state, float* out, int T,
+ *    float scale) with Sv=128, Hq=16, Hv=48 compiled in.
+ * Same recurrence (src/gdn_sm75.cu:6-11): per token
+ *   g = exp(g_log); kv = S k; d = (v - g*kv)*beta; S = g*S + d k^T;
+ *   o = scale * S q
+ * computed by the chunked (WY/UT) algebra with chunk 64.
+ *   q, k  : [B][T][Hqk][dk]  in_dtype (F16, BF16 or F32)
+ *   v     : [B][T][Hv ][dv]  in_dtype
+ *   g_log, beta : [B][T][Hv] fp32
+ *   state : [B][Hv][dv][dk] fp32, read and updated in place; element
+ *           state[c*dk + i] multiplies k[i] (the reference's layout,
+ *           src/gdn_sm75.cu:1094)
+ *   o     : [B][T][Hv][dv]  out_dtype (F16, BF16 or F32)
+ *   head_map: 0 -> v-head h reads q/k head h % Hqk (the reference,
+ *             src/gdn_sm75.cu:1083); 1 -> h / (Hv/Hqk).
+ *   dk = dv = 128.  workspace: gdn_prefill_sm100_workspace() bytes. */
+int gdn_prefill_sm100(const void* q, const void* k, const void* v,
+                      const float* g_log, const float* beta, float* state, void* o,
+                      int B, int T, int Hqk, int Hv, int dk, int dv, int head_map,
+                      float scale, int in_dtype, int out_dtype,
+                      void* workspace, size_t ws_bytes, void* stream);
+size_t gdn_prefill_sm100_workspace(int B, int T, int Hqk, int Hv, int dk, int dv);
+
+/* ---- Gated DeltaNet single-token decode ----------------------------------
+ * Replaces the token-serial kernels with T = 1, e.g. gdn_occ8_kernel
+ * (src/gdn_sm75.cu:722-730) and gdn_occ_kernel (src/gdn_sm75.cu:135-145),
+ * batched over B sequences.  Same per-token math as gdn_prefill_sm100.
+ *   q, k : [B][Hqk][dk] in_dtype;  v : [B][Hv][dv] in_dtype
+ *   g_log, beta : [B][Hv] fp32;  state : [B][Hv][dv][dk] fp32 in place
+ *   o : [B][Hv][dv] out_dtype.   dk = dv = 128. */
+int gdn_decode_sm100(const void* q, const void* k, const void* v,
+                     const float* g_log, const float* beta, float* state, void* o,
+                     int B, int Hqk, int Hv, int dk, int dv, int head_map,
+                     float scale, int in_dtype, int out_dtype, void* stream);
+
+/* ---- utilities ----------------------------------------------------------- */
+/* Message for a status code (static storage). */
+const char* b200lab_strerror(int status);
+/* Synchronises `stream`, then returns B200LAB_ERR_TIMEOUT (and clears the
+ * flag) if any kernel of this library on the current device gave up a
+ * bounded wait since the last call, B200LAB_ERR_CUDA on a CUDA error, else
+ * B200LAB_OK.  The reference's equivalent is CUDA_CHECK -> exit(1)
+ * (src/attn_sm75.cu:40-48); this library reports instead of exiting. */
+int b200lab_device_status(void* stream);
+/* Library version, major*10000 + minor*100 + patch. */
+int b200lab_version(void);
+/* Number of kernels this library has enqueued in this process (all devices,
+ * all threads) since it was loaded.  Benchmarks read it before and after a
+ * timed region to count their own launches. */
+unsigned long long b200lab_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* B200LAB_H */

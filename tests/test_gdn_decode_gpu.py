@@ -1,0 +1,60 @@
+"""GPU parity tests: gdn_decode_sm100 vs the fp64 serial recurrence (T=1 per step)."""
+import numpy as np
+import pytest
+import torch
+
+import b200lab
+import oracle
+import workloads
+from helpers import assert_close, to_np
+
+pytestmark = pytest.mark.gpu
+
+
+def _steps(B, Hqk, Hv, dtype, out_dtype, head_map, steps, seed=0):
+    dev = torch.device("cuda:0")
+    S = workloads.gdn_state(B, Hv, 128, std=0.02, seed=seed + 100)
+    S_dev = S.to(dev)
+    S_ref = S.double().numpy()
+    scale = 1.0 / np.sqrt(128)
+    for t in range(steps):
+        q, k, v, g, b = workloads.gdn_decode_inputs(B, Hqk, Hv, 128, dtype, seed=seed + t)
+        o = b200lab.gdn_decode(q.to(dev), k.to(dev), v.to(dev), g.to(dev), b.to(dev), S_dev,
+                               scale=scale, head_map=head_map, out_dtype=out_dtype)
+        o_ref, S_ref = oracle.gdn_recurrent(to_np(q)[:, None], to_np(k)[:, None], to_np(v)[:, None],
+                                            to_np(g)[:, None], to_np(b)[:, None], S_ref, scale,
+                                            head_map)
+        assert_close(to_np(o), o_ref[:, 0], f"out step {t}")
+    assert b200lab.device_status() == b200lab.OK
+    assert_close(to_np(S_dev), S_ref, "state")
+
+
+@pytest.mark.parametrize("head_map", [0, 1])
+@pytest.mark.parametrize("dtype,out_dtype", [(torch.bfloat16, torch.bfloat16),
+                                             (torch.float16, torch.float32),
+                                             (torch.float32, torch.float32)])
+def test_small(cuda, head_map, dtype, out_dtype):
+    _steps(3, 2, 4, dtype, out_dtype, head_map, steps=5)
+
+
+def test_c4_shape_two_steps(cuda):
+    c = workloads.CONFIGS["gdn_decode_c4"]
+    _steps(c["B"], c["Hqk"], c["Hv"], torch.bfloat16, torch.bfloat16, 0, steps=2, seed=5)
+
+
+def test_decode_equals_prefill_oracle_chain(cuda):
+    """256 decode steps from a zero state = the recurrence over T=256 (checkpoint/resume)."""
+    dev = torch.device("cuda:0")
+    B, Hqk, Hv, T = 2, 2, 4, 64
+    q, k, v, g, b = workloads.gdn_inputs(B, T, Hqk, Hv, 128, torch.bfloat16, seed=3)
+    S = torch.zeros((B, Hv, 128, 128), device=dev)
+    outs = []
+    for t in range(T):
+        outs.append(b200lab.gdn_decode(q[:, t].contiguous().to(dev), k[:, t].contiguous().to(dev),
+                                       v[:, t].contiguous().to(dev), g[:, t].contiguous().to(dev),
+                                       b[:, t].contiguous().to(dev), S, out_dtype=torch.float32))
+    o = torch.stack(outs, 1)
+    o_ref, S_ref = oracle.gdn_recurrent(to_np(q), to_np(k), to_np(v), to_np(g), to_np(b),
+                                        np.zeros((B, Hv, 128, 128)), 1.0 / np.sqrt(128))
+    assert_close(to_np(o), o_ref, "outputs")
+    assert_close(to_np(S), S_ref, "state")

@@ -1,0 +1,214 @@
+"""Python binding of the B200-native attention / Gated DeltaNet library.
+
+A thin ctypes layer over ``lib/libb200lab.so`` (C ABI in ``include/b200lab.h``)
+that takes torch CUDA tensors.  torch is used only for device memory and
+streams; every computation runs in the library's sm_100a kernels.  There is
+no CPU fallback: if the shared library is missing or the device is not a
+B200, calls raise.
+
+Entry points (reference interface each replaces, cookys/turing-sm75):
+
+* :func:`attn_fwd`     -- flash_attn_sm75_wmma / _ffma  (src/attn_sm75.cu:107-375)
+* :func:`gdn_prefill`  -- gdn_wmma_kernel, gdn_prep/apply (src/gdn_sm75.cu:361-574, 896-1073)
+* :func:`gdn_decode`   -- token-serial gdn_occ*_kernel at T=1 (src/gdn_sm75.cu:722-789)
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "lib", "libb200lab.so")
+
+OK = 0
+ERR_INVALID = -1
+ERR_UNSUPPORTED = -2
+ERR_CUDA = -3
+ERR_TIMEOUT = -4
+ERR_WORKSPACE = -5
+ERR_DEVICE = -6
+
+F16, BF16, F32 = 0, 1, 2
+
+# Every symbol include/b200lab.h declares (checked by tests/test_capi.py).
+EXPORTED = (
+    "attn_fwd_sm100", "attn_fwd_sm100_workspace",
+    "gdn_prefill_sm100", "gdn_prefill_sm100_workspace",
+    "gdn_decode_sm100",
+    "b200lab_strerror", "b200lab_device_status", "b200lab_version", "b200lab_launch_count",
+)
+
+_LIB = None
+
+
+class B200LabError(RuntimeError):
+    def __init__(self, status: int, what: str):
+        self.status = status
+        super().__init__(f"{what}: {strerror(status)} (status {status})")
+
+
+def build() -> None:
+    """Compile the library in-tree (make -C turing-sm75_b200)."""
+    import subprocess
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+
+
+def lib() -> ctypes.CDLL:
+    """Load lib/libb200lab.so (raises if it has not been built)."""
+    global _LIB
+    if _LIB is None:
+        if not os.path.exists(LIB_PATH):
+            raise FileNotFoundError(
+                f"{LIB_PATH} is missing: build it with `make -C {_HERE}` "
+                "(there is no fallback implementation)")
+        L = ctypes.CDLL(LIB_PATH)
+        vp, ci, cf, sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_size_t
+        L.attn_fwd_sm100.restype = ci
+        L.attn_fwd_sm100.argtypes = [vp, vp, vp, vp] + [ci] * 6 + [cf, ci, ci, vp, sz, vp]
+        L.attn_fwd_sm100_workspace.restype = sz
+        L.attn_fwd_sm100_workspace.argtypes = [ci] * 7
+        L.gdn_prefill_sm100.restype = ci
+        L.gdn_prefill_sm100.argtypes = [vp] * 7 + [ci] * 7 + [cf, ci, ci, vp, sz, vp]
+        L.gdn_prefill_sm100_workspace.restype = sz
+        L.gdn_prefill_sm100_workspace.argtypes = [ci] * 6
+        L.gdn_decode_sm100.restype = ci
+        L.gdn_decode_sm100.argtypes = [vp] * 7 + [ci] * 6 + [cf, ci, ci, vp]
+        L.b200lab_strerror.restype = ctypes.c_char_p
+        L.b200lab_strerror.argtypes = [ci]
+        L.b200lab_device_status.restype = ci
+        L.b200lab_device_status.argtypes = [vp]
+        L.b200lab_version.restype = ci
+        L.b200lab_version.argtypes = []
+        L.b200lab_launch_count.restype = ctypes.c_ulonglong
+        L.b200lab_launch_count.argtypes = []
+        _LIB = L
+    return _LIB
+
+
+def strerror(status: int) -> str:
+    return lib().b200lab_strerror(int(status)).decode()
+
+
+def _check(status: int, what: str) -> None:
+    if status != OK:
+        raise B200LabError(status, what)
+
+
+# ----------------------------------------------------------------------------
+# torch-facing wrappers
+# ----------------------------------------------------------------------------
+def _torch():
+    import torch
+    return torch
+
+
+def _dtype_code(t) -> int:
+    torch = _torch()
+    if t.dtype == torch.float16:
+        return F16
+    if t.dtype == torch.bfloat16:
+        return BF16
+    if t.dtype == torch.float32:
+        return F32
+    raise TypeError(f"unsupported dtype {t.dtype}")
+
+
+def _dev(t, name):
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (no CPU path)")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(stream):
+    torch = _torch()
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return ctypes.c_void_p(stream.cuda_stream)
+
+
+def attn_fwd(Q, K, V, *, scale: float | None = None, causal: bool = False, out=None,
+             workspace=None, stream=None):
+    """Softmax attention forward.  Q [B,Hq,Sq,D], K/V [B,Hkv,Skv,D] (fp16/bf16) -> O like Q."""
+    torch = _torch()
+    B, Hq, Sq, D = Q.shape
+    _, Hkv, Skv, _ = K.shape
+    if K.shape != V.shape or K.shape[0] != B or K.shape[3] != D:
+        raise ValueError("K/V shape mismatch")
+    if K.dtype != Q.dtype or V.dtype != Q.dtype:
+        raise TypeError("Q, K, V must share a dtype")
+    if scale is None:
+        scale = 1.0 / (D ** 0.5)
+    if out is None:
+        out = torch.empty_like(Q)
+    need = lib().attn_fwd_sm100_workspace(B, Hq, Hkv, Sq, Skv, D, int(bool(causal)))
+    ws_ptr, ws_bytes = ctypes.c_void_p(0), 0
+    if need:
+        if workspace is None:
+            workspace = torch.empty(need, dtype=torch.uint8, device=Q.device)
+        ws_ptr, ws_bytes = _dev(workspace, "workspace"), workspace.numel() * workspace.element_size()
+    st = lib().attn_fwd_sm100(_dev(Q, "Q"), _dev(K, "K"), _dev(V, "V"), _dev(out, "out"),
+                              B, Hq, Hkv, Sq, Skv, D, float(scale), int(bool(causal)),
+                              _dtype_code(Q), ws_ptr, ws_bytes, _stream(stream))
+    _check(st, "attn_fwd_sm100")
+    return out
+
+
+def gdn_prefill_workspace_bytes(B, T, Hqk, Hv, dk=128, dv=128) -> int:
+    return int(lib().gdn_prefill_sm100_workspace(B, T, Hqk, Hv, dk, dv))
+
+
+def gdn_prefill(q, k, v, g_log, beta, state, *, scale: float | None = None, head_map: int = 0,
+                out=None, out_dtype=None, workspace=None, stream=None):
+    """Chunked Gated DeltaNet prefill.  q,k [B,T,Hqk,dk]; v [B,T,Hv,dv]; g_log,beta [B,T,Hv]
+    fp32; state [B,Hv,dv,dk] fp32 (updated in place).  Returns o [B,T,Hv,dv]."""
+    torch = _torch()
+    B, T, Hqk, dk = q.shape
+    Hv, dv = v.shape[2], v.shape[3]
+    if scale is None:
+        scale = 1.0 / (dk ** 0.5)
+    if out is None:
+        out = torch.empty((B, T, Hv, dv), dtype=out_dtype or q.dtype, device=q.device)
+    need = gdn_prefill_workspace_bytes(B, T, Hqk, Hv, dk, dv)
+    ws_ptr, ws_bytes = ctypes.c_void_p(0), 0
+    if need:
+        if workspace is None:
+            workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+        ws_ptr, ws_bytes = _dev(workspace, "workspace"), workspace.numel() * workspace.element_size()
+    st = lib().gdn_prefill_sm100(_dev(q, "q"), _dev(k, "k"), _dev(v, "v"), _dev(g_log, "g_log"),
+                                 _dev(beta, "beta"), _dev(state, "state"), _dev(out, "out"),
+                                 B, T, Hqk, Hv, dk, dv, int(head_map), float(scale),
+                                 _dtype_code(q), _dtype_code(out), ws_ptr, ws_bytes,
+                                 _stream(stream))
+    _check(st, "gdn_prefill_sm100")
+    return out
+
+
+def gdn_decode(q, k, v, g_log, beta, state, *, scale: float | None = None, head_map: int = 0,
+               out=None, out_dtype=None, stream=None):
+    """One Gated DeltaNet decode step.  q,k [B,Hqk,dk]; v [B,Hv,dv]; g_log,beta [B,Hv] fp32;
+    state [B,Hv,dv,dk] fp32 (in place).  Returns o [B,Hv,dv]."""
+    torch = _torch()
+    B, Hqk, dk = q.shape
+    Hv, dv = v.shape[1], v.shape[2]
+    if scale is None:
+        scale = 1.0 / (dk ** 0.5)
+    if out is None:
+        out = torch.empty((B, Hv, dv), dtype=out_dtype or q.dtype, device=q.device)
+    st = lib().gdn_decode_sm100(_dev(q, "q"), _dev(k, "k"), _dev(v, "v"), _dev(g_log, "g_log"),
+                                _dev(beta, "beta"), _dev(state, "state"), _dev(out, "out"),
+                                B, Hqk, Hv, dk, dv, int(head_map), float(scale),
+                                _dtype_code(q), _dtype_code(out), _stream(stream))
+    _check(st, "gdn_decode_sm100")
+    return out
+
+
+def launch_count() -> int:
+    """Kernels this library has enqueued in this process so far."""
+    return int(lib().b200lab_launch_count())
+
+
+def device_status(stream=None) -> int:
+    """Synchronise and return the library's device status (0 = no wait gave up)."""
+    return int(lib().b200lab_device_status(_stream(stream)))

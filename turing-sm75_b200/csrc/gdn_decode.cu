@@ -1,0 +1,170 @@
+// gdn_decode.cu -- Gated DeltaNet single-token decode step for sm_100a.
+//
+// Reference semantics: the token-serial kernels of src/gdn_sm75.cu run with
+// T = 1 (gdn_occ8_kernel, src/gdn_sm75.cu:722-789; gdn_occ_kernel :135-188):
+//   g = exp(g_log); kv = S k; d = (v - g*kv)*beta; S = g*S + d k^T;
+//   o = scale * S q,  per (sequence b, v-head h), state row c = v column.
+//
+// The step is memory-bound: the fp32 state (dv*dk*4 = 64 KiB per (b,h)) is
+// read once and written once, everything else is < 2% of the bytes.  Layout
+// in HBM is the reference's [B][Hv][dv][dk] with dk innermost, so a state row
+// is 512 contiguous bytes = one warp x one float4 per lane: every load and
+// store is a fully coalesced 128-bit access.  One CTA of 8 warps owns one
+// (b, h); each warp owns 16 rows and issues all 16 row loads before the first
+// reduction, so 8 KiB per warp (64 KiB per CTA) is in flight.  Loads and
+// stores use the streaming (evict-first) cache policy: a step touches each
+// state byte exactly once.
+#include "common.cuh"
+#include "errwords.h"
+
+namespace b200 {
+namespace {
+
+__device__ int g_err_gdn_decode = 0;
+
+constexpr int kD = 128;           // dk = dv
+constexpr int kRowsPerWarp = 16;  // 8 warps x 16 rows = 128 rows per CTA
+constexpr int kThreads = 256;
+
+// Streaming 128-bit load / store.  asm volatile keeps the 16 row loads of a
+// warp issued back to back, ahead of the first reduction that consumes them.
+__device__ __forceinline__ float4 ld_stream(const float* p) {
+    float4 v;
+    asm volatile("ld.global.cs.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p));
+    return v;
+}
+__device__ __forceinline__ void st_stream(float* p, float4 v) {
+    asm volatile("st.global.cs.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(v.x), "f"(v.y),
+                 "f"(v.z), "f"(v.w)
+                 : "memory");
+}
+
+__device__ __forceinline__ float warp_sum(float x) {
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) x += __shfl_xor_sync(0xffffffffu, x, m);
+    return x;
+}
+
+template <typename T>
+__device__ __forceinline__ float4 load4(const T* p) {
+    if constexpr (sizeof(T) == 4) {
+        return *reinterpret_cast<const float4*>(p);
+    } else {
+        const uint2 raw = *reinterpret_cast<const uint2*>(p);
+        const T* e = reinterpret_cast<const T*>(&raw);
+        return make_float4(Elem<T>::to_f(e[0]), Elem<T>::to_f(e[1]), Elem<T>::to_f(e[2]),
+                           Elem<T>::to_f(e[3]));
+    }
+}
+
+template <typename TIn, typename TOut>
+__global__ void __launch_bounds__(kThreads) gdn_decode_kernel(
+    const TIn* __restrict__ q, const TIn* __restrict__ k, const TIn* __restrict__ v,
+    const float* __restrict__ g_log, const float* __restrict__ beta, float* __restrict__ state,
+    TOut* __restrict__ o, int Hqk, int Hv, int head_map, float scale) {
+    const int bh = blockIdx.x;  // b * Hv + h
+    const int b = bh / Hv;
+    const int h = bh - b * Hv;
+    const int hq = head_map == 0 ? h % Hqk : h / (Hv / Hqk);
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int row0 = warp * kRowsPerWarp;
+
+    float* S = state + (size_t)bh * kD * kD + (size_t)row0 * kD + 4 * lane;
+    float4 s[kRowsPerWarp];
+#pragma unroll
+    for (int r = 0; r < kRowsPerWarp; ++r) s[r] = ld_stream(S + r * kD);
+
+    const size_t qk_off = ((size_t)b * Hqk + hq) * kD + 4 * lane;
+    const float4 kk = load4(k + qk_off);
+    const float4 qq = load4(q + qk_off);
+    const float g = expf(g_log[bh]);
+    const float be = beta[bh];
+    const float vr = lane < kRowsPerWarp ? Elem<TIn>::to_f(v[(size_t)bh * kD + row0 + lane]) : 0.f;
+
+    float out = 0.f;
+#pragma unroll
+    for (int r = 0; r < kRowsPerWarp; ++r) {
+        float kv = s[r].x * kk.x + s[r].y * kk.y + s[r].z * kk.z + s[r].w * kk.w;
+        kv = warp_sum(kv);
+        const float vv = __shfl_sync(0xffffffffu, vr, r);
+        const float d = (vv - g * kv) * be;
+        s[r].x = g * s[r].x + kk.x * d;
+        s[r].y = g * s[r].y + kk.y * d;
+        s[r].z = g * s[r].z + kk.z * d;
+        s[r].w = g * s[r].w + kk.w * d;
+        float od = s[r].x * qq.x + s[r].y * qq.y + s[r].z * qq.z + s[r].w * qq.w;
+        od = warp_sum(od);
+        if (lane == r) out = od * scale;
+        st_stream(S + r * kD, s[r]);
+    }
+    if (lane < kRowsPerWarp) o[(size_t)bh * kD + row0 + lane] = Elem<TOut>::from_f(out);
+}
+
+template <typename TIn, typename TOut>
+int launch(const void* q, const void* k, const void* v, const float* g_log, const float* beta,
+           float* state, void* o, int B, int Hqk, int Hv, int head_map, float scale,
+           cudaStream_t st) {
+    gdn_decode_kernel<TIn, TOut><<<B * Hv, kThreads, 0, st>>>(
+        static_cast<const TIn*>(q), static_cast<const TIn*>(k), static_cast<const TIn*>(v),
+        g_log, beta, state, static_cast<TOut*>(o), Hqk, Hv, head_map, scale);
+    count_launch(1);
+    return cudaGetLastError() == cudaSuccess ? B200LAB_OK : B200LAB_ERR_CUDA;
+}
+
+template <typename TIn>
+int dispatch_out(int out_dtype, const void* q, const void* k, const void* v, const float* g_log,
+                 const float* beta, float* state, void* o, int B, int Hqk, int Hv, int head_map,
+                 float scale, cudaStream_t st) {
+    switch (out_dtype) {
+        case B200LAB_F16:
+            return launch<TIn, __half>(q, k, v, g_log, beta, state, o, B, Hqk, Hv, head_map, scale, st);
+        case B200LAB_BF16:
+            return launch<TIn, __nv_bfloat16>(q, k, v, g_log, beta, state, o, B, Hqk, Hv, head_map,
+                                              scale, st);
+        case B200LAB_F32:
+            return launch<TIn, float>(q, k, v, g_log, beta, state, o, B, Hqk, Hv, head_map, scale, st);
+    }
+    return B200LAB_ERR_UNSUPPORTED;
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+}  // namespace
+}  // namespace b200
+
+B200_DEFINE_ERR_TAKER(gdn_decode, b200::g_err_gdn_decode)
+
+extern "C" int gdn_decode_sm100(const void* q, const void* k, const void* v, const float* g_log,
+                                const float* beta, float* state, void* o, int B, int Hqk, int Hv,
+                                int dk, int dv, int head_map, float scale, int in_dtype,
+                                int out_dtype, void* stream) {
+    using namespace b200;
+    if (!q || !k || !v || !g_log || !beta || !state || !o) return B200LAB_ERR_INVALID;
+    if (B < 1 || Hqk < 1 || Hv < 1 || dk < 1 || dv < 1) return B200LAB_ERR_INVALID;
+    if (head_map != 0 && head_map != 1) return B200LAB_ERR_INVALID;
+    if (head_map == 1 && Hv % Hqk != 0) return B200LAB_ERR_INVALID;
+    if (in_dtype < B200LAB_F16 || in_dtype > B200LAB_F32) return B200LAB_ERR_INVALID;
+    if (out_dtype < B200LAB_F16 || out_dtype > B200LAB_F32) return B200LAB_ERR_INVALID;
+    if (dk != 128 || dv != 128) return B200LAB_ERR_UNSUPPORTED;
+    if ((long long)B * Hv > 0x7fffffffLL) return B200LAB_ERR_UNSUPPORTED;
+    const uintptr_t in_align = in_dtype == B200LAB_F32 ? 16 : 8;
+    if (!aligned(q, in_align) || !aligned(k, in_align) || !aligned(state, 16))
+        return B200LAB_ERR_INVALID;
+    int rc = check_device_sm100();
+    if (rc != B200LAB_OK) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    switch (in_dtype) {
+        case B200LAB_F16:
+            return dispatch_out<__half>(out_dtype, q, k, v, g_log, beta, state, o, B, Hqk, Hv,
+                                        head_map, scale, st);
+        case B200LAB_BF16:
+            return dispatch_out<__nv_bfloat16>(out_dtype, q, k, v, g_log, beta, state, o, B, Hqk, Hv,
+                                               head_map, scale, st);
+        default:
+            return dispatch_out<float>(out_dtype, q, k, v, g_log, beta, state, o, B, Hqk, Hv,
+                                       head_map, scale, st);
+    }
+}
