@@ -257,19 +257,25 @@ __global__ void __launch_bounds__(kThreads, 1)
 
             const int k0 = j * BN;
             const bool need_mask = k0 + BN - 1 > key_lim;
-            float smax = -INFINITY;
+            // row max as 8 independent chains (a single 128-long fmax chain is
+            // latency bound with one warp per SM sub-partition)
+            float mx[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) mx[u] = -INFINITY;
             if (need_mask) {
 #pragma unroll
                 for (int c = 0; c < BN; ++c) {
                     float s = __uint_as_float(sr[c]);
                     if (k0 + c > key_lim) s = -INFINITY;
                     sr[c] = __float_as_uint(s);
-                    smax = fmaxf(smax, s);
+                    mx[c & 7] = fmaxf(mx[c & 7], s);
                 }
             } else {
 #pragma unroll
-                for (int c = 0; c < BN; ++c) smax = fmaxf(smax, __uint_as_float(sr[c]));
+                for (int c = 0; c < BN; ++c) mx[c & 7] = fmaxf(mx[c & 7], __uint_as_float(sr[c]));
             }
+            const float smax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                     fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
             const float mt = smax * sl2;
             float alpha = 1.f;
             bool rescale = false;
@@ -284,14 +290,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 
             // P_j -> shared (swizzled 128B rows), 8 keys per 16-byte chunk.
             uint8_t* prow = sP + st * L::kPBytes + r * 128;
-            float rowsum = 0.f;
+            float rs[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) rs[u] = 0.f;
 #pragma unroll
             for (int ch = 0; ch < BN / 8; ++ch) {
                 float e[8];
 #pragma unroll
                 for (int u = 0; u < 8; ++u) {
                     e[u] = ex2(fmaf(__uint_as_float(sr[ch * 8 + u]), sl2, neg_mb));
-                    rowsum += e[u];
+                    rs[u] += e[u];
                 }
                 uint4 pk;
                 pk.x = Elem<T>::pack2(e[0], e[1]);
@@ -303,6 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 *reinterpret_cast<uint4*>(prow + atom * (BM * 128) + c16 * 16) = pk;
             }
             fence_proxy_async_smem();
+            const float rowsum = ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
 
             // PV_{j-1} must be complete before O is touched and before P[(j+1)%2]
             // is rewritten next iteration.

@@ -41,6 +41,13 @@ int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
                  int elem_bytes, uint64_t d0, uint64_t d1, uint64_t d2, uint32_t box0,
                  uint32_t box1, CUtensorMapSwizzle swizzle);
 
+// 4-D variant over a row-major [d3][d2][d1][d0] tensor with a (box0, box1,
+// box2, 1) box.  Used for the GDN inputs [B][T][H][d] (box = 64 columns of one
+// head for 64 tokens).
+int make_tmap_4d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
+                 int elem_bytes, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t d3,
+                 uint32_t box0, uint32_t box1, uint32_t box2, CUtensorMapSwizzle swizzle);
+
 // ---------------------------------------------------------------------------
 // device-side helpers
 // ---------------------------------------------------------------------------
@@ -119,6 +126,16 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* m
         "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
         " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(smem_dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
+                                            int c0, int c1, int c2, int c3) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2),
+        "r"(c3)
         : "memory");
 }
 

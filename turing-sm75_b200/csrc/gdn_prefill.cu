@@ -1,9 +1,671 @@
-// placeholder replaced below
+// gdn_prefill.cu -- chunked Gated DeltaNet prefill for sm_100a (tcgen05 + TMA).
+//
+// Reference semantics: the recurrence of src/gdn_sm75.cu:6-11 (gdn_cpu,
+// :1078-1106), computed with the chunked WY/UT algebra of gdn_chunked_cpu
+// (:1109-1244) and the reference's two-pass split gdn_prep_kernel /
+// gdn_apply_kernel (:896-1073).  The triangular solve here is the exact
+// (I + A)^-1, so the chunked result equals the recurrence (the reference's
+// own solve loop is not exact; see oracle/oracle.c).
+//
+// Chunk C = 64 tokens.  Per chunk, with gcs = cumsum(g_log), Gam = e^gcs:
+//   A[t][s]  = beta_t (k_t.k_s) e^{gcs_t-gcs_s}      s < t
+//   T        = (I + A)^-1
+//   W        = T diag(beta Gam) K          U = T diag(beta) V
+//   Aqk[t][s]= (q_t.k_s) e^{gcs_t-gcs_s}              s <= t
+//   Vn       = U - W S^T                    (state-dependent, sequential)
+//   o_t      = scale (Gam_t (S q_t) + sum_s Aqk[t][s] Vn_s)
+//   S       <- e^{gcs_last} S + sum_t e^{gcs_last-gcs_t} Vn_t k_t^T
+//
+// Kernel 1, gdn_prep_kernel: one CTA per (b, v-head, chunk), fully parallel.
+//   TMA loads K, Q, V chunk tiles; ONE M=128 tcgen05 MMA gives [K;Q] K^T
+//   (lanes 0-63: K K^T, lanes 64-127: Q K^T); the threads form A and Aqk,
+//   solve T by column-parallel forward substitution in fp32, and ONE M=128,
+//   N=256 MMA gives [T diag(beta Gam); T diag(beta)] [K | V] -> W and U.
+//   W, U, Aqk (16-bit) and gcs (fp32) go to the workspace.
+// Kernel 2, gdn_state_kernel: one CTA per (b, v-head, 32-column slice of the
+//   state), sequential over chunks.  The fp32 state slice lives in registers
+//   (thread i holds S[c0..c0+31][i]); per chunk:
+//     MMA1  [W;Q] S^T          (M=128,N=32,K=128) -> W S^T (lanes 0-63), Q S^T (64-127)
+//     Vn  = U - W S^T           (warps 0-1, 16-bit copy to shared memory)
+//     MMA2  [0;Aqk] Vn         (M=128,N=32,K=64)  -> intra-chunk output, lanes 64-127
+//     MMA3  K^T diag(e^{..}) Vn (M=128,N=32,K=64) -> state increment, lane i = key dim
+//     o = scale (Gam * Q S^T + intra)  (warps 2-3)      S = e^{gcs_last} S + increment
+//   A TMA producer warp double-buffers the chunk inputs; one thread issues MMAs.
+// Every wait is bounded (common.cuh).
 #include "common.cuh"
 #include "errwords.h"
-namespace b200 { namespace { __device__ int g_err_gdn_prefill = 0; } }
+
+namespace b200 {
+namespace {
+
+__device__ int g_err_gdn_prefill = 0;
+
+constexpr int kC = 64;    // chunk length
+constexpr int kD = 128;   // dk = dv
+constexpr int kSlice = 32;  // state columns (v dim) per kernel-2 CTA
+
+// ---- workspace layout ------------------------------------------------------
+struct WsLayout {
+    size_t w, u, aqk, gcs, total;
+};
+__host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+__host__ __device__ inline WsLayout ws_layout(size_t nbhc) {
+    WsLayout L;
+    L.w = 0;
+    L.u = align_up(L.w + nbhc * kC * kD * 2, 1024);
+    L.aqk = align_up(L.u + nbhc * kC * kD * 2, 1024);
+    L.gcs = align_up(L.aqk + nbhc * kC * kC * 2, 1024);
+    L.total = align_up(L.gcs + nbhc * kC * 4, 1024);
+    return L;
+}
+
+struct PrepParams {
+    uint8_t* ws;
+    const float* g_log;
+    const float* beta;
+    size_t ws_u, ws_aqk, ws_gcs;
+    int T, Hqk, Hv, nch, head_map;
+};
+
+__device__ __forceinline__ int qk_head(int h, int Hqk, int Hv, int head_map) {
+    return head_map == 0 ? h % Hqk : h / (Hv / Hqk);
+}
+
+// byte offset of element (row r, col j) in a K-major 128B-swizzled tile whose
+// rows are 128 bytes (64 16-bit elements) and whose 8-row groups are packed.
+__device__ __forceinline__ uint32_t sw128_off(int r, int j) {
+    return (uint32_t)(r * 128 + ((((j >> 3) ^ (r & 7)) & 7) << 4) + (j & 7) * 2);
+}
+
+// ===========================================================================
+// Kernel 1: per-chunk preparation
+// ===========================================================================
+namespace prep {
+constexpr int kThreads = 128;
+// shared layout (bytes)
+constexpr int kTiles = 0;          // [K0|Q0|K1|Q1|V0|pad|V1|pad], 8 KiB each
+constexpr int kK0 = 0, kQ0 = 8192, kK1 = 16384, kQ1 = 24576, kV0 = 32768, kV1 = 49152;
+constexpr int kAT = 65536;         // [T diag(beta Gam); T diag(beta)] 128 x 64, 16 KiB
+constexpr int kAs = 81920;         // A (fp32 64 x 64), 16 KiB
+constexpr int kMisc = 98304;       // gcs[64], beta[64], barriers
+constexpr int kBytes = kMisc + 1024;
+constexpr int kAlloc = kBytes + 1024;
+constexpr uint32_t kTmemCols = 256;
+
+struct Misc {
+    float gcs[kC];
+    float beta[kC];
+    uint64_t bar_tma, bar_mma1, bar_mma2, drain;
+    uint32_t tmem_base;
+    int abort;
+};
+}  // namespace prep
+
+template <typename T16>
+__global__ void __launch_bounds__(prep::kThreads, 2)
+    gdn_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const PrepParams p) {
+    using namespace prep;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    Misc* ms = reinterpret_cast<Misc*>(smem + kMisc);
+    float* As = reinterpret_cast<float*>(smem + kAs);
+    volatile int* abort = &ms->abort;
+
+    const int c = blockIdx.x;   // chunk
+    const int h = blockIdx.y;   // v-head
+    const int b = blockIdx.z;
+    const int hq = qk_head(h, p.Hqk, p.Hv, p.head_map);
+    const int t0 = c * kC;
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const size_t bhc = ((size_t)b * p.Hv + h) * p.nch + c;
+
+    if (tid == 0) {
+        mbar_init(&ms->bar_tma, 1);
+        mbar_init(&ms->bar_mma1, 1);
+        mbar_init(&ms->bar_mma2, 1);
+        mbar_init(&ms->drain, 1);
+        ms->abort = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(&ms->tmem_base, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = ms->tmem_base;
+
+    if (tid == 0) {
+        mbar_arrive_expect_tx(&ms->bar_tma, 6 * 8192);
+        tma_load_4d(smem + kK0, &tmK, &ms->bar_tma, 0, hq, t0, b);
+        tma_load_4d(smem + kK1, &tmK, &ms->bar_tma, 64, hq, t0, b);
+        tma_load_4d(smem + kQ0, &tmQ, &ms->bar_tma, 0, hq, t0, b);
+        tma_load_4d(smem + kQ1, &tmQ, &ms->bar_tma, 64, hq, t0, b);
+        tma_load_4d(smem + kV0, &tmV, &ms->bar_tma, 0, h, t0, b);
+        tma_load_4d(smem + kV1, &tmV, &ms->bar_tma, 64, h, t0, b);
+    }
+    // gates: gcs = inclusive prefix sum of g_log over the chunk (padded tokens: g=0, beta=0)
+    if (tid < kC) {
+        const int tt = t0 + tid;
+        const size_t gi = ((size_t)b * p.T + tt) * p.Hv + h;
+        float g = 0.f, be = 0.f;
+        if (tt < p.T) {
+            g = p.g_log[gi];
+            be = p.beta[gi];
+        }
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float y = __shfl_up_sync(0xffffffffu, g, o);
+            if (lane >= o) g += y;
+        }
+        ms->gcs[tid] = g;  // per-warp inclusive scan; warp 1 adds warp 0's total below
+        ms->beta[tid] = be;
+    }
+    __syncthreads();
+    if (tid >= 32 && tid < kC) ms->gcs[tid] += ms->gcs[31];
+    __syncthreads();
+
+    // MMA1: [K;Q] K^T  (M=128, N=64, K=128)
+    bool ok = true;
+    if (tid == 0) {
+        ok = mbar_wait(&ms->bar_tma, 0, abort, &g_err_gdn_prefill);
+        if (ok) {
+            tc_fence_after();
+            constexpr uint32_t idesc = make_idesc(Elem<T16>::kFmt, 128, 64, false, false);
+            const uint32_t base = smem_u32(smem + kTiles);
+#pragma unroll
+            for (int kk = 0; kk < kD / 16; ++kk) {
+                const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+                mma_f16_ss(tmem, smem_desc(base + off, 16, 1024, kLayoutSW128),
+                           smem_desc(base + off, 16, 1024, kLayoutSW128), idesc, kk > 0 ? 1u : 0u);
+            }
+            mma_commit(&ms->bar_mma1);
+        }
+    }
+    ok = __all_sync(0xffffffffu, mbar_wait(&ms->bar_mma1, 0, abort, &g_err_gdn_prefill));
+    tc_fence_after();
+    const int row = (warp & 1) * 32 + lane;  // token within the chunk
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const float gcs_r = ms->gcs[row];
+    if (ok) {
+        uint32_t v[64];
+        tmem_ld32(tmem + lane_base + 0, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+        tmem_ld32(tmem + lane_base + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+        tmem_ld_wait();
+        if (warp < 2) {
+            // A row (strictly lower), fp32, to shared
+            const float be = ms->beta[row];
+#pragma unroll
+            for (int s = 0; s < kC; s += 4) {
+                float4 a;
+                float* pa = &a.x;
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int ss = s + u;
+                    pa[u] = ss < row ? be * __uint_as_float(v[ss]) * __expf(gcs_r - ms->gcs[ss]) : 0.f;
+                }
+                *reinterpret_cast<float4*>(As + row * kC + s) = a;
+            }
+        } else {
+            // Aqk row (lower incl. diagonal), 16-bit, straight to the workspace
+            T16* dst = reinterpret_cast<T16*>(p.ws + p.ws_aqk) + bhc * kC * kC + row * kC;
+#pragma unroll
+            for (int s = 0; s < kC; s += 8) {
+                uint4 pk;
+                uint32_t* pw = &pk.x;
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int s0 = s + 2 * u, s1 = s0 + 1;
+                    const float a0 = s0 <= row ? __uint_as_float(v[s0]) * __expf(gcs_r - ms->gcs[s0]) : 0.f;
+                    const float a1 = s1 <= row ? __uint_as_float(v[s1]) * __expf(gcs_r - ms->gcs[s1]) : 0.f;
+                    pw[u] = Elem<T16>::pack2(a0, a1);
+                }
+                *reinterpret_cast<uint4*>(dst + s) = pk;
+            }
+        }
+    }
+    __syncthreads();
+
+    // T = (I + A)^-1: thread j < 64 computes column j by forward substitution.
+    if (warp < 2 && ok) {
+        const int j = tid;
+        float col[kC];
+#pragma unroll
+        for (int t = 0; t < kC; ++t) {
+            float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+#pragma unroll
+            for (int s = 0; s + 3 < t; s += 4) {
+                const float4 a = *reinterpret_cast<const float4*>(As + t * kC + s);
+                acc0 = fmaf(a.x, col[s], acc0);
+                acc1 = fmaf(a.y, col[s + 1], acc1);
+                acc2 = fmaf(a.z, col[s + 2], acc2);
+                acc3 = fmaf(a.w, col[s + 3], acc3);
+            }
+#pragma unroll
+            for (int s = (t & ~3); s < t; ++s) acc0 = fmaf(As[t * kC + s], col[s], acc0);
+            const float x = -((acc0 + acc1) + (acc2 + acc3));
+            col[t] = t < j ? 0.f : (t == j ? 1.f : x);
+        }
+        // columns scaled: rows 0-63 <- T diag(beta Gam), rows 64-127 <- T diag(beta)
+        const float bj = ms->beta[j];
+        const float bgj = bj * __expf(ms->gcs[j]);
+        uint8_t* at = smem + kAT;
+#pragma unroll
+        for (int t = 0; t < kC; ++t) {
+            *reinterpret_cast<T16*>(at + sw128_off(t, j)) = Elem<T16>::from_f(col[t] * bgj);
+            *reinterpret_cast<T16*>(at + sw128_off(kC + t, j)) = Elem<T16>::from_f(col[t] * bj);
+        }
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+
+    // MMA2: [T'; T''] [K | V]  (M=128, N=256, K=64); B is MN-major over 4 chunks of 64
+    if (tid == 0 && ok) {
+        tc_fence_after();
+        constexpr uint32_t idesc = make_idesc(Elem<T16>::kFmt, 128, 256, false, true);
+        const uint32_t a0 = smem_u32(smem + kAT);
+        const uint32_t b0 = smem_u32(smem + kTiles);
+#pragma unroll
+        for (int kk = 0; kk < kC / 16; ++kk) {
+            mma_f16_ss(tmem, smem_desc(a0 + kk * 32, 16, 1024, kLayoutSW128),
+                       smem_desc(b0 + kk * 2048, 16384, 1024, kLayoutSW128), idesc, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(&ms->bar_mma2);
+    }
+    ok = __all_sync(0xffffffffu, mbar_wait(&ms->bar_mma2, 0, abort, &g_err_gdn_prefill)) && ok;
+    tc_fence_after();
+    if (ok) {
+        // warps 0-1: W rows (lanes 0-63, cols 0-127); warps 2-3: U rows (lanes 64-127, cols 128-255)
+        const uint32_t col0 = warp < 2 ? 0u : 128u;
+        T16* dst = reinterpret_cast<T16*>(p.ws + (warp < 2 ? 0 : p.ws_u)) + bhc * kC * kD + row * kD;
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+            uint32_t v[32];
+            tmem_ld32(tmem + lane_base + col0 + cc * 32, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int q8 = 0; q8 < 4; ++q8) {
+                uint4 pk;
+                pk.x = Elem<T16>::pack2(__uint_as_float(v[q8 * 8 + 0]), __uint_as_float(v[q8 * 8 + 1]));
+                pk.y = Elem<T16>::pack2(__uint_as_float(v[q8 * 8 + 2]), __uint_as_float(v[q8 * 8 + 3]));
+                pk.z = Elem<T16>::pack2(__uint_as_float(v[q8 * 8 + 4]), __uint_as_float(v[q8 * 8 + 5]));
+                pk.w = Elem<T16>::pack2(__uint_as_float(v[q8 * 8 + 6]), __uint_as_float(v[q8 * 8 + 7]));
+                *reinterpret_cast<uint4*>(dst + cc * 32 + q8 * 8) = pk;
+            }
+        }
+        if (warp < 2)
+            reinterpret_cast<float*>(p.ws + p.ws_gcs)[bhc * kC + row] = gcs_r;
+    }
+    if (tid == 0) {
+        mma_commit(&ms->drain);
+        mbar_wait(&ms->drain, 0, abort, &g_err_gdn_prefill);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// ===========================================================================
+// Kernel 2: sequential state pass
+// ===========================================================================
+namespace st {
+constexpr int kThreads = 192;  // warps 0-3 compute, 4 TMA producer, 5 MMA issuer
+constexpr int kWarpProducer = 4, kWarpMma = 5;
+// one stage of chunk inputs (64 KiB):
+//   [W0|Q0|W1|Q1] A1 tile 32 KiB; [K0|K1] 16 KiB; [zero|Aqk] 16 KiB
+constexpr int kStage = 65536;
+constexpr int kA1 = 0, kKt = 32768, kZero = 49152, kAqk = 57344;
+constexpr int kStages = 2;
+constexpr int kSt = kStages * kStage;    // S tile: 32 rows (v) x 128 (k), 16-bit, 8 KiB
+constexpr int kVn = kSt + 8192;          // Vn^T tile 32 x 64, 4 KiB
+constexpr int kVt = kVn + 4096;          // decayed Vn^T tile, 4 KiB
+constexpr int kMisc = kVt + 4096;
+constexpr int kBytes = kMisc + 256;
+constexpr int kAlloc = kBytes + 1024;
+constexpr uint32_t kTmemCols = 128;
+constexpr uint32_t kColP = 0, kColOI = 32, kColDS = 64;
+
+struct Misc {
+    uint64_t full[kStages], empty[kStages];
+    uint64_t s_ready, p_full, v_ready, o_full, drain;
+    uint32_t tmem_base;
+    int abort;
+};
+}  // namespace st
+
+struct StateParams {
+    const uint8_t* ws;
+    float* state;
+    void* o;
+    size_t ws_u, ws_gcs;
+    int T, Hqk, Hv, nch, head_map;
+    float scale;
+};
+
+template <typename T16, typename TOut>
+__global__ void __launch_bounds__(st::kThreads, 1)
+    gdn_state_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmAqk,
+                     const StateParams p) {
+    using namespace st;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    Misc* ms = reinterpret_cast<Misc*>(smem + kMisc);
+    volatile int* abort = &ms->abort;
+
+    const int slice = blockIdx.x;
+    const int h = blockIdx.y;
+    const int b = blockIdx.z;
+    const int c0 = slice * kSlice;
+    const int hq = qk_head(h, p.Hqk, p.Hv, p.head_map);
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const size_t bh = (size_t)b * p.Hv + h;
+
+    if (tid == 0) {
+        for (int i = 0; i < kStages; ++i) {
+            mbar_init(&ms->full[i], 1);
+            mbar_init(&ms->empty[i], 1);
+        }
+        mbar_init(&ms->s_ready, 128);
+        mbar_init(&ms->p_full, 1);
+        mbar_init(&ms->v_ready, 64);
+        mbar_init(&ms->o_full, 1);
+        mbar_init(&ms->drain, 1);
+        ms->abort = 0;
+        fence_barrier_init();
+    }
+    // zero rows 0-63 of both [0;Aqk] tiles (never written by TMA)
+    for (int i = tid; i < kStages * 8192 / 16; i += blockDim.x) {
+        const int s = i / (8192 / 16), o = i % (8192 / 16);
+        reinterpret_cast<uint4*>(smem + s * kStage + kZero)[o] = make_uint4(0, 0, 0, 0);
+    }
+    fence_proxy_async_smem();
+    if (warp == kWarpMma) {
+        tmem_alloc(&ms->tmem_base, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = ms->tmem_base;
+
+    if (warp == kWarpProducer) {
+        if (lane == 0) {
+            int issued = 0;
+            for (int c = 0; c < p.nch; ++c) {
+                const int s = c & 1;
+                if (!mbar_wait(&ms->empty[s], ((c >> 1) & 1) ^ 1, abort, &g_err_gdn_prefill)) break;
+                uint8_t* stg = smem + s * kStage;
+                uint64_t* bar = &ms->full[s];
+                const int bhc = (int)(bh * p.nch + c);
+                mbar_arrive_expect_tx(bar, 7 * 8192);
+                tma_load_3d(stg + kA1 + 0, &tmW, bar, 0, 0, bhc);
+                tma_load_3d(stg + kA1 + 16384, &tmW, bar, 64, 0, bhc);
+                tma_load_4d(stg + kA1 + 8192, &tmQ, bar, 0, hq, c * kC, b);
+                tma_load_4d(stg + kA1 + 24576, &tmQ, bar, 64, hq, c * kC, b);
+                tma_load_4d(stg + kKt, &tmK, bar, 0, hq, c * kC, b);
+                tma_load_4d(stg + kKt + 8192, &tmK, bar, 64, hq, c * kC, b);
+                tma_load_3d(stg + kAqk, &tmAqk, bar, 0, 0, bhc);
+                issued = c + 1;
+            }
+            for (int c = max(0, issued - 2); c < issued; ++c)
+                mbar_wait(&ms->full[c & 1], (c >> 1) & 1, abort, &g_err_gdn_prefill);
+        }
+    } else if (warp == kWarpMma) {
+        if (lane == 0) {
+            constexpr uint32_t kFmt = Elem<T16>::kFmt;
+            constexpr uint32_t id_k = make_idesc(kFmt, 128, kSlice, false, false);   // both K-major
+            constexpr uint32_t id_mn = make_idesc(kFmt, 128, kSlice, true, false);   // A MN-major
+            const uint32_t sS = smem_u32(smem + kSt);
+            const uint32_t sVn = smem_u32(smem + kVn);
+            const uint32_t sVt = smem_u32(smem + kVt);
+            for (int c = 0; c < p.nch; ++c) {
+                const int s = c & 1;
+                const uint32_t stg = smem_u32(smem + s * kStage);
+                if (!mbar_wait(&ms->full[s], (c >> 1) & 1, abort, &g_err_gdn_prefill)) break;
+                if (!mbar_wait(&ms->s_ready, c & 1, abort, &g_err_gdn_prefill)) break;
+                tc_fence_after();
+                // MMA1: [W;Q] S^T
+#pragma unroll
+                for (int kk = 0; kk < kD / 16; ++kk) {
+                    const uint32_t ao = (kk >> 2) * 16384 + (kk & 3) * 32;
+                    const uint32_t bo = (kk >> 2) * 4096 + (kk & 3) * 32;
+                    mma_f16_ss(tmem + kColP, smem_desc(stg + kA1 + ao, 16, 1024, kLayoutSW128),
+                               smem_desc(sS + bo, 16, 1024, kLayoutSW128), id_k, kk > 0 ? 1u : 0u);
+                }
+                mma_commit(&ms->p_full);
+                if (!mbar_wait(&ms->v_ready, c & 1, abort, &g_err_gdn_prefill)) break;
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < kC / 16; ++kk) {
+                    // MMA2: [0;Aqk] Vn  -> intra-chunk outputs in lanes 64-127
+                    mma_f16_ss(tmem + kColOI, smem_desc(stg + kZero + kk * 32, 16, 1024, kLayoutSW128),
+                               smem_desc(sVn + kk * 32, 16, 1024, kLayoutSW128), id_k, kk > 0 ? 1u : 0u);
+                    // MMA3: K^T (decayed Vn) -> state increment, lane = key index
+                    mma_f16_ss(tmem + kColDS, smem_desc(stg + kKt + kk * 2048, 8192, 1024, kLayoutSW128),
+                               smem_desc(sVt + kk * 32, 16, 1024, kLayoutSW128), id_mn, kk > 0 ? 1u : 0u);
+                }
+                mma_commit(&ms->o_full);
+                mma_commit(&ms->empty[s]);
+            }
+            mma_commit(&ms->drain);
+            mbar_wait(&ms->drain, 0, abort, &g_err_gdn_prefill);
+        }
+    } else {
+        // ---------------- compute warps 0-3 -----------------------------------
+        const int i = tid;                         // key index this thread owns (0..127)
+        const int row = (warp & 1) * 32 + lane;    // token row for warps 0-1 (Vn) and 2-3 (O)
+        const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+        float S[kSlice];
+        float* Sg = p.state + (bh * kD + c0) * kD + i;
+#pragma unroll
+        for (int cc = 0; cc < kSlice; ++cc) S[cc] = Sg[(size_t)cc * kD];
+        const float* gcs_all = reinterpret_cast<const float*>(p.ws + p.ws_gcs);
+        const T16* U_all = reinterpret_cast<const T16*>(p.ws + p.ws_u);
+        uint8_t* sS = smem + kSt;
+        uint8_t* sVn = smem + kVn;
+        uint8_t* sVt = smem + kVt;
+        bool ok = true;
+        for (int c = 0; c < p.nch && ok; ++c) {
+            const size_t bhc = bh * p.nch + c;
+            // S (16-bit) -> shared, B operand of MMA1: row = v column cc, col = key i
+#pragma unroll
+            for (int cc = 0; cc < kSlice; ++cc)
+                *reinterpret_cast<T16*>(sS + (i >> 6) * 4096 + sw128_off(cc, i & 63)) =
+                    Elem<T16>::from_f(S[cc]);
+            fence_proxy_async_smem();
+            tc_fence_before();
+            mbar_arrive(&ms->s_ready);
+
+            const float gcs_t = gcs_all[bhc * kC + row];
+            const float g_last = gcs_all[bhc * kC + kC - 1];
+            if (warp < 2) {
+                float u[kSlice];
+                const uint4* up = reinterpret_cast<const uint4*>(U_all + (bhc * kC + row) * kD + c0);
+#pragma unroll
+                for (int q8 = 0; q8 < kSlice / 8; ++q8) {
+                    const uint4 raw = up[q8];
+                    const T16* e = reinterpret_cast<const T16*>(&raw);
+#pragma unroll
+                    for (int u8 = 0; u8 < 8; ++u8) u[q8 * 8 + u8] = Elem<T16>::to_f(e[u8]);
+                }
+                ok = __all_sync(0xffffffffu, mbar_wait(&ms->p_full, c & 1, abort, &g_err_gdn_prefill));
+                if (!ok) break;
+                tc_fence_after();
+                uint32_t pr[32];
+                tmem_ld32(tmem + lane_base + kColP, pr);
+                tmem_ld_wait();
+                const float dec = __expf(g_last - gcs_t);
+#pragma unroll
+                for (int cc = 0; cc < kSlice; ++cc) {
+                    const float vn = u[cc] - __uint_as_float(pr[cc]);
+                    *reinterpret_cast<T16*>(sVn + sw128_off(cc, row)) = Elem<T16>::from_f(vn);
+                    *reinterpret_cast<T16*>(sVt + sw128_off(cc, row)) = Elem<T16>::from_f(vn * dec);
+                }
+                fence_proxy_async_smem();
+                tc_fence_before();
+                mbar_arrive(&ms->v_ready);
+            }
+            ok = __all_sync(0xffffffffu, mbar_wait(&ms->o_full, c & 1, abort, &g_err_gdn_prefill));
+            if (!ok) break;
+            tc_fence_after();
+            if (warp >= 2) {
+                uint32_t pq[32], oi[32];
+                tmem_ld32(tmem + lane_base + kColP, pq);
+                tmem_ld32(tmem + lane_base + kColOI, oi);
+                tmem_ld_wait();
+                const int tt = c * kC + row;
+                if (tt < p.T) {
+                    const float eg = __expf(gcs_t);
+                    TOut* op = static_cast<TOut*>(p.o) + (((size_t)b * p.T + tt) * p.Hv + h) * kD + c0;
+#pragma unroll
+                    for (int cc = 0; cc < kSlice; ++cc)
+                        op[cc] = Elem<TOut>::from_f(
+                            p.scale * fmaf(eg, __uint_as_float(pq[cc]), __uint_as_float(oi[cc])));
+                }
+            }
+            uint32_t ds[32];
+            tmem_ld32(tmem + lane_base + kColDS, ds);
+            tmem_ld_wait();
+            const float gam = __expf(g_last);
+#pragma unroll
+            for (int cc = 0; cc < kSlice; ++cc) S[cc] = fmaf(gam, S[cc], __uint_as_float(ds[cc]));
+        }
+        if (ok) {
+#pragma unroll
+            for (int cc = 0; cc < kSlice; ++cc) Sg[(size_t)cc * kD] = S[cc];
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kWarpMma) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// ===========================================================================
+// host side
+// ===========================================================================
+template <typename T16, typename TOut>
+int launch(const void* q, const void* k, const void* v, const float* g_log, const float* beta,
+           float* state, void* o, int B, int T, int Hqk, int Hv, int head_map, float scale,
+           void* ws, cudaStream_t stream) {
+    const int nch = (T + kC - 1) / kC;
+    const size_t nbhc = (size_t)B * Hv * nch;
+    const WsLayout L = ws_layout(nbhc);
+    const CUtensorMapDataType dt = Elem<T16>::kFmt == 0 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                        : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    CUtensorMap tq, tk, tv, tw, ta;
+    int rc;
+    if ((rc = make_tmap_4d(&tq, q, dt, 2, kD, Hqk, T, B, 64, 1, kC, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
+    if ((rc = make_tmap_4d(&tk, k, dt, 2, kD, Hqk, T, B, 64, 1, kC, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
+    if ((rc = make_tmap_4d(&tv, v, dt, 2, kD, Hv, T, B, 64, 1, kC, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
+    uint8_t* wsb = static_cast<uint8_t*>(ws);
+    if ((rc = make_tmap_3d(&tw, wsb + L.w, dt, 2, kD, kC, nbhc, 64, kC, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
+    if ((rc = make_tmap_3d(&ta, wsb + L.aqk, dt, 2, kC, kC, nbhc, 64, kC, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
+
+    PrepParams pp;
+    pp.ws = wsb;
+    pp.g_log = g_log;
+    pp.beta = beta;
+    pp.ws_u = L.u;
+    pp.ws_aqk = L.aqk;
+    pp.ws_gcs = L.gcs;
+    pp.T = T;
+    pp.Hqk = Hqk;
+    pp.Hv = Hv;
+    pp.nch = nch;
+    pp.head_map = head_map;
+    auto k1 = gdn_prep_kernel<T16>;
+    B200_TRY_CUDA(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, prep::kAlloc));
+    k1<<<dim3(nch, Hv, B), prep::kThreads, prep::kAlloc, stream>>>(tq, tk, tv, pp);
+    B200_TRY_CUDA(cudaGetLastError());
+
+    StateParams sp;
+    sp.ws = wsb;
+    sp.state = state;
+    sp.o = o;
+    sp.ws_u = L.u;
+    sp.ws_gcs = L.gcs;
+    sp.T = T;
+    sp.Hqk = Hqk;
+    sp.Hv = Hv;
+    sp.nch = nch;
+    sp.head_map = head_map;
+    sp.scale = scale;
+    auto k2 = gdn_state_kernel<T16, TOut>;
+    B200_TRY_CUDA(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, st::kAlloc));
+    k2<<<dim3(kD / kSlice, Hv, B), st::kThreads, st::kAlloc, stream>>>(tq, tk, tw, ta, sp);
+    count_launch(2);
+    return cudaGetLastError() == cudaSuccess ? B200LAB_OK : B200LAB_ERR_CUDA;
+}
+
+template <typename T16>
+int dispatch_out(int out_dtype, const void* q, const void* k, const void* v, const float* g,
+                 const float* be, float* state, void* o, int B, int T, int Hqk, int Hv, int hm,
+                 float scale, void* ws, cudaStream_t s) {
+    switch (out_dtype) {
+        case B200LAB_F16: return launch<T16, __half>(q, k, v, g, be, state, o, B, T, Hqk, Hv, hm, scale, ws, s);
+        case B200LAB_BF16:
+            return launch<T16, __nv_bfloat16>(q, k, v, g, be, state, o, B, T, Hqk, Hv, hm, scale, ws, s);
+        case B200LAB_F32: return launch<T16, float>(q, k, v, g, be, state, o, B, T, Hqk, Hv, hm, scale, ws, s);
+    }
+    return B200LAB_ERR_UNSUPPORTED;
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+}  // namespace
+}  // namespace b200
+
 B200_DEFINE_ERR_TAKER(gdn_prefill, b200::g_err_gdn_prefill)
-extern "C" size_t gdn_prefill_sm100_workspace(int, int, int, int, int, int) { return 0; }
-extern "C" int gdn_prefill_sm100(const void*, const void*, const void*, const float*, const float*,
-                                 float*, void*, int, int, int, int, int, int, int, float, int, int,
-                                 void*, size_t, void*) { return B200LAB_ERR_UNSUPPORTED; }
+
+extern "C" size_t gdn_prefill_sm100_workspace(int B, int T, int Hqk, int Hv, int dk, int dv) {
+    (void)Hqk;
+    (void)dk;
+    (void)dv;
+    if (B < 1 || T < 1 || Hv < 1) return 0;
+    const size_t nch = ((size_t)T + b200::kC - 1) / b200::kC;
+    return b200::ws_layout((size_t)B * Hv * nch).total;
+}
+
+extern "C" int gdn_prefill_sm100(const void* q, const void* k, const void* v, const float* g_log,
+                                 const float* beta, float* state, void* o, int B, int T, int Hqk,
+                                 int Hv, int dk, int dv, int head_map, float scale, int in_dtype,
+                                 int out_dtype, void* workspace, size_t ws_bytes, void* stream) {
+    using namespace b200;
+    if (!q || !k || !v || !g_log || !beta || !state || !o) return B200LAB_ERR_INVALID;
+    if (B < 1 || T < 0 || Hqk < 1 || Hv < 1 || dk < 1 || dv < 1) return B200LAB_ERR_INVALID;
+    if (head_map != 0 && head_map != 1) return B200LAB_ERR_INVALID;
+    if (head_map == 1 && Hv % Hqk != 0) return B200LAB_ERR_INVALID;
+    if (in_dtype < B200LAB_F16 || in_dtype > B200LAB_F32) return B200LAB_ERR_INVALID;
+    if (out_dtype < B200LAB_F16 || out_dtype > B200LAB_F32) return B200LAB_ERR_INVALID;
+    if (dk != 128 || dv != 128) return B200LAB_ERR_UNSUPPORTED;
+    if (in_dtype == B200LAB_F32) return B200LAB_ERR_UNSUPPORTED;  // 16-bit operands only
+    if (B > 65535 || Hv > 65535) return B200LAB_ERR_UNSUPPORTED;
+    if (T == 0) return B200LAB_OK;
+    if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(state, 16))
+        return B200LAB_ERR_INVALID;
+    const size_t need = gdn_prefill_sm100_workspace(B, T, Hqk, Hv, dk, dv);
+    if (!workspace || ws_bytes < need || !aligned(workspace, 256)) return B200LAB_ERR_WORKSPACE;
+    int rc = check_device_sm100();
+    if (rc != B200LAB_OK) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (in_dtype == B200LAB_BF16)
+        return dispatch_out<__nv_bfloat16>(out_dtype, q, k, v, g_log, beta, state, o, B, T, Hqk, Hv,
+                                           head_map, scale, workspace, s);
+    return dispatch_out<__half>(out_dtype, q, k, v, g_log, beta, state, o, B, T, Hqk, Hv, head_map,
+                                scale, workspace, s);
+}

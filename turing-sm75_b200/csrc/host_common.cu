@@ -52,6 +52,23 @@ int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
     return r == CUDA_SUCCESS ? B200LAB_OK : B200LAB_ERR_INVALID;
 }
 
+int make_tmap_4d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes,
+                 uint64_t d0, uint64_t d1, uint64_t d2, uint64_t d3, uint32_t box0, uint32_t box1,
+                 uint32_t box2, CUtensorMapSwizzle swizzle) {
+    auto fn = encode_fn();
+    if (!fn) return B200LAB_ERR_CUDA;
+    const uint64_t e = (uint64_t)elem_bytes;
+    cuuint64_t dims[4] = {d0, d1, d2, d3};
+    cuuint64_t strides[3] = {d0 * e, d0 * d1 * e, d0 * d1 * d2 * e};
+    cuuint32_t box[4] = {box0, box1, box2, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    std::memset(map, 0, sizeof(*map));
+    CUresult r = fn(map, dtype, 4, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? B200LAB_OK : B200LAB_ERR_INVALID;
+}
+
 }  // namespace b200
 
 extern "C" const char* b200lab_strerror(int status) {
