@@ -13,7 +13,8 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 def _declared_functions():
     src = open(os.path.join(ROOT, "include", "b200lab.h")).read()
     src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
-    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\s*\**\s*(\w+)\s*\(", src, flags=re.M)))
+    src = re.sub(r"^\s*#.*$", "", src, flags=re.M)
+    return sorted(set(re.findall(r"^\s*(?:[A-Za-z_]\w*[\s*]+)+([A-Za-z_]\w*)\s*\(", src, flags=re.M)))
 
 
 def test_header_symbols_exported():
