@@ -169,10 +169,11 @@ class Dist:
 
 
 def split_units(total, world, rank):
-    if total % world:
-        raise SystemExit(f"{total} units do not split over {world} GPUs")
-    n = total // world
-    return rank * n, n
+    import sharding
+    try:
+        return sharding.split_units(total, world, rank)
+    except ValueError as e:
+        raise SystemExit(str(e))
 
 
 # ----------------------------------------------------------------------------
@@ -180,12 +181,9 @@ def split_units(total, world, rank):
 # ----------------------------------------------------------------------------
 def attn_shard(cfg, world, rank):
     """(batch, kv-head) units with their q-heads; returns the local (B, Hq, Hkv)."""
-    units = cfg["B"] * cfg["Hkv"]
-    u0, n = split_units(units, world, rank)
-    group = cfg["Hq"] // cfg["Hkv"]
-    if n >= cfg["Hkv"]:
-        return n // cfg["Hkv"], cfg["Hq"], cfg["Hkv"]
-    return 1, n * group, n
+    import sharding
+    b0, nb, h0, nh = sharding.attn_shard(cfg["B"], cfg["Hq"], cfg["Hkv"], world, rank)
+    return nb, nh * (cfg["Hq"] // cfg["Hkv"]), nh
 
 
 def attn_flops(B, Hq, S, D, causal):
@@ -365,8 +363,8 @@ def bench_gdn_prefill(cfg, args, dist, peaks):
     import workloads
 
     T, Hqk, Hv, d, dtype = cfg["T"], cfg["Hqk"], cfg["Hv"], cfg["d"], cfg["dtype"]
-    h0, Hv_l = split_units(Hv, dist.world, dist.rank)
-    Hqk_l = min(Hqk, Hv_l)
+    import sharding
+    h0, Hv_l, hq0, Hqk_l = sharding.gdn_prefill_shard(Hqk, Hv, dist.world, dist.rank)
     dev = torch.device("cuda", dist.local)
     q, k, v, g, b = workloads.gdn_inputs(1, T, Hqk_l, Hv_l, d, dtype, seed=7 + dist.rank, device=dev)
     state = torch.zeros((1, Hv_l, d, d), dtype=torch.float32, device=dev)
