@@ -96,6 +96,33 @@ int gdn_prefill_sm100(const void* q, const void* k, const void* v,
                       void* workspace, size_t ws_bytes, void* stream);
 size_t gdn_prefill_sm100_workspace(int B, int T, int Hqk, int Hv, int dk, int dv);
 
+/* ---- Gated DeltaNet chunked prefill without any allocation ----------------
+ * No counterpart in the reference: it has no library, so nothing there
+ * allocates on a caller's behalf.  This entry is for callers that cannot call
+ * cudaMalloc or provide a workspace -- e.g. a host framework whose graph
+ * allocator plans every buffer ahead of time and hands an operator only its
+ * inputs and outputs, or a serving loop that must not hit cudaMalloc's
+ * implicit device-wide synchronisation.
+ * Same arguments and results as gdn_prefill_sm100, minus the workspace: the
+ * scratch is a file-scope device array of B200LAB_NOALLOC_SCRATCH_BYTES
+ * (64 MiB) that every GPU loading the prefill kernels holds until the process
+ * exits.  A problem whose gdn_prefill_sm100_workspace() exceeds that size is
+ * rejected with B200LAB_ERR_WORKSPACE before anything is launched (about
+ * 41 KB per (sequence, v-head, 64-token chunk): B*Hv*ceil(T/64) <= 1628,
+ * e.g. Hv=48 up to T=2048, Hv=32 up to T=3200).
+ * The first call on a device looks up the array's device address (with that
+ * device current) and caches it; make that first call before any stream
+ * capture.  All calls on a device share the one array, so calls that overlap
+ * on the GPU (other streams, other host threads) race and must be
+ * serialised by the caller.  Nothing in the scratch needs to start at zero:
+ * the preparation kernel writes every byte the state kernel reads. */
+#define B200LAB_NOALLOC_SCRATCH_BYTES (64u << 20)
+int gdn_prefill_sm100_noalloc(const void* q, const void* k, const void* v,
+                              const float* g_log, const float* beta, float* state,
+                              void* o, int B, int T, int Hqk, int Hv, int dk, int dv,
+                              int head_map, float scale, int in_dtype, int out_dtype,
+                              void* stream);
+
 /* ---- Gated DeltaNet single-token decode ----------------------------------
  * Replaces the token-serial kernels with T = 1, e.g. gdn_occ8_kernel
  * (src/gdn_sm75.cu:722-730) and gdn_occ_kernel (src/gdn_sm75.cu:135-145),

@@ -33,7 +33,7 @@ F16, BF16, F32 = 0, 1, 2
 # Every symbol include/b200lab.h declares (checked by tests/test_capi.py).
 EXPORTED = (
     "attn_fwd_sm100", "attn_fwd_sm100_workspace",
-    "gdn_prefill_sm100", "gdn_prefill_sm100_workspace",
+    "gdn_prefill_sm100", "gdn_prefill_sm100_workspace", "gdn_prefill_sm100_noalloc",
     "gdn_decode_sm100",
     "b200lab_strerror", "b200lab_device_status", "b200lab_version", "b200lab_launch_count",
 )
@@ -71,6 +71,8 @@ def lib() -> ctypes.CDLL:
         L.gdn_prefill_sm100.argtypes = [vp] * 7 + [ci] * 7 + [cf, ci, ci, vp, sz, vp]
         L.gdn_prefill_sm100_workspace.restype = sz
         L.gdn_prefill_sm100_workspace.argtypes = [ci] * 6
+        L.gdn_prefill_sm100_noalloc.restype = ci
+        L.gdn_prefill_sm100_noalloc.argtypes = [vp] * 7 + [ci] * 7 + [cf, ci, ci, vp]
         L.gdn_decode_sm100.restype = ci
         L.gdn_decode_sm100.argtypes = [vp] * 7 + [ci] * 6 + [cf, ci, ci, vp]
         L.b200lab_strerror.restype = ctypes.c_char_p
