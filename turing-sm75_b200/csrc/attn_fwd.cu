@@ -5,20 +5,27 @@
 // (src/attn_sm75.cu:55-94): O = softmax(scale * Q K^T, causal k <= q) V,
 // online softmax with running (m, l, O), masked scores = -inf, l == 0 -> 0.
 //
-// Design (one CTA per (128-row query tile, q-head, batch)):
-//   warp 4      TMA producer: Q tile once, then K_j / V_j tiles into a
-//               two-stage ring (128-byte swizzled boxes of 64 columns).
-//   warp 5      MMA issuer (one thread) and TMEM owner:
-//                 S_j = Q K_j^T   -> TMEM columns [128*(j%2), +128)  (M=128,N=128)
-//                 O  += P_j V_j   -> TMEM columns [256, 256+D)        (M=128,N=D)
-//               issue order QK_0, QK_1, PV_0, QK_2, PV_1, ... so the tensor
-//               core computes S_{j+1} while the softmax warps work on S_j.
-//   warps 0-3   softmax + epilogue; thread t owns query row t (= TMEM lane t).
-//               Reads S_j with tcgen05.ld, masks, keeps the running max m in
-//               log2 units and rescales O only when the max grows by more
-//               than 2^8 (exact: the final 1/l uses the same m), writes
-//               P_j = exp2(s*scale*log2e - m) as 16-bit values into a
-//               swizzled shared tile (double-buffered) for the PV MMA.
+// Design: one CTA per (256 query rows = two 128-row tiles, q-head, batch),
+// 320 threads, every K/V tile loaded once and used by both query tiles.
+//   warp 8      TMA producer: Q0, Q1 once, then K_j / V_j into a two-stage
+//               ring (128-byte swizzled boxes of 64 columns).
+//   warp 9      MMA issuer (one thread) and owner of all 512 TMEM columns:
+//                 S_t  = Q_t K_j^T      TMEM cols [128 t, 128 t + 128)   (M=N=128)
+//                 O_t += P_t V_j        TMEM cols [256 + D t, +D)        (M=128, N=D)
+//               P_t is read from TMEM (the ".kind::f16 [d], [a], b" form) where
+//               the softmax wrote it over the first 64 columns of S_t.  Issue
+//               order per key tile: PV_0(j), QK_0(j+1), PV_1(j), QK_1(j+1), so
+//               the tensor core always has the other tile's work queued while a
+//               softmax warpgroup works.
+//   warps 0-3   softmax of tile 0, warps 4-7 softmax of tile 1: thread = query
+//               row = TMEM lane.  tcgen05.ld S, mask, running max in log2
+//               units with lazy O rescale (only when the max grows by > 2^8;
+//               exact since the final 1/l uses the same max), P = exp2(s*c - m)
+//               packed to 16 bits and stored back with tcgen05.st, then the
+//               epilogue O / l -> HBM.
+// Ordering without extra barriers: tcgen05.commit tracks every earlier MMA of
+// the issuing thread, so "S_t(j) ready" also means PV_t(j-1) has finished --
+// O_t may be rescaled and P_t's columns rewritten.
 // Causal tiles above the diagonal are skipped; only tiles that straddle the
 // diagonal or the key end are masked.  GQA: q-head h reads kv-head
 // h / (Hq/Hkv).  Every mbarrier wait is bounded (common.cuh).
@@ -30,22 +37,23 @@ namespace {
 
 __device__ int g_err_attn = 0;
 
-constexpr int BM = 128;
-constexpr int BN = 128;
-constexpr int kThreads = 192;
-constexpr int kWarpProducer = 4;
-constexpr int kWarpMma = 5;
+constexpr int BM = 128;  // rows per query tile
+constexpr int BN = 128;  // keys per K/V tile
+constexpr int kQTiles = 2;
+constexpr int kThreads = 320;
+constexpr int kWarpProducer = 8;
+constexpr int kWarpMma = 9;
+constexpr int kStages = 2;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemO = 256;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P <= 2^8 between rescales
 
 struct Bars {
     uint64_t q_full;
-    uint64_t k_full[2], k_empty[2];
-    uint64_t v_full[2], v_empty[2];
-    uint64_t s_full[2], s_empty[2];
-    uint64_t p_full[2];
-    uint64_t o_done;
+    uint64_t k_full[kStages], k_empty[kStages];
+    uint64_t v_full[kStages], v_empty[kStages];
+    uint64_t s_full[kQTiles];
+    uint64_t p_full[kQTiles];
+    uint64_t o_final;
     uint64_t drain;
     uint32_t tmem_base;
     int abort;
@@ -53,22 +61,21 @@ struct Bars {
 
 template <int D>
 struct Layout {
-    static constexpr int kQBytes = BM * D * 2;
+    static constexpr int kQTileBytes = BM * D * 2;
     static constexpr int kKVBytes = BN * D * 2;
-    static constexpr int kPBytes = BM * BN * 2;
     static constexpr int kQ = 0;
-    static constexpr int kK = kQ + kQBytes;
-    static constexpr int kV = kK + 2 * kKVBytes;
-    static constexpr int kP = kV + 2 * kKVBytes;
-    static constexpr int kBar = kP + 2 * kPBytes;
+    static constexpr int kK = kQ + kQTiles * kQTileBytes;
+    static constexpr int kV = kK + kStages * kKVBytes;
+    static constexpr int kBar = kV + kStages * kKVBytes;
     static constexpr int kBytes = kBar + (int)sizeof(Bars);
     static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
     static_assert(kAlloc <= 232448, "shared memory budget");
+    static constexpr uint32_t kTmemO = 256;       // O_t at kTmemO + t*D
 };
 
 struct Params {
     void* O;
-    int Hq, Sq, Skv, group, n_qtiles, causal;
+    int Hq, Sq, Skv, group, n_ctas, causal;
     float scale_log2;
 };
 
@@ -91,32 +98,34 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int qt = p.causal ? (p.n_qtiles - 1 - (int)blockIdx.x) : (int)blockIdx.x;
+    const int cta = p.causal ? (p.n_ctas - 1 - (int)blockIdx.x) : (int)blockIdx.x;
     const int hq = blockIdx.y;
     const int b = blockIdx.z;
-    const int q0 = qt * BM;
+    const int q0 = cta * (kQTiles * BM);
     const int off = p.Skv - p.Sq;
 
-    // number of key tiles this query tile needs
+    // key tiles this CTA needs: enough for its last valid query row
     const int nkv_all = (p.Skv + BN - 1) / BN;
     int nkv = nkv_all;
     if (p.causal) {
-        const long long lim = (long long)q0 + BM - 1 + off;  // last row's last visible key
+        const long long last_row = min(q0 + kQTiles * BM, p.Sq) - 1;
+        const long long lim = last_row + off;  // last visible key of that row
         nkv = lim < 0 ? 0 : min(nkv_all, (int)(lim / BN) + 1);
     }
 
     if (threadIdx.x == 0) {
         mbar_init(&bars->q_full, 1);
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < kStages; ++i) {
             mbar_init(&bars->k_full[i], 1);
             mbar_init(&bars->k_empty[i], 1);
             mbar_init(&bars->v_full[i], 1);
             mbar_init(&bars->v_empty[i], 1);
-            mbar_init(&bars->s_full[i], 1);
-            mbar_init(&bars->s_empty[i], 128);
-            mbar_init(&bars->p_full[i], 128);
         }
-        mbar_init(&bars->o_done, 1);
+        for (int t = 0; t < kQTiles; ++t) {
+            mbar_init(&bars->s_full[t], 1);
+            mbar_init(&bars->p_full[t], 128);
+        }
+        mbar_init(&bars->o_final, 1);
         mbar_init(&bars->drain, 1);
         bars->abort = 0;
         fence_barrier_init();
@@ -133,7 +142,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t sQ = smem_u32(smem + L::kQ);
     const uint32_t sK0 = smem_u32(smem + L::kK);
     const uint32_t sV0 = smem_u32(smem + L::kV);
-    const uint32_t sP0 = smem_u32(smem + L::kP);
 
     if (warp == kWarpProducer) {
         if (lane == 0) {
@@ -142,10 +150,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             prefetch_tmap(&tmV);
             const int bh_q = b * p.Hq + hq;
             const int bh_kv = b * (p.Hq / p.group) + hq / p.group;
-            mbar_arrive_expect_tx(&bars->q_full, L::kQBytes);
+            mbar_arrive_expect_tx(&bars->q_full, kQTiles * L::kQTileBytes);
 #pragma unroll
-            for (int a = 0; a < D / 64; ++a)
-                tma_load_3d(smem + L::kQ + a * BM * 128, &tmQ, &bars->q_full, a * 64, q0, bh_q);
+            for (int t = 0; t < kQTiles; ++t)
+#pragma unroll
+                for (int a = 0; a < D / 64; ++a)
+                    tma_load_3d(smem + L::kQ + t * L::kQTileBytes + a * BM * 128, &tmQ, &bars->q_full,
+                                a * 64, q0 + t * BM, bh_q);
             int issued = 0;
             for (int j = 0; j < nkv; ++j) {
                 const int st = j & 1;
@@ -181,67 +192,82 @@ __global__ void __launch_bounds__(kThreads, 1)
             constexpr uint32_t kFmt = Elem<T>::kFmt;
             constexpr uint32_t idesc_qk = make_idesc(kFmt, BM, BN, false, false);
             constexpr uint32_t idesc_pv = make_idesc(kFmt, BM, D, false, true);
-            bool ok = mbar_wait(&bars->q_full, 0, abort, &g_err_attn);
-            auto issue_pv = [&](int i) -> bool {
-                const int st = i & 1;
-                const uint32_t ph = (i >> 1) & 1;
-                if (!mbar_wait(&bars->v_full[st], ph, abort, &g_err_attn)) return false;
-                if (!mbar_wait(&bars->p_full[st], ph, abort, &g_err_attn)) return false;
-                tc_fence_after();
-                const uint32_t pa = sP0 + st * L::kPBytes;
-                const uint32_t va = sV0 + st * L::kKVBytes;
+            auto qk = [&](int t, int j) {  // S_t = Q_t K_j^T
+                const uint32_t qa = sQ + t * L::kQTileBytes;
+                const uint32_t ka = sK0 + (j & 1) * L::kKVBytes;
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    const uint32_t o = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
+                    mma_f16_ss(tmem + t * BN, smem_desc(qa + o, 16, 1024, kLayoutSW128),
+                               smem_desc(ka + o, 16, 1024, kLayoutSW128), idesc_qk, kk > 0 ? 1u : 0u);
+                }
+                mma_commit(&bars->s_full[t]);
+            };
+            auto pv = [&](int t, int j) {  // O_t += P_t V_j, P from TMEM
+                const uint32_t va = sV0 + (j & 1) * L::kKVBytes;
 #pragma unroll
                 for (int kk = 0; kk < BN / 16; ++kk) {
-                    // A = P tile, K-major, 128B-swizzled atoms of 64 keys.
-                    const uint64_t a = smem_desc(pa + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16,
-                                                 1024, kLayoutSW128);
-                    // B = V tile [key][d], MN-major: 16 keys = 2 groups of 8 rows.
-                    const uint64_t bd = smem_desc(va + kk * 16 * 128, BN * 128, 1024, kLayoutSW128);
-                    mma_f16_ss(tmem + kTmemO, a, bd, idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
+                    // B = V tile [key][d], MN-major: 16 keys = two 8-row groups; 64-column
+                    // boxes BN*128 bytes apart.
+                    mma_f16_ts(tmem + L::kTmemO + t * D, tmem + t * BN + kk * 8,
+                               smem_desc(va + kk * 16 * 128, BN * 128, 1024, kLayoutSW128), idesc_pv,
+                               (j > 0 || kk > 0) ? 1u : 0u);
                 }
-                mma_commit(&bars->v_empty[st]);
-                mma_commit(&bars->o_done);
-                return true;
             };
+            bool ok = mbar_wait(&bars->q_full, 0, abort, &g_err_attn);
+            if (ok && nkv > 0) {
+                ok = mbar_wait(&bars->k_full[0], 0, abort, &g_err_attn);
+                if (ok) {
+                    tc_fence_after();
+                    qk(0, 0);
+                    qk(1, 0);
+                    mma_commit(&bars->k_empty[0]);
+                }
+            }
             for (int j = 0; ok && j < nkv; ++j) {
                 const int st = j & 1;
                 const uint32_t ph = (j >> 1) & 1;
-                if (!mbar_wait(&bars->k_full[st], ph, abort, &g_err_attn)) { ok = false; break; }
-                if (!mbar_wait(&bars->s_empty[st], ph ^ 1, abort, &g_err_attn)) { ok = false; break; }
+                const int jn = j + 1;
+                if (!mbar_wait(&bars->v_full[st], ph, abort, &g_err_attn)) break;
+                // tile 0
+                if (!mbar_wait(&bars->p_full[0], j & 1, abort, &g_err_attn)) break;
                 tc_fence_after();
-                const uint32_t ka = sK0 + st * L::kKVBytes;
-#pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk) {
-                    const uint64_t a =
-                        smem_desc(sQ + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024, kLayoutSW128);
-                    const uint64_t bd =
-                        smem_desc(ka + (kk >> 2) * (BN * 128) + (kk & 3) * 32, 16, 1024, kLayoutSW128);
-                    mma_f16_ss(tmem + st * BN, a, bd, idesc_qk, kk > 0 ? 1u : 0u);
+                pv(0, j);
+                if (jn < nkv) {
+                    if (!mbar_wait(&bars->k_full[jn & 1], (jn >> 1) & 1, abort, &g_err_attn)) break;
+                    tc_fence_after();
+                    qk(0, jn);
                 }
-                mma_commit(&bars->s_full[st]);
-                mma_commit(&bars->k_empty[st]);
-                if (j > 0 && !issue_pv(j - 1)) { ok = false; break; }
+                // tile 1
+                if (!mbar_wait(&bars->p_full[1], j & 1, abort, &g_err_attn)) break;
+                tc_fence_after();
+                pv(1, j);
+                mma_commit(&bars->v_empty[st]);
+                if (jn < nkv) {
+                    qk(1, jn);
+                    mma_commit(&bars->k_empty[jn & 1]);
+                }
             }
-            if (ok && nkv > 0) issue_pv(nkv - 1);
+            mma_commit(&bars->o_final);
             // Drain: all MMAs issued by this thread are complete before TMEM is freed.
             mma_commit(&bars->drain);
             mbar_wait(&bars->drain, 0, abort, &g_err_attn);
         }
     } else {
-        // ---------------- softmax warps 0..3: thread owns query row r -------------
-        const int r = warp * 32 + lane;
-        const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-        const int qrow = q0 + r;
+        // ---------------- softmax warpgroups: tile t, thread owns query row r ------------
+        const int t = warp >> 2;
+        const int r = (warp & 3) * 32 + lane;
+        const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+        const uint32_t tS = tmem + lane_base + t * BN;
+        const uint32_t tO = tmem + lane_base + L::kTmemO + t * D;
+        const int qrow = q0 + t * BM + r;
         const int key_lim = p.causal ? min(p.Skv - 1, qrow + off) : (p.Skv - 1);
         const float sl2 = p.scale_log2;
         float m = -INFINITY;  // running max of scaled scores, log2 units
         float l = 0.f;
-        uint8_t* sP = smem + L::kP;
         bool ok = true;
         for (int j = 0; j < nkv; ++j) {
-            const int st = j & 1;
-            const uint32_t ph = (j >> 1) & 1;
-            if (!__all_sync(0xffffffffu, mbar_wait(&bars->s_full[st], ph, abort, &g_err_attn))) {
+            if (!__all_sync(0xffffffffu, mbar_wait(&bars->s_full[t], j & 1, abort, &g_err_attn))) {
                 ok = false;
                 break;
             }
@@ -249,16 +275,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t sr[BN];
 #pragma unroll
             for (int c = 0; c < BN / 32; ++c)
-                tmem_ld32(tmem + lane_base + st * BN + c * 32,
-                          *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
+                tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
             tmem_ld_wait();
-            tc_fence_before();
-            mbar_arrive(&bars->s_empty[st]);
 
             const int k0 = j * BN;
             const bool need_mask = k0 + BN - 1 > key_lim;
-            // row max as 8 independent chains (a single 128-long fmax chain is
-            // latency bound with one warp per SM sub-partition)
+            // row max as 8 independent chains
             float mx[8];
 #pragma unroll
             for (int u = 0; u < 8; ++u) mx[u] = -INFINITY;
@@ -288,60 +310,44 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             const float neg_mb = (m == -INFINITY) ? 0.f : -m;
 
-            // P_j -> shared (swizzled 128B rows), 8 keys per 16-byte chunk.
-            uint8_t* prow = sP + st * L::kPBytes + r * 128;
+            // P = exp2(s*c - m), packed two per 32-bit column, over S's first 64 columns
             float rs[8];
 #pragma unroll
             for (int u = 0; u < 8; ++u) rs[u] = 0.f;
+            uint32_t pk[BN / 2];
 #pragma unroll
-            for (int ch = 0; ch < BN / 8; ++ch) {
-                float e[8];
-#pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    e[u] = ex2(fmaf(__uint_as_float(sr[ch * 8 + u]), sl2, neg_mb));
-                    rs[u] += e[u];
-                }
-                uint4 pk;
-                pk.x = Elem<T>::pack2(e[0], e[1]);
-                pk.y = Elem<T>::pack2(e[2], e[3]);
-                pk.z = Elem<T>::pack2(e[4], e[5]);
-                pk.w = Elem<T>::pack2(e[6], e[7]);
-                const int atom = ch >> 3;
-                const int c16 = (ch & 7) ^ (r & 7);
-                *reinterpret_cast<uint4*>(prow + atom * (BM * 128) + c16 * 16) = pk;
+            for (int c = 0; c < BN; c += 2) {
+                const float e0 = ex2(fmaf(__uint_as_float(sr[c]), sl2, neg_mb));
+                const float e1 = ex2(fmaf(__uint_as_float(sr[c + 1]), sl2, neg_mb));
+                rs[c & 7] += e0;
+                rs[(c + 1) & 7] += e1;
+                pk[c >> 1] = Elem<T>::pack2(e0, e1);
             }
-            fence_proxy_async_smem();
+            tmem_st32(tS, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
+            tmem_st32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
             const float rowsum = ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
 
-            // PV_{j-1} must be complete before O is touched and before P[(j+1)%2]
-            // is rewritten next iteration.
-            if (j > 0) {
-                if (!__all_sync(0xffffffffu, mbar_wait(&bars->o_done, (j - 1) & 1, abort, &g_err_attn))) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                if (__any_sync(0xffffffffu, rescale)) {
+            // O_t is idle here: PV_t(j-1) finished before S_t(j) was signalled.
+            if (j > 0 && __any_sync(0xffffffffu, rescale)) {
 #pragma unroll
-                    for (int c = 0; c < D / 32; ++c) {
-                        uint32_t o[32];
-                        tmem_ld32(tmem + lane_base + kTmemO + c * 32, o);
-                        tmem_ld_wait();
+                for (int c = 0; c < D / 32; ++c) {
+                    uint32_t o[32];
+                    tmem_ld32(tO + c * 32, o);
+                    tmem_ld_wait();
 #pragma unroll
-                        for (int u = 0; u < 32; ++u) o[u] = __float_as_uint(__uint_as_float(o[u]) * alpha);
-                        tmem_st32(tmem + lane_base + kTmemO + c * 32, o);
-                    }
-                    tmem_st_wait();
+                    for (int u = 0; u < 32; ++u) o[u] = __float_as_uint(__uint_as_float(o[u]) * alpha);
+                    tmem_st32(tO + c * 32, o);
                 }
             }
+            tmem_st_wait();
             l = l * alpha + rowsum;
             tc_fence_before();
-            mbar_arrive(&bars->p_full[st]);
+            mbar_arrive(&bars->p_full[t]);
         }
 
         // ---------------- epilogue: O / l -> global -------------------------------
         if (ok && nkv > 0) {
-            ok = __all_sync(0xffffffffu, mbar_wait(&bars->o_done, (nkv - 1) & 1, abort, &g_err_attn));
+            ok = __all_sync(0xffffffffu, mbar_wait(&bars->o_final, 0, abort, &g_err_attn));
             tc_fence_after();
         }
         const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
@@ -350,7 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < D / 32; ++c) {
             uint32_t o[32];
             if (ok && nkv > 0) {
-                tmem_ld32(tmem + lane_base + kTmemO + c * 32, o);
+                tmem_ld32(tO + c * 32, o);
                 tmem_ld_wait();
             } else {
 #pragma unroll
@@ -359,16 +365,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (qrow < p.Sq) {
 #pragma unroll
                 for (int v4 = 0; v4 < 4; ++v4) {
-                    uint4 pk;
-                    pk.x = Elem<T>::pack2(__uint_as_float(o[v4 * 8 + 0]) * inv_l,
+                    uint4 q4;
+                    q4.x = Elem<T>::pack2(__uint_as_float(o[v4 * 8 + 0]) * inv_l,
                                           __uint_as_float(o[v4 * 8 + 1]) * inv_l);
-                    pk.y = Elem<T>::pack2(__uint_as_float(o[v4 * 8 + 2]) * inv_l,
+                    q4.y = Elem<T>::pack2(__uint_as_float(o[v4 * 8 + 2]) * inv_l,
                                           __uint_as_float(o[v4 * 8 + 3]) * inv_l);
-                    pk.z = Elem<T>::pack2(__uint_as_float(o[v4 * 8 + 4]) * inv_l,
+                    q4.z = Elem<T>::pack2(__uint_as_float(o[v4 * 8 + 4]) * inv_l,
                                           __uint_as_float(o[v4 * 8 + 5]) * inv_l);
-                    pk.w = Elem<T>::pack2(__uint_as_float(o[v4 * 8 + 6]) * inv_l,
+                    q4.w = Elem<T>::pack2(__uint_as_float(o[v4 * 8 + 6]) * inv_l,
                                           __uint_as_float(o[v4 * 8 + 7]) * inv_l);
-                    *reinterpret_cast<uint4*>(orow + c * 32 + v4 * 8) = pk;
+                    *reinterpret_cast<uint4*>(orow + c * 32 + v4 * 8) = q4;
                 }
             }
         }
@@ -403,10 +409,10 @@ int launch(const void* Q, const void* K, const void* V, void* O, int B, int Hq, 
     p.Sq = Sq;
     p.Skv = Skv;
     p.group = Hq / Hkv;
-    p.n_qtiles = (Sq + BM - 1) / BM;
+    p.n_ctas = (Sq + kQTiles * BM - 1) / (kQTiles * BM);
     p.causal = causal;
     p.scale_log2 = scale * 1.4426950408889634f;
-    dim3 grid(p.n_qtiles, Hq, B);
+    dim3 grid(p.n_ctas, Hq, B);
     kern<<<grid, kThreads, L::kAlloc, st>>>(tq, tk, tv, p);
     count_launch(1);
     return cudaGetLastError() == cudaSuccess ? B200LAB_OK : B200LAB_ERR_CUDA;

@@ -103,12 +103,15 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
                                           int* err) {
     if (mbar_test(bar, parity)) return true;
-    const unsigned long long t0 = globaltimer_ns();
-    for (uint32_t it = 0;; ++it) {
+    unsigned long long t0 = 0;  // the timer is read only once a wait is not short
+    for (uint32_t it = 1;; ++it) {
         if (mbar_test(bar, parity)) return true;
-        if ((it & 63u) == 63u) {
+        if ((it & 63u) == 0) {
             if (*abort) return false;
-            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            const unsigned long long now = globaltimer_ns();
+            if (t0 == 0) {
+                t0 = now;
+            } else if (now - t0 > kWaitLimitNs) {
                 *abort = 1;
                 atomicExch(err, B200LAB_ERR_TIMEOUT);
                 return false;
@@ -217,6 +220,18 @@ __device__ __forceinline__ void mma_tf32_ss(uint32_t d_tmem, uint64_t a_desc, ui
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem] (A from tensor memory, 16-bit values packed two
+// per 32-bit column, lane = row); issued by a single thread.
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                           uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 

@@ -350,6 +350,26 @@ struct StateParams {
     float scale;
 };
 
+// 32 consecutive outputs of one thread as 16-byte vector stores
+template <typename TOut>
+__device__ __forceinline__ void store_row32(TOut* dst, const float (&v)[32]) {
+    if constexpr (sizeof(TOut) == 4) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+            reinterpret_cast<float4*>(dst)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            uint4 pk;
+            pk.x = Elem<TOut>::pack2(v[8 * q + 0], v[8 * q + 1]);
+            pk.y = Elem<TOut>::pack2(v[8 * q + 2], v[8 * q + 3]);
+            pk.z = Elem<TOut>::pack2(v[8 * q + 4], v[8 * q + 5]);
+            pk.w = Elem<TOut>::pack2(v[8 * q + 6], v[8 * q + 7]);
+            reinterpret_cast<uint4*>(dst)[q] = pk;
+        }
+    }
+}
+
 template <typename T16, typename TOut>
 __global__ void __launch_bounds__(st::kThreads, 1)
     gdn_state_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -475,9 +495,29 @@ __global__ void __launch_bounds__(st::kThreads, 1)
         uint8_t* sS = smem + kSt;
         uint8_t* sVn = smem + kVn;
         uint8_t* sVt = smem + kVt;
+        // chunk inputs read by the threads (U slice row, gates) are fetched one
+        // chunk ahead so their latency hides behind the previous chunk
+        uint4 u_nx[kSlice / 8] = {};
+        float gcs_nx = 0.f, glast_nx = 0.f;
+        auto prefetch = [&](int c) {
+            const size_t bhc = bh * p.nch + c;
+            gcs_nx = gcs_all[bhc * kC + row];
+            glast_nx = gcs_all[bhc * kC + kC - 1];
+            if (warp < 2) {
+                const uint4* up = reinterpret_cast<const uint4*>(U_all + (bhc * kC + row) * kD + c0);
+#pragma unroll
+                for (int q8 = 0; q8 < kSlice / 8; ++q8) u_nx[q8] = up[q8];
+            }
+        };
+        if (p.nch > 0) prefetch(0);
         bool ok = true;
         for (int c = 0; c < p.nch && ok; ++c) {
-            const size_t bhc = bh * p.nch + c;
+            const float gcs_t = gcs_nx;
+            const float g_last = glast_nx;
+            uint4 u_raw[kSlice / 8];
+#pragma unroll
+            for (int q8 = 0; q8 < kSlice / 8; ++q8) u_raw[q8] = u_nx[q8];
+            if (c + 1 < p.nch) prefetch(c + 1);
             // S (16-bit) -> shared, B operand of MMA1: row = v column cc, col = key i
 #pragma unroll
             for (int cc = 0; cc < kSlice; ++cc)
@@ -487,15 +527,11 @@ __global__ void __launch_bounds__(st::kThreads, 1)
             tc_fence_before();
             mbar_arrive(&ms->s_ready);
 
-            const float gcs_t = gcs_all[bhc * kC + row];
-            const float g_last = gcs_all[bhc * kC + kC - 1];
             if (warp < 2) {
                 float u[kSlice];
-                const uint4* up = reinterpret_cast<const uint4*>(U_all + (bhc * kC + row) * kD + c0);
 #pragma unroll
                 for (int q8 = 0; q8 < kSlice / 8; ++q8) {
-                    const uint4 raw = up[q8];
-                    const T16* e = reinterpret_cast<const T16*>(&raw);
+                    const T16* e = reinterpret_cast<const T16*>(&u_raw[q8]);
 #pragma unroll
                     for (int u8 = 0; u8 < 8; ++u8) u[q8 * 8 + u8] = Elem<T16>::to_f(e[u8]);
                 }
@@ -527,11 +563,11 @@ __global__ void __launch_bounds__(st::kThreads, 1)
                 const int tt = c * kC + row;
                 if (tt < p.T) {
                     const float eg = __expf(gcs_t);
-                    TOut* op = static_cast<TOut*>(p.o) + (((size_t)b * p.T + tt) * p.Hv + h) * kD + c0;
+                    float ov[kSlice];
 #pragma unroll
                     for (int cc = 0; cc < kSlice; ++cc)
-                        op[cc] = Elem<TOut>::from_f(
-                            p.scale * fmaf(eg, __uint_as_float(pq[cc]), __uint_as_float(oi[cc])));
+                        ov[cc] = p.scale * fmaf(eg, __uint_as_float(pq[cc]), __uint_as_float(oi[cc]));
+                    store_row32(static_cast<TOut*>(p.o) + (((size_t)b * p.T + tt) * p.Hv + h) * kD + c0, ov);
                 }
             }
             uint32_t ds[32];
@@ -656,7 +692,8 @@ extern "C" int gdn_prefill_sm100(const void* q, const void* k, const void* v, co
     if (in_dtype == B200LAB_F32) return B200LAB_ERR_UNSUPPORTED;  // 16-bit operands only
     if (B > 65535 || Hv > 65535) return B200LAB_ERR_UNSUPPORTED;
     if (T == 0) return B200LAB_OK;
-    if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(state, 16))
+    if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(state, 16) ||
+        !aligned(o, 16))
         return B200LAB_ERR_INVALID;
     const size_t need = gdn_prefill_sm100_workspace(B, T, Hqk, Hv, dk, dv);
     if (!workspace || ws_bytes < need || !aligned(workspace, 256)) return B200LAB_ERR_WORKSPACE;
