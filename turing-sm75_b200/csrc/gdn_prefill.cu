@@ -19,8 +19,8 @@
 // Kernel 1, gdn_prep_kernel: one CTA per (b, v-head, chunk), fully parallel.
 //   TMA loads K, Q, V chunk tiles; ONE M=128 tcgen05 MMA gives [K;Q] K^T
 //   (lanes 0-63: K K^T, lanes 64-127: Q K^T); the threads form A and Aqk,
-//   solve T by column-parallel forward substitution in fp32, and ONE M=128,
-//   N=256 MMA gives [T diag(beta Gam); T diag(beta)] [K | V] -> W and U.
+//   invert (I + A) column-parallel in fp32, and two M=128, N=128 MMAs give
+//   [T diag(beta Gam); T diag(beta)] K -> W and [...] V -> U.
 //   W, U, Aqk (16-bit) and gcs (fp32) go to the workspace.
 // Kernel 2, gdn_state_kernel: one CTA per (b, v-head, 32-column slice of the
 //   state), sequential over chunks.  The fp32 state slice lives in registers
@@ -83,23 +83,66 @@ __device__ __forceinline__ uint32_t sw128_off(int r, int j) {
 namespace prep {
 constexpr int kThreads = 128;
 // shared layout (bytes)
-constexpr int kTiles = 0;          // [K0|Q0|K1|Q1|V0|pad|V1|pad], 8 KiB each
-constexpr int kK0 = 0, kQ0 = 8192, kK1 = 16384, kQ1 = 24576, kV0 = 32768, kV1 = 49152;
-constexpr int kAT = 65536;         // [T diag(beta Gam); T diag(beta)] 128 x 64, 16 KiB
-constexpr int kAs = 81920;         // A (fp32 64 x 64), 16 KiB
-constexpr int kMisc = 98304;       // gcs[64], beta[64], barriers
+constexpr int kTiles = 0;          // [K0|Q0|K1|Q1|V0|V1], 8 KiB each (64 tokens x 64 dims)
+constexpr int kK0 = 0, kQ0 = 8192, kK1 = 16384, kQ1 = 24576, kV0 = 32768, kV1 = 40960;
+constexpr int kAT = 49152;         // [T diag(beta Gam); T diag(beta)] 128 x 64, 16 KiB
+constexpr int kLd = 68;            // fp32 row pitch of A and T (16-byte aligned, fewer conflicts)
+constexpr int kAs = 65536;         // A, fp32 64 x kLd
+constexpr int kMisc = kAs + kC * kLd * 4;
 constexpr int kBytes = kMisc + 1024;
 constexpr int kAlloc = kBytes + 1024;
 constexpr uint32_t kTmemCols = 256;
 
 struct Misc {
-    float gcs[kC];
+    float gcs[kC];   // natural log units (stored to the workspace)
+    float g2[kC];    // gcs * log2(e), for ex2
     float beta[kC];
     uint64_t bar_tma, bar_mma1, bar_mma2, drain;
     uint32_t tmem_base;
     int abort;
 };
 }  // namespace prep
+
+__device__ __forceinline__ float ex2f(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// Column j of T = (I + A)^-1 for a strictly lower 64 x 64 A (fp32, shared,
+// row pitch kLd), by forward substitution: T[t][j] = [t==j] - sum_{s<t} A[t][s] T[s][j].
+// Rows are processed in blocks of 8: the contributions of all earlier rows to
+// the 8 rows of a block are 8 independent dot-product chains (ILP), then the
+// 8 x 8 triangle of the block is resolved.  Every A read is a broadcast.
+__device__ __forceinline__ void inverse_column(const float* As, int j, float (&col)[kC]) {
+    using prep::kLd;
+#pragma unroll
+    for (int b = 0; b < kC / 8; ++b) {
+        const int t0 = b * 8;
+        float acc[8];
+#pragma unroll
+        for (int r = 0; r < 8; ++r) acc[r] = 0.f;
+#pragma unroll
+        for (int s = 0; s < t0; s += 4) {
+#pragma unroll
+            for (int r = 0; r < 8; ++r) {
+                const float4 a = *reinterpret_cast<const float4*>(As + (t0 + r) * kLd + s);
+                acc[r] = fmaf(a.x, col[s], acc[r]);
+                acc[r] = fmaf(a.y, col[s + 1], acc[r]);
+                acc[r] = fmaf(a.z, col[s + 2], acc[r]);
+                acc[r] = fmaf(a.w, col[s + 3], acc[r]);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+            const int t = t0 + r;
+            float x = acc[r];
+#pragma unroll
+            for (int s = 0; s < r; ++s) x = fmaf(As[t * kLd + t0 + s], col[t0 + s], x);
+            col[t] = t < j ? 0.f : (t == j ? 1.f : -x);
+        }
+    }
+}
 
 template <typename T16>
 __global__ void __launch_bounds__(prep::kThreads, 2)
@@ -166,7 +209,12 @@ __global__ void __launch_bounds__(prep::kThreads, 2)
         ms->beta[tid] = be;
     }
     __syncthreads();
-    if (tid >= 32 && tid < kC) ms->gcs[tid] += ms->gcs[31];
+    if (tid < kC) {
+        const float g = tid >= 32 ? ms->gcs[tid] + ms->gcs[31] : ms->gcs[tid];
+        __syncwarp();
+        ms->gcs[tid] = g;
+        ms->g2[tid] = g * 1.4426950408889634f;
+    }
     __syncthreads();
 
     // MMA1: [K;Q] K^T  (M=128, N=64, K=128)
@@ -191,6 +239,7 @@ __global__ void __launch_bounds__(prep::kThreads, 2)
     const int row = (warp & 1) * 32 + lane;  // token within the chunk
     const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
     const float gcs_r = ms->gcs[row];
+    const float g2_r = ms->g2[row];
     if (ok) {
         uint32_t v[64];
         tmem_ld32(tmem + lane_base + 0, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
@@ -206,9 +255,9 @@ __global__ void __launch_bounds__(prep::kThreads, 2)
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     const int ss = s + u;
-                    pa[u] = ss < row ? be * __uint_as_float(v[ss]) * __expf(gcs_r - ms->gcs[ss]) : 0.f;
+                    pa[u] = ss < row ? be * __uint_as_float(v[ss]) * ex2f(g2_r - ms->g2[ss]) : 0.f;
                 }
-                *reinterpret_cast<float4*>(As + row * kC + s) = a;
+                *reinterpret_cast<float4*>(As + row * kLd + s) = a;
             }
         } else {
             // Aqk row (lower incl. diagonal), 16-bit, straight to the workspace
@@ -220,8 +269,8 @@ __global__ void __launch_bounds__(prep::kThreads, 2)
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     const int s0 = s + 2 * u, s1 = s0 + 1;
-                    const float a0 = s0 <= row ? __uint_as_float(v[s0]) * __expf(gcs_r - ms->gcs[s0]) : 0.f;
-                    const float a1 = s1 <= row ? __uint_as_float(v[s1]) * __expf(gcs_r - ms->gcs[s1]) : 0.f;
+                    const float a0 = s0 <= row ? __uint_as_float(v[s0]) * ex2f(g2_r - ms->g2[s0]) : 0.f;
+                    const float a1 = s1 <= row ? __uint_as_float(v[s1]) * ex2f(g2_r - ms->g2[s1]) : 0.f;
                     pw[u] = Elem<T16>::pack2(a0, a1);
                 }
                 *reinterpret_cast<uint4*>(dst + s) = pk;
@@ -230,29 +279,13 @@ __global__ void __launch_bounds__(prep::kThreads, 2)
     }
     __syncthreads();
 
-    // T = (I + A)^-1: thread j < 64 computes column j by forward substitution.
-    if (warp < 2 && ok) {
+    if (tid < kC) {
+        // thread j: column j of T, scaled into rows 0-63 (T diag(beta Gam)) and 64-127 (T diag(beta))
         const int j = tid;
         float col[kC];
-#pragma unroll
-        for (int t = 0; t < kC; ++t) {
-            float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
-#pragma unroll
-            for (int s = 0; s + 3 < t; s += 4) {
-                const float4 a = *reinterpret_cast<const float4*>(As + t * kC + s);
-                acc0 = fmaf(a.x, col[s], acc0);
-                acc1 = fmaf(a.y, col[s + 1], acc1);
-                acc2 = fmaf(a.z, col[s + 2], acc2);
-                acc3 = fmaf(a.w, col[s + 3], acc3);
-            }
-#pragma unroll
-            for (int s = (t & ~3); s < t; ++s) acc0 = fmaf(As[t * kC + s], col[s], acc0);
-            const float x = -((acc0 + acc1) + (acc2 + acc3));
-            col[t] = t < j ? 0.f : (t == j ? 1.f : x);
-        }
-        // columns scaled: rows 0-63 <- T diag(beta Gam), rows 64-127 <- T diag(beta)
+        inverse_column(As, j, col);
         const float bj = ms->beta[j];
-        const float bgj = bj * __expf(ms->gcs[j]);
+        const float bgj = bj * ex2f(ms->g2[j]);
         uint8_t* at = smem + kAT;
 #pragma unroll
         for (int t = 0; t < kC; ++t) {
@@ -264,16 +297,20 @@ __global__ void __launch_bounds__(prep::kThreads, 2)
     tc_fence_before();
     __syncthreads();
 
-    // MMA2: [T'; T''] [K | V]  (M=128, N=256, K=64); B is MN-major over 4 chunks of 64
+    // MMA2: [T'; T''] K  -> cols 0-127, [T'; T''] V -> cols 128-255  (M=128, N=128, K=64);
+    // B operands MN-major: K chunks 16 KiB apart ([K0|Q0|K1|Q1]), V chunks 8 KiB apart
     if (tid == 0 && ok) {
         tc_fence_after();
-        constexpr uint32_t idesc = make_idesc(Elem<T16>::kFmt, 128, 256, false, true);
+        constexpr uint32_t idesc = make_idesc(Elem<T16>::kFmt, 128, 128, false, true);
         const uint32_t a0 = smem_u32(smem + kAT);
-        const uint32_t b0 = smem_u32(smem + kTiles);
+        const uint32_t bk = smem_u32(smem + kK0);
+        const uint32_t bv = smem_u32(smem + kV0);
 #pragma unroll
         for (int kk = 0; kk < kC / 16; ++kk) {
             mma_f16_ss(tmem, smem_desc(a0 + kk * 32, 16, 1024, kLayoutSW128),
-                       smem_desc(b0 + kk * 2048, 16384, 1024, kLayoutSW128), idesc, kk > 0 ? 1u : 0u);
+                       smem_desc(bk + kk * 2048, 16384, 1024, kLayoutSW128), idesc, kk > 0 ? 1u : 0u);
+            mma_f16_ss(tmem + 128, smem_desc(a0 + kk * 32, 16, 1024, kLayoutSW128),
+                       smem_desc(bv + kk * 2048, 8192, 1024, kLayoutSW128), idesc, kk > 0 ? 1u : 0u);
         }
         mma_commit(&ms->bar_mma2);
     }
