@@ -106,3 +106,29 @@ def test_oracle_and_kernel_vs_reference_naive(cuda, B, H, S, D):
     assert_close(to_np(O), ref64, "vs oracle")
     ea2, _ = errors(to_np(O), to_np(On))
     assert ea2 < 2e-2, ea2       # the reference's own PASS bar (src/attn_sm75.cu:501)
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,Sq,Skv,D", [(1, 8, 2, 1, 4096, 128), (2, 4, 4, 64, 3000, 64),
+                                               (1, 4, 1, 300, 5000, 128), (1, 2, 2, 17, 1025, 128)])
+@pytest.mark.parametrize("causal", [False, True])
+def test_split_kv_short_queries(cuda, B, Hq, Hkv, Sq, Skv, D, causal):
+    """Short queries over long keys take the split-KV path (partials + combine)."""
+    assert b200lab.lib().attn_fwd_sm100_workspace(B, Hq, Hkv, Sq, Skv, D, int(causal)) > 0
+    O, ref = _run(B, Hq, Hkv, Sq, Skv, D, causal, torch.bfloat16, seed=Sq * 7 + Skv)
+    assert_close(O, ref, f"split-KV Sq{Sq} Skv{Skv}")
+
+
+def test_split_kv_without_workspace_runs_unsplit(cuda):
+    """A caller that passes no workspace gets the single-pass kernel: same result."""
+    import ctypes
+    dev = torch.device("cuda:0")
+    Q, K, V = (t.to(dev) for t in workloads.attn_inputs(1, 8, 2, 1, 128, torch.bfloat16, Skv=4096))
+    O1 = b200lab.attn_fwd(Q, K, V, causal=False)
+    O2 = torch.empty_like(O1)
+    p = lambda t: ctypes.c_void_p(t.data_ptr())
+    st = b200lab.lib().attn_fwd_sm100(p(Q), p(K), p(V), p(O2), 1, 8, 2, 1, 4096, 128,
+                                      1.0 / np.sqrt(128), 0, b200lab.BF16, ctypes.c_void_p(0), 0,
+                                      ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert st == b200lab.OK
+    assert b200lab.device_status() == b200lab.OK
+    assert_close(to_np(O2), to_np(O1), "unsplit vs split")

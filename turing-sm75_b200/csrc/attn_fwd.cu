@@ -28,7 +28,10 @@
 // O_t may be rescaled and P_t's columns rewritten.
 // Causal tiles above the diagonal are skipped; only tiles that straddle the
 // diagonal or the key end are masked.  GQA: q-head h reads kv-head
-// h / (Hq/Hkv).  Every mbarrier wait is bounded (common.cuh).
+// h / (Hq/Hkv).  Split-KV: when the (query-tile pair, head, batch) grid cannot
+// fill the GPU (short queries), the key tiles are split over extra CTAs that
+// write fp32 partials (O, max, sum) to the caller's workspace, merged by
+// attn_combine_kernel.  Every mbarrier wait is bounded (common.cuh).
 #include "common.cuh"
 #include "errwords.h"
 
@@ -75,7 +78,10 @@ struct Layout {
 
 struct Params {
     void* O;
+    float* part_o;   // split-KV partials: [B*Hq*Sq][nsplit][D] fp32 (unnormalised)
+    float* part_ml;  // [B*Hq*Sq][nsplit][2]: running max (log2 units), row sum
     int Hq, Sq, Skv, group, n_ctas, causal;
+    int nsplit, tiles_per_split;
     float scale_log2;
 };
 
@@ -85,7 +91,7 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
-template <int D, typename T>
+template <int D, typename T, bool kSplit>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const Params p) {
@@ -98,20 +104,25 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int cta = p.causal ? (p.n_ctas - 1 - (int)blockIdx.x) : (int)blockIdx.x;
+    const int split = (int)blockIdx.x % p.nsplit;
+    const int cta_lin = (int)blockIdx.x / p.nsplit;
+    const int cta = p.causal ? (p.n_ctas - 1 - cta_lin) : cta_lin;
     const int hq = blockIdx.y;
     const int b = blockIdx.z;
     const int q0 = cta * (kQTiles * BM);
     const int off = p.Skv - p.Sq;
 
-    // key tiles this CTA needs: enough for its last valid query row
+    // key tiles this CTA needs: enough for its last valid query row, then the
+    // part [j0, j0 + nkv) of them that belongs to this CTA's key split
     const int nkv_all = (p.Skv + BN - 1) / BN;
-    int nkv = nkv_all;
+    int nkv_need = nkv_all;
     if (p.causal) {
         const long long last_row = min(q0 + kQTiles * BM, p.Sq) - 1;
         const long long lim = last_row + off;  // last visible key of that row
-        nkv = lim < 0 ? 0 : min(nkv_all, (int)(lim / BN) + 1);
+        nkv_need = lim < 0 ? 0 : min(nkv_all, (int)(lim / BN) + 1);
     }
+    const int j0 = split * p.tiles_per_split;
+    const int nkv = max(0, min(nkv_need - j0, p.tiles_per_split));
 
     if (threadIdx.x == 0) {
         mbar_init(&bars->q_full, 1);
@@ -166,7 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int a = 0; a < D / 64; ++a)
                     tma_load_3d(smem + L::kK + st * L::kKVBytes + a * BN * 128, &tmK,
-                                &bars->k_full[st], a * 64, j * BN, bh_kv);
+                                &bars->k_full[st], a * 64, (j0 + j) * BN, bh_kv);
                 if (!mbar_wait(&bars->v_empty[st], ph ^ 1, abort, &g_err_attn)) {
                     issued = -(j + 1);  // K_j issued, V_j not
                     break;
@@ -175,7 +186,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int a = 0; a < D / 64; ++a)
                     tma_load_3d(smem + L::kV + st * L::kKVBytes + a * BN * 128, &tmV,
-                                &bars->v_full[st], a * 64, j * BN, bh_kv);
+                                &bars->v_full[st], a * 64, (j0 + j) * BN, bh_kv);
                 issued = j + 1;
             }
             // Drain: every TMA load this thread issued has landed before exit.
@@ -278,7 +289,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
             tmem_ld_wait();
 
-            const int k0 = j * BN;
+            const int k0 = (j0 + j) * BN;
             const bool need_mask = k0 + BN - 1 > key_lim;
             // row max as 8 independent chains
             float mx[8];
@@ -345,36 +356,65 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_arrive(&bars->p_full[t]);
         }
 
-        // ---------------- epilogue: O / l -> global -------------------------------
+        // ---------------- epilogue -------------------------------------------------
         if (ok && nkv > 0) {
             ok = __all_sync(0xffffffffu, mbar_wait(&bars->o_final, 0, abort, &g_err_attn));
             tc_fence_after();
         }
-        const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
-        T* orow = static_cast<T*>(p.O) + ((size_t)(b * p.Hq + hq) * p.Sq + qrow) * D;
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-            uint32_t o[32];
-            if (ok && nkv > 0) {
-                tmem_ld32(tO + c * 32, o);
-                tmem_ld_wait();
-            } else {
-#pragma unroll
-                for (int u = 0; u < 32; ++u) o[u] = 0u;
-            }
+        if constexpr (kSplit) {
+            // split-KV partial: unnormalised O, running max and sum, fp32
             if (qrow < p.Sq) {
+                const size_t prow = ((size_t)(b * p.Hq + hq) * p.Sq + qrow) * p.nsplit + split;
+                float* po = p.part_o + prow * D;
+                float2 ml = make_float2(m, l);
+                if (!(ok && nkv > 0)) ml = make_float2(-INFINITY, 0.f);
+                *reinterpret_cast<float2*>(p.part_ml + prow * 2) = ml;
+            }
 #pragma unroll
-                for (int v4 = 0; v4 < 4; ++v4) {
-                    uint4 q4;
-                    q4.x = Elem<T>::pack2(__uint_as_float(o[v4 * 8 + 0]) * inv_l,
-                                          __uint_as_float(o[v4 * 8 + 1]) * inv_l);
-                    q4.y = Elem<T>::pack2(__uint_as_float(o[v4 * 8 + 2]) * inv_l,
-                                          __uint_as_float(o[v4 * 8 + 3]) * inv_l);
-                    q4.z = Elem<T>::pack2(__uint_as_float(o[v4 * 8 + 4]) * inv_l,
-                                          __uint_as_float(o[v4 * 8 + 5]) * inv_l);
-                    q4.w = Elem<T>::pack2(__uint_as_float(o[v4 * 8 + 6]) * inv_l,
-                                          __uint_as_float(o[v4 * 8 + 7]) * inv_l);
-                    *reinterpret_cast<uint4*>(orow + c * 32 + v4 * 8) = q4;
+            for (int c = 0; c < D / 32; ++c) {
+                uint32_t o[32];
+                if (ok && nkv > 0) {
+                    tmem_ld32(tO + c * 32, o);
+                    tmem_ld_wait();
+                } else {
+#pragma unroll
+                    for (int u = 0; u < 32; ++u) o[u] = 0u;
+                }
+                if (qrow < p.Sq) {
+                    float* po = p.part_o + (((size_t)(b * p.Hq + hq) * p.Sq + qrow) * p.nsplit + split) * D;
+#pragma unroll
+                    for (int v4 = 0; v4 < 8; ++v4)
+                        *reinterpret_cast<uint4*>(po + c * 32 + v4 * 4) =
+                            make_uint4(o[v4 * 4], o[v4 * 4 + 1], o[v4 * 4 + 2], o[v4 * 4 + 3]);
+                }
+            }
+        } else {
+            const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
+            T* orow = static_cast<T*>(p.O) + ((size_t)(b * p.Hq + hq) * p.Sq + qrow) * D;
+#pragma unroll
+            for (int c = 0; c < D / 32; ++c) {
+                uint32_t o[32];
+                if (ok && nkv > 0) {
+                    tmem_ld32(tO + c * 32, o);
+                    tmem_ld_wait();
+                } else {
+#pragma unroll
+                    for (int u = 0; u < 32; ++u) o[u] = 0u;
+                }
+                if (qrow < p.Sq) {
+#pragma unroll
+                    for (int v4 = 0; v4 < 4; ++v4) {
+                        uint4 q4;
+                        q4.x = Elem<T>::pack2(__uint_as_float(o[v4 * 8 + 0]) * inv_l,
+                                              __uint_as_float(o[v4 * 8 + 1]) * inv_l);
+                        q4.y = Elem<T>::pack2(__uint_as_float(o[v4 * 8 + 2]) * inv_l,
+                                              __uint_as_float(o[v4 * 8 + 3]) * inv_l);
+                        q4.z = Elem<T>::pack2(__uint_as_float(o[v4 * 8 + 4]) * inv_l,
+                                              __uint_as_float(o[v4 * 8 + 5]) * inv_l);
+                        q4.w = Elem<T>::pack2(__uint_as_float(o[v4 * 8 + 6]) * inv_l,
+                                              __uint_as_float(o[v4 * 8 + 7]) * inv_l);
+                        *reinterpret_cast<uint4*>(orow + c * 32 + v4 * 8) = q4;
+                    }
                 }
             }
         }
@@ -388,9 +428,81 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// Split-KV combine: one warp per query row merges the nsplit partials,
+//   M = max_s m_s,  O = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s   (0 if no key seen).
+template <int D, typename T>
+__global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restrict__ part_o,
+                                                           const float* __restrict__ part_ml,
+                                                           T* __restrict__ O, long long rows, int nsplit) {
+    const long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const float2* ml = reinterpret_cast<const float2*>(part_ml) + row * nsplit;
+    float M = -INFINITY;
+    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, ml[s].x);
+    constexpr int kPer = D / 32;  // values per lane (4 or 2)
+    float acc[kPer];
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) acc[u] = 0.f;
+    float L = 0.f;
+    if (M != -INFINITY) {
+        for (int s = 0; s < nsplit; ++s) {
+            const float2 e = ml[s];
+            if (!(e.y > 0.f)) continue;
+            const float w = ex2(e.x - M);
+            L = fmaf(w, e.y, L);
+            const float* po = part_o + (row * nsplit + s) * D + lane * kPer;
+#pragma unroll
+            for (int u = 0; u < kPer; ++u) acc[u] = fmaf(w, po[u], acc[u]);
+        }
+    }
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    T* orow = O + row * D + lane * kPer;
+#pragma unroll
+    for (int u = 0; u < kPer; u += 2) {
+        const uint32_t pk = Elem<T>::pack2(acc[u] * inv, acc[u + 1] * inv);
+        *reinterpret_cast<uint32_t*>(orow + u) = pk;
+    }
+}
+
+inline size_t align_up_floats(size_t n) { return (n + 63) / 64 * 64; }  // 256-byte steps
+
+// Key splits for a launch: split the key tiles only when the (query-tile pair,
+// q-head, batch) grid cannot fill the GPU; each split gets >= 2 key tiles.
+struct SplitPlan {
+    int nsplit, tiles_per_split;
+};
+SplitPlan plan_splits(int B, int Hq, int Sq, int Skv) {
+    int sms = 148;
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) {
+        int v = 0;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0) sms = v;
+    }
+    const long long base = (long long)((Sq + kQTiles * BM - 1) / (kQTiles * BM)) * Hq * B;
+    const int nkv = (Skv + BN - 1) / BN;
+    SplitPlan sp{1, nkv};
+    if (base >= sms || nkv < 4) return sp;
+    long long want_ll = (sms + base - 1) / base;
+    if (want_ll > 64) want_ll = 64;
+    int want = (int)want_ll;
+    want = min(want, nkv / 2);
+    if (want < 2) return sp;
+    sp.tiles_per_split = (nkv + want - 1) / want;
+    sp.nsplit = (nkv + sp.tiles_per_split - 1) / sp.tiles_per_split;
+    return sp;
+}
+
+size_t split_workspace_bytes(int B, int Hq, int Sq, int Skv, int D) {
+    const SplitPlan sp = plan_splits(B, Hq, Sq, Skv);
+    if (sp.nsplit <= 1) return 0;
+    const size_t rows = (size_t)B * Hq * Sq;
+    return rows * sp.nsplit * ((size_t)D + 2) * sizeof(float) + 256;
+}
+
 template <int D, typename T>
 int launch(const void* Q, const void* K, const void* V, void* O, int B, int Hq, int Hkv, int Sq,
-           int Skv, float scale, int causal, cudaStream_t st) {
+           int Skv, float scale, int causal, void* ws, size_t ws_bytes, cudaStream_t st) {
     using L = Layout<D>;
     const CUtensorMapDataType dt = Elem<T>::kFmt == 0 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                       : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
@@ -401,8 +513,6 @@ int launch(const void* Q, const void* K, const void* V, void* O, int B, int Hq, 
     if (rc) return rc;
     rc = make_tmap_3d(&tv, V, dt, 2, D, Skv, (uint64_t)B * Hkv, 64, BN, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
-    auto kern = attn_fwd_kernel<D, T>;
-    B200_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc));
     Params p;
     p.O = O;
     p.Hq = Hq;
@@ -412,10 +522,31 @@ int launch(const void* Q, const void* K, const void* V, void* O, int B, int Hq, 
     p.n_ctas = (Sq + kQTiles * BM - 1) / (kQTiles * BM);
     p.causal = causal;
     p.scale_log2 = scale * 1.4426950408889634f;
-    dim3 grid(p.n_ctas, Hq, B);
+    SplitPlan sp = plan_splits(B, Hq, Sq, Skv);
+    const size_t need = split_workspace_bytes(B, Hq, Sq, Skv, D);
+    if (sp.nsplit > 1 && (ws == nullptr || ws_bytes < need)) sp = SplitPlan{1, (Skv + BN - 1) / BN};
+    p.nsplit = sp.nsplit;
+    p.tiles_per_split = sp.tiles_per_split;
+    const size_t rows = (size_t)B * Hq * Sq;
+    p.part_o = nullptr;
+    p.part_ml = nullptr;
+    if (sp.nsplit > 1) {
+        p.part_ml = static_cast<float*>(ws);
+        p.part_o = p.part_ml + align_up_floats(rows * sp.nsplit * 2);
+    }
+    dim3 grid(p.n_ctas * p.nsplit, Hq, B);
+    auto kern = sp.nsplit > 1 ? attn_fwd_kernel<D, T, true> : attn_fwd_kernel<D, T, false>;
+    B200_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc));
     kern<<<grid, kThreads, L::kAlloc, st>>>(tq, tk, tv, p);
     count_launch(1);
-    return cudaGetLastError() == cudaSuccess ? B200LAB_OK : B200LAB_ERR_CUDA;
+    B200_TRY_CUDA(cudaGetLastError());
+    if (sp.nsplit > 1) {
+        attn_combine_kernel<D, T><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(
+            p.part_o, p.part_ml, static_cast<T*>(O), (long long)rows, sp.nsplit);
+        count_launch(1);
+        B200_TRY_CUDA(cudaGetLastError());
+    }
+    return B200LAB_OK;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -427,16 +558,16 @@ B200_DEFINE_ERR_TAKER(attn, b200::g_err_attn)
 
 extern "C" size_t attn_fwd_sm100_workspace(int B, int Hq, int Hkv, int Sq, int Skv, int D,
                                            int causal) {
-    (void)B; (void)Hq; (void)Hkv; (void)Sq; (void)Skv; (void)D; (void)causal;
-    return 0;
+    (void)Hkv;
+    (void)causal;
+    if (B < 1 || Hq < 1 || Sq < 1 || Skv < 1 || (D != 64 && D != 128)) return 0;
+    return b200::split_workspace_bytes(B, Hq, Sq, Skv, D);
 }
 
 extern "C" int attn_fwd_sm100(const void* Q, const void* K, const void* V, void* O, int B, int Hq,
                               int Hkv, int Sq, int Skv, int D, float scale, int causal, int dtype,
                               void* workspace, size_t ws_bytes, void* stream) {
     using namespace b200;
-    (void)workspace;
-    (void)ws_bytes;
     if (!Q || !K || !V || !O) return B200LAB_ERR_INVALID;
     if (B < 1 || Hq < 1 || Hkv < 1 || Sq < 1 || Skv < 1 || Hq % Hkv != 0) return B200LAB_ERR_INVALID;
     if (dtype != B200LAB_F16 && dtype != B200LAB_BF16) return B200LAB_ERR_INVALID;
@@ -449,9 +580,9 @@ extern "C" int attn_fwd_sm100(const void* Q, const void* K, const void* V, void*
     if (rc != B200LAB_OK) return rc;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (dtype == B200LAB_BF16) {
-        return D == 128 ? launch<128, __nv_bfloat16>(Q, K, V, O, B, Hq, Hkv, Sq, Skv, scale, causal, st)
-                        : launch<64, __nv_bfloat16>(Q, K, V, O, B, Hq, Hkv, Sq, Skv, scale, causal, st);
+        return D == 128 ? launch<128, __nv_bfloat16>(Q, K, V, O, B, Hq, Hkv, Sq, Skv, scale, causal, workspace, ws_bytes, st)
+                        : launch<64, __nv_bfloat16>(Q, K, V, O, B, Hq, Hkv, Sq, Skv, scale, causal, workspace, ws_bytes, st);
     }
-    return D == 128 ? launch<128, __half>(Q, K, V, O, B, Hq, Hkv, Sq, Skv, scale, causal, st)
-                    : launch<64, __half>(Q, K, V, O, B, Hq, Hkv, Sq, Skv, scale, causal, st);
+    return D == 128 ? launch<128, __half>(Q, K, V, O, B, Hq, Hkv, Sq, Skv, scale, causal, workspace, ws_bytes, st)
+                    : launch<64, __half>(Q, K, V, O, B, Hq, Hkv, Sq, Skv, scale, causal, workspace, ws_bytes, st);
 }
