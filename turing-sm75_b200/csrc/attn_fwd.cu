@@ -325,17 +325,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             float rs[8];
 #pragma unroll
             for (int u = 0; u < 8; ++u) rs[u] = 0.f;
-            uint32_t pk[BN / 2];
 #pragma unroll
-            for (int c = 0; c < BN; c += 2) {
-                const float e0 = ex2(fmaf(__uint_as_float(sr[c]), sl2, neg_mb));
-                const float e1 = ex2(fmaf(__uint_as_float(sr[c + 1]), sl2, neg_mb));
-                rs[c & 7] += e0;
-                rs[(c + 1) & 7] += e1;
-                pk[c >> 1] = Elem<T>::pack2(e0, e1);
+            for (int half = 0; half < 2; ++half) {  // 64 keys -> 32 packed columns at a time
+                uint32_t pk[32];
+#pragma unroll
+                for (int c2 = 0; c2 < 32; ++c2) {
+                    const int c = half * 64 + 2 * c2;
+                    const float e0 = ex2(fmaf(__uint_as_float(sr[c]), sl2, neg_mb));
+                    const float e1 = ex2(fmaf(__uint_as_float(sr[c + 1]), sl2, neg_mb));
+                    rs[c & 7] += e0;
+                    rs[(c + 1) & 7] += e1;
+                    pk[c2] = Elem<T>::pack2(e0, e1);
+                }
+                tmem_st32(tS + half * 32, pk);
             }
-            tmem_st32(tS, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
-            tmem_st32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
             const float rowsum = ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
 
             // O_t is idle here: PV_t(j-1) finished before S_t(j) was signalled.

@@ -9,9 +9,10 @@
 // read once and written once, everything else is < 2% of the bytes.  Layout
 // in HBM is the reference's [B][Hv][dv][dk] with dk innermost, so a state row
 // is 512 contiguous bytes = one warp x one float4 per lane: every load and
-// store is a fully coalesced 128-bit access.  One CTA of 8 warps owns one
-// (b, h); each warp owns 16 rows and issues all 16 row loads before the first
-// reduction, so 8 KiB per warp (64 KiB per CTA) is in flight.  Loads and
+// store is a fully coalesced 128-bit access.  One CTA of 8 warps owns half a
+// (b, h) (64 rows); each warp owns 8 rows and issues all 8 row loads before the
+// first reduction.  Small CTAs keep 64 warps resident per SM and make the last
+// partial wave short.  Loads and
 // stores use the streaming (evict-first) cache policy: a step touches each
 // state byte exactly once.
 #include "common.cuh"
@@ -23,7 +24,8 @@ namespace {
 __device__ int g_err_gdn_decode = 0;
 
 constexpr int kD = 128;           // dk = dv
-constexpr int kRowsPerWarp = 16;  // 8 warps x 16 rows = 128 rows per CTA
+constexpr int kRowsPerWarp = 8;   // 8 warps x 8 rows = 64 rows: half a (b, h) per CTA
+constexpr int kCtasPerHead = kD / (kRowsPerWarp * 8);
 constexpr int kThreads = 256;
 
 // Streaming 128-bit load / store.  asm volatile keeps the 16 row loads of a
@@ -64,13 +66,13 @@ __global__ void __launch_bounds__(kThreads) gdn_decode_kernel(
     const TIn* __restrict__ q, const TIn* __restrict__ k, const TIn* __restrict__ v,
     const float* __restrict__ g_log, const float* __restrict__ beta, float* __restrict__ state,
     TOut* __restrict__ o, int Hqk, int Hv, int head_map, float scale) {
-    const int bh = blockIdx.x;  // b * Hv + h
+    const int bh = blockIdx.x / kCtasPerHead;  // b * Hv + h
     const int b = bh / Hv;
     const int h = bh - b * Hv;
     const int hq = head_map == 0 ? h % Hqk : h / (Hv / Hqk);
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int row0 = warp * kRowsPerWarp;
+    const int row0 = (blockIdx.x % kCtasPerHead) * (kRowsPerWarp * 8) + warp * kRowsPerWarp;
 
     float* S = state + (size_t)bh * kD * kD + (size_t)row0 * kD + 4 * lane;
     float4 s[kRowsPerWarp];
@@ -107,7 +109,7 @@ template <typename TIn, typename TOut>
 int launch(const void* q, const void* k, const void* v, const float* g_log, const float* beta,
            float* state, void* o, int B, int Hqk, int Hv, int head_map, float scale,
            cudaStream_t st) {
-    gdn_decode_kernel<TIn, TOut><<<B * Hv, kThreads, 0, st>>>(
+    gdn_decode_kernel<TIn, TOut><<<B * Hv * kCtasPerHead, kThreads, 0, st>>>(
         static_cast<const TIn*>(q), static_cast<const TIn*>(k), static_cast<const TIn*>(v),
         g_log, beta, state, static_cast<TOut*>(o), Hqk, Hv, head_map, scale);
     count_launch(1);
