@@ -203,26 +203,29 @@ __global__ void __launch_bounds__(kThreads, 1)
             constexpr uint32_t kFmt = Elem<T>::kFmt;
             constexpr uint32_t idesc_qk = make_idesc(kFmt, BM, BN, false, false);
             constexpr uint32_t idesc_pv = make_idesc(kFmt, BM, D, false, true);
+            // Descriptors are built once; per K-step only the start-address field
+            // (bits 0-13, address >> 4) advances, by a plain 64-bit add.
+            const uint64_t dq0 = smem_desc(sQ, 16, 1024, kLayoutSW128);
+            const uint64_t dk0 = smem_desc(sK0, 16, 1024, kLayoutSW128);
+            const uint64_t dv0 = smem_desc(sV0, BN * 128, 1024, kLayoutSW128);
             auto qk = [&](int t, int j) {  // S_t = Q_t K_j^T
-                const uint32_t qa = sQ + t * L::kQTileBytes;
-                const uint32_t ka = sK0 + (j & 1) * L::kKVBytes;
+                const uint64_t qa = dq0 + ((t * L::kQTileBytes) >> 4);
+                const uint64_t ka = dk0 + (((j & 1) * L::kKVBytes) >> 4);
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
-                    const uint32_t o = (kk >> 2) * (BM * 128) + (kk & 3) * 32;
-                    mma_f16_ss(tmem + t * BN, smem_desc(qa + o, 16, 1024, kLayoutSW128),
-                               smem_desc(ka + o, 16, 1024, kLayoutSW128), idesc_qk, kk > 0 ? 1u : 0u);
+                    const uint32_t o = ((kk >> 2) * (BM * 128) + (kk & 3) * 32) >> 4;
+                    mma_f16_ss(tmem + t * BN, qa + o, ka + o, idesc_qk, kk > 0 ? 1u : 0u);
                 }
                 mma_commit(&bars->s_full[t]);
             };
             auto pv = [&](int t, int j) {  // O_t += P_t V_j, P from TMEM
-                const uint32_t va = sV0 + (j & 1) * L::kKVBytes;
+                // B = V tile [key][d], MN-major: 16 keys = two 8-row groups; 64-column
+                // boxes BN*128 bytes apart (the descriptor's leading byte offset).
+                const uint64_t va = dv0 + (((j & 1) * L::kKVBytes) >> 4);
 #pragma unroll
                 for (int kk = 0; kk < BN / 16; ++kk) {
-                    // B = V tile [key][d], MN-major: 16 keys = two 8-row groups; 64-column
-                    // boxes BN*128 bytes apart.
-                    mma_f16_ts(tmem + L::kTmemO + t * D, tmem + t * BN + kk * 8,
-                               smem_desc(va + kk * 16 * 128, BN * 128, 1024, kLayoutSW128), idesc_pv,
-                               (j > 0 || kk > 0) ? 1u : 0u);
+                    mma_f16_ts(tmem + L::kTmemO + t * D, tmem + t * BN + kk * 8, va + ((kk * 16 * 128) >> 4),
+                               idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
                 }
             };
             bool ok = mbar_wait(&bars->q_full, 0, abort, &g_err_attn);

@@ -19,7 +19,7 @@
 // Kernel 1, gdn_prep_kernel: one CTA per (b, v-head, chunk), fully parallel.
 //   TMA loads K, Q, V chunk tiles; ONE M=128 tcgen05 MMA gives [K;Q] K^T
 //   (lanes 0-63: K K^T, lanes 64-127: Q K^T); the threads form A and Aqk,
-//   invert (I + A) column-parallel in fp32, and two M=128, N=128 MMAs give
+//   invert (I + A) as a 2 x 2 block inverse in fp32, and two M=128, N=128 MMAs give
 //   [T diag(beta Gam); T diag(beta)] K -> W and [...] V -> U.
 //   W, U, Aqk (16-bit) and gcs (fp32) go to the workspace.
 // Kernel 2, gdn_state_kernel: one CTA per (b, v-head, 32-column slice of the
@@ -88,8 +88,10 @@ constexpr int kK0 = 0, kQ0 = 8192, kK1 = 16384, kQ1 = 24576, kV0 = 32768, kV1 = 
 constexpr int kAT = 49152;         // [T diag(beta Gam); T diag(beta)] 128 x 64, 16 KiB
 constexpr int kLd = 68;            // fp32 row pitch of A and T (16-byte aligned, fewer conflicts)
 constexpr int kAs = 65536;         // A, fp32 64 x kLd
-constexpr int kMisc = kAs + kC * kLd * 4;
-constexpr int kBytes = kMisc + 1024;
+constexpr int kTs = kAs + kC * kLd * 4;   // T = (I + A)^-1, fp32 64 x kLd
+constexpr int kXs = kTs + kC * kLd * 4;   // 32 x 36 fp32 scratch of the block inverse
+constexpr int kMisc = kXs + 32 * 36 * 4;
+constexpr int kBytes = kMisc + 2048;
 constexpr int kAlloc = kBytes + 1024;
 constexpr uint32_t kTmemCols = 256;
 
@@ -97,10 +99,12 @@ struct Misc {
     float gcs[kC];   // natural log units (stored to the workspace)
     float g2[kC];    // gcs * log2(e), for ex2
     float beta[kC];
+    float colscale[2 * kC];  // [beta Gam | beta], the column scales of T' and T''
     uint64_t bar_tma, bar_mma1, bar_mma2, drain;
     uint32_t tmem_base;
     int abort;
 };
+static_assert(sizeof(Misc) <= kBytes - kMisc, "prep Misc overflows its slot");
 }  // namespace prep
 
 __device__ __forceinline__ float ex2f(float x) {
@@ -109,51 +113,106 @@ __device__ __forceinline__ float ex2f(float x) {
     return y;
 }
 
-// Column j of T = (I + A)^-1 for a strictly lower 64 x 64 A (fp32, shared,
-// row pitch kLd), by forward substitution: T[t][j] = [t==j] - sum_{s<t} A[t][s] T[s][j].
-// Rows are processed in blocks of 8: the contributions of all earlier rows to
-// the 8 rows of a block are 8 independent dot-product chains (ILP), then the
-// 8 x 8 triangle of the block is resolved.  Every A read is a broadcast.
-__device__ __forceinline__ void inverse_column(const float* As, int j, float (&col)[kC]) {
+// T = (I + A)^-1 for a strictly lower 64 x 64 A (fp32, shared, row pitch kLd)
+// as a 2 x 2 block inverse of 32 x 32 blocks:
+//   T11 = (I + A11)^-1, T22 = (I + A22)^-1      (warp 0 / warp 1: one column per
+//                                                lane, forward substitution)
+//   T21 = -T22 (A21 T11),  T12 = 0              (all 128 threads, 8 outputs each)
+// Result in Ts (fp32, row pitch kLd); X (32 x 32) is scratch.
+__device__ __forceinline__ void lower_unit_inverse(const float* As, float* Ts, float* X, int tid) {
     using prep::kLd;
+    if (tid < 64) {
+        const int o = (tid >> 5) * 32;  // diagonal block origin
+        const int j = tid & 31;         // column within the block
+        float col[32];
 #pragma unroll
-    for (int b = 0; b < kC / 8; ++b) {
-        const int t0 = b * 8;
-        float acc[8];
+        for (int b = 0; b < 4; ++b) {   // rows in blocks of 8: 8 independent chains
+            const int t0 = b * 8;
+            float acc[8];
 #pragma unroll
-        for (int r = 0; r < 8; ++r) acc[r] = 0.f;
+            for (int r = 0; r < 8; ++r) acc[r] = 0.f;
 #pragma unroll
-        for (int s = 0; s < t0; s += 4) {
+            for (int s = 0; s < t0; s += 4) {
+#pragma unroll
+                for (int r = 0; r < 8; ++r) {
+                    const float4 a = *reinterpret_cast<const float4*>(As + (o + t0 + r) * kLd + o + s);
+                    acc[r] = fmaf(a.x, col[s], acc[r]);
+                    acc[r] = fmaf(a.y, col[s + 1], acc[r]);
+                    acc[r] = fmaf(a.z, col[s + 2], acc[r]);
+                    acc[r] = fmaf(a.w, col[s + 3], acc[r]);
+                }
+            }
 #pragma unroll
             for (int r = 0; r < 8; ++r) {
-                const float4 a = *reinterpret_cast<const float4*>(As + (t0 + r) * kLd + s);
-                acc[r] = fmaf(a.x, col[s], acc[r]);
-                acc[r] = fmaf(a.y, col[s + 1], acc[r]);
-                acc[r] = fmaf(a.z, col[s + 2], acc[r]);
-                acc[r] = fmaf(a.w, col[s + 3], acc[r]);
+                const int t = t0 + r;
+                float x = acc[r];
+#pragma unroll
+                for (int s = 0; s < r; ++s) x = fmaf(As[(o + t) * kLd + o + t0 + s], col[t0 + s], x);
+                col[t] = t < j ? 0.f : (t == j ? 1.f : -x);
             }
         }
 #pragma unroll
-        for (int r = 0; r < 8; ++r) {
-            const int t = t0 + r;
-            float x = acc[r];
+        for (int t = 0; t < 32; ++t) Ts[(o + t) * kLd + o + j] = col[t];
+        if (o == 0) {
 #pragma unroll
-            for (int s = 0; s < r; ++s) x = fmaf(As[t * kLd + t0 + s], col[t0 + s], x);
-            col[t] = t < j ? 0.f : (t == j ? 1.f : -x);
+            for (int t = 0; t < 32; ++t) Ts[t * kLd + 32 + j] = 0.f;  // T12 = 0
         }
     }
+    __syncthreads();
+    // 128 threads x 8 outputs: row r = tid / 4, columns c0 .. c0 + 7 with c0 = (tid % 4) * 8
+    const int r = tid >> 2, c0 = (tid & 3) * 8;
+    {   // X = A21 T11
+        float acc[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) acc[u] = 0.f;
+#pragma unroll
+        for (int s = 0; s < 32; ++s) {
+            const float a = As[(32 + r) * kLd + s];
+            const float4 t0 = *reinterpret_cast<const float4*>(Ts + s * kLd + c0);
+            const float4 t1 = *reinterpret_cast<const float4*>(Ts + s * kLd + c0 + 4);
+            acc[0] = fmaf(a, t0.x, acc[0]); acc[1] = fmaf(a, t0.y, acc[1]);
+            acc[2] = fmaf(a, t0.z, acc[2]); acc[3] = fmaf(a, t0.w, acc[3]);
+            acc[4] = fmaf(a, t1.x, acc[4]); acc[5] = fmaf(a, t1.y, acc[5]);
+            acc[6] = fmaf(a, t1.z, acc[6]); acc[7] = fmaf(a, t1.w, acc[7]);
+        }
+        *reinterpret_cast<float4*>(X + r * 36 + c0) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        *reinterpret_cast<float4*>(X + r * 36 + c0 + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    }
+    __syncthreads();
+    {   // T21 = -T22 X
+        float acc[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) acc[u] = 0.f;
+#pragma unroll
+        for (int s = 0; s < 32; ++s) {
+            const float a = Ts[(32 + r) * kLd + 32 + s];
+            const float4 x0 = *reinterpret_cast<const float4*>(X + s * 36 + c0);
+            const float4 x1 = *reinterpret_cast<const float4*>(X + s * 36 + c0 + 4);
+            acc[0] = fmaf(a, x0.x, acc[0]); acc[1] = fmaf(a, x0.y, acc[1]);
+            acc[2] = fmaf(a, x0.z, acc[2]); acc[3] = fmaf(a, x0.w, acc[3]);
+            acc[4] = fmaf(a, x1.x, acc[4]); acc[5] = fmaf(a, x1.y, acc[5]);
+            acc[6] = fmaf(a, x1.z, acc[6]); acc[7] = fmaf(a, x1.w, acc[7]);
+        }
+        *reinterpret_cast<float4*>(Ts + (32 + r) * kLd + c0) = make_float4(-acc[0], -acc[1], -acc[2], -acc[3]);
+        *reinterpret_cast<float4*>(Ts + (32 + r) * kLd + c0 + 4) = make_float4(-acc[4], -acc[5], -acc[6], -acc[7]);
+    }
+    __syncthreads();
 }
 
 template <typename T16>
 __global__ void __launch_bounds__(prep::kThreads, 2)
     gdn_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                    const __grid_constant__ CUtensorMap tmV, const PrepParams p) {
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmW,
+                    const __grid_constant__ CUtensorMap tmU, const __grid_constant__ CUtensorMap tmAqk,
+                    const PrepParams p) {
     using namespace prep;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     Misc* ms = reinterpret_cast<Misc*>(smem + kMisc);
     float* As = reinterpret_cast<float*>(smem + kAs);
+    float* Ts = reinterpret_cast<float*>(smem + kTs);
+    float* Xs = reinterpret_cast<float*>(smem + kXs);
     volatile int* abort = &ms->abort;
 
     const int c = blockIdx.x;   // chunk
@@ -260,8 +319,9 @@ __global__ void __launch_bounds__(prep::kThreads, 2)
                 *reinterpret_cast<float4*>(As + row * kLd + s) = a;
             }
         } else {
-            // Aqk row (lower incl. diagonal), 16-bit, straight to the workspace
-            T16* dst = reinterpret_cast<T16*>(p.ws + p.ws_aqk) + bhc * kC * kC + row * kC;
+            // Aqk row (lower incl. diagonal), 16-bit, staged 128B-swizzled in the (not yet
+            // used) AT tile and written to the workspace by one TMA store
+            uint8_t* stg = smem + kAT + row * 128;
 #pragma unroll
             for (int s = 0; s < kC; s += 8) {
                 uint4 pk;
@@ -273,24 +333,43 @@ __global__ void __launch_bounds__(prep::kThreads, 2)
                     const float a1 = s1 <= row ? __uint_as_float(v[s1]) * ex2f(g2_r - ms->g2[s1]) : 0.f;
                     pw[u] = Elem<T16>::pack2(a0, a1);
                 }
-                *reinterpret_cast<uint4*>(dst + s) = pk;
+                *reinterpret_cast<uint4*>(stg + (((s >> 3) ^ (row & 7)) << 4)) = pk;
             }
+            fence_proxy_async_smem();
         }
     }
     __syncthreads();
+    if (tid == 64 && ok) {
+        tma_store_3d(&tmAqk, smem + kAT, 0, 0, (int)bhc);
+        bulk_commit();
+        bulk_wait_read();  // the AT tile is rewritten after the solve
+    }
 
-    if (tid < kC) {
-        // thread j: column j of T, scaled into rows 0-63 (T diag(beta Gam)) and 64-127 (T diag(beta))
-        const int j = tid;
-        float col[kC];
-        inverse_column(As, j, col);
-        const float bj = ms->beta[j];
-        const float bgj = bj * ex2f(ms->g2[j]);
-        uint8_t* at = smem + kAT;
+    {
+        const int j = tid & 63;
+        ms->colscale[tid] = tid < kC ? ms->beta[j] * ex2f(ms->g2[j]) : ms->beta[j];
+    }
+    lower_unit_inverse(As, Ts, Xs, tid);  // contains __syncthreads: every thread calls it
+    {
+        // AT rows 0-63 <- T diag(beta Gam), rows 64-127 <- T diag(beta). Thread = AT row:
+        // eight 16-byte swizzled chunks of 8 columns each (conflict-free row reads of Ts,
+        // broadcast reads of the column scales)
+        const int r = tid;
+        const float* trow = Ts + (r & (kC - 1)) * kLd;
+        const float* sc = ms->colscale + (r < kC ? 0 : kC);
+        uint8_t* at = smem + kAT + r * 128;
 #pragma unroll
-        for (int t = 0; t < kC; ++t) {
-            *reinterpret_cast<T16*>(at + sw128_off(t, j)) = Elem<T16>::from_f(col[t] * bgj);
-            *reinterpret_cast<T16*>(at + sw128_off(kC + t, j)) = Elem<T16>::from_f(col[t] * bj);
+        for (int c8 = 0; c8 < 8; ++c8) {
+            const float4 a = *reinterpret_cast<const float4*>(trow + c8 * 8);
+            const float4 b = *reinterpret_cast<const float4*>(trow + c8 * 8 + 4);
+            const float4 sa = *reinterpret_cast<const float4*>(sc + c8 * 8);
+            const float4 sb = *reinterpret_cast<const float4*>(sc + c8 * 8 + 4);
+            uint4 pk;
+            pk.x = Elem<T16>::pack2(a.x * sa.x, a.y * sa.y);
+            pk.y = Elem<T16>::pack2(a.z * sa.z, a.w * sa.w);
+            pk.z = Elem<T16>::pack2(b.x * sb.x, b.y * sb.y);
+            pk.w = Elem<T16>::pack2(b.z * sb.z, b.w * sb.w);
+            *reinterpret_cast<uint4*>(at + ((c8 ^ (r & 7)) << 4)) = pk;
         }
     }
     fence_proxy_async_smem();
@@ -317,9 +396,11 @@ __global__ void __launch_bounds__(prep::kThreads, 2)
     ok = __all_sync(0xffffffffu, mbar_wait(&ms->bar_mma2, 0, abort, &g_err_gdn_prefill)) && ok;
     tc_fence_after();
     if (ok) {
-        // warps 0-1: W rows (lanes 0-63, cols 0-127); warps 2-3: U rows (lanes 64-127, cols 128-255)
+        // warps 0-1: W rows (lanes 0-63, cols 0-127); warps 2-3: U rows (lanes 64-127,
+        // cols 128-255), staged 128B-swizzled over the dead K/Q/V tiles (W at 0, U at 16 KiB,
+        // two 64-column boxes each) for TMA stores
         const uint32_t col0 = warp < 2 ? 0u : 128u;
-        T16* dst = reinterpret_cast<T16*>(p.ws + (warp < 2 ? 0 : p.ws_u)) + bhc * kC * kD + row * kD;
+        uint8_t* stg = smem + kTiles + (warp < 2 ? 0 : 16384) + row * 128;
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc) {
             uint32_t v[32];
@@ -332,11 +413,22 @@ __global__ void __launch_bounds__(prep::kThreads, 2)
                 pk.y = Elem<T16>::pack2(__uint_as_float(v[q8 * 8 + 2]), __uint_as_float(v[q8 * 8 + 3]));
                 pk.z = Elem<T16>::pack2(__uint_as_float(v[q8 * 8 + 4]), __uint_as_float(v[q8 * 8 + 5]));
                 pk.w = Elem<T16>::pack2(__uint_as_float(v[q8 * 8 + 6]), __uint_as_float(v[q8 * 8 + 7]));
-                *reinterpret_cast<uint4*>(dst + cc * 32 + q8 * 8) = pk;
+                const int q = cc * 4 + q8;  // 16-byte chunk 0..15 of the 256-byte row
+                *reinterpret_cast<uint4*>(stg + (q >> 3) * 8192 + (((q & 7) ^ (row & 7)) << 4)) = pk;
             }
         }
+        fence_proxy_async_smem();
         if (warp < 2)
             reinterpret_cast<float*>(p.ws + p.ws_gcs)[bhc * kC + row] = gcs_r;
+    }
+    __syncthreads();
+    if (tid == 0 && ok) {
+        tma_store_3d(&tmW, smem + kTiles, 0, 0, (int)bhc);
+        tma_store_3d(&tmW, smem + kTiles + 8192, 64, 0, (int)bhc);
+        tma_store_3d(&tmU, smem + kTiles + 16384, 0, 0, (int)bhc);
+        tma_store_3d(&tmU, smem + kTiles + 24576, 64, 0, (int)bhc);
+        bulk_commit();
+        bulk_wait_all();
     }
     if (tid == 0) {
         mma_commit(&ms->drain);
@@ -483,22 +575,25 @@ __global__ void __launch_bounds__(st::kThreads, 1)
             constexpr uint32_t kFmt = Elem<T16>::kFmt;
             constexpr uint32_t id_k = make_idesc(kFmt, 128, kSlice, false, false);   // both K-major
             constexpr uint32_t id_mn = make_idesc(kFmt, 128, kSlice, true, false);   // A MN-major
-            const uint32_t sS = smem_u32(smem + kSt);
-            const uint32_t sVn = smem_u32(smem + kVn);
-            const uint32_t sVt = smem_u32(smem + kVt);
+            // Descriptors built once; per K-step only the address field advances.
+            const uint64_t dS = smem_desc(smem_u32(smem + kSt), 16, 1024, kLayoutSW128);
+            const uint64_t dVn = smem_desc(smem_u32(smem + kVn), 16, 1024, kLayoutSW128);
+            const uint64_t dVt = smem_desc(smem_u32(smem + kVt), 16, 1024, kLayoutSW128);
+            const uint64_t dA1 = smem_desc(smem_u32(smem + kA1), 16, 1024, kLayoutSW128);
+            const uint64_t dZ = smem_desc(smem_u32(smem + kZero), 16, 1024, kLayoutSW128);
+            const uint64_t dK = smem_desc(smem_u32(smem + kKt), 8192, 1024, kLayoutSW128);
             for (int c = 0; c < p.nch; ++c) {
                 const int s = c & 1;
-                const uint32_t stg = smem_u32(smem + s * kStage);
+                const uint32_t so = (s * kStage) >> 4;
                 if (!mbar_wait(&ms->full[s], (c >> 1) & 1, abort, &g_err_gdn_prefill)) break;
                 if (!mbar_wait(&ms->s_ready, c & 1, abort, &g_err_gdn_prefill)) break;
                 tc_fence_after();
                 // MMA1: [W;Q] S^T
 #pragma unroll
                 for (int kk = 0; kk < kD / 16; ++kk) {
-                    const uint32_t ao = (kk >> 2) * 16384 + (kk & 3) * 32;
-                    const uint32_t bo = (kk >> 2) * 4096 + (kk & 3) * 32;
-                    mma_f16_ss(tmem + kColP, smem_desc(stg + kA1 + ao, 16, 1024, kLayoutSW128),
-                               smem_desc(sS + bo, 16, 1024, kLayoutSW128), id_k, kk > 0 ? 1u : 0u);
+                    const uint32_t ao = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
+                    const uint32_t bo = ((kk >> 2) * 4096 + (kk & 3) * 32) >> 4;
+                    mma_f16_ss(tmem + kColP, dA1 + so + ao, dS + bo, id_k, kk > 0 ? 1u : 0u);
                 }
                 mma_commit(&ms->p_full);
                 if (!mbar_wait(&ms->v_ready, c & 1, abort, &g_err_gdn_prefill)) break;
@@ -506,11 +601,11 @@ __global__ void __launch_bounds__(st::kThreads, 1)
 #pragma unroll
                 for (int kk = 0; kk < kC / 16; ++kk) {
                     // MMA2: [0;Aqk] Vn  -> intra-chunk outputs in lanes 64-127
-                    mma_f16_ss(tmem + kColOI, smem_desc(stg + kZero + kk * 32, 16, 1024, kLayoutSW128),
-                               smem_desc(sVn + kk * 32, 16, 1024, kLayoutSW128), id_k, kk > 0 ? 1u : 0u);
+                    mma_f16_ss(tmem + kColOI, dZ + so + ((kk * 32) >> 4), dVn + ((kk * 32) >> 4), id_k,
+                               kk > 0 ? 1u : 0u);
                     // MMA3: K^T (decayed Vn) -> state increment, lane = key index
-                    mma_f16_ss(tmem + kColDS, smem_desc(stg + kKt + kk * 2048, 8192, 1024, kLayoutSW128),
-                               smem_desc(sVt + kk * 32, 16, 1024, kLayoutSW128), id_mn, kk > 0 ? 1u : 0u);
+                    mma_f16_ss(tmem + kColDS, dK + so + ((kk * 2048) >> 4), dVt + ((kk * 32) >> 4), id_mn,
+                               kk > 0 ? 1u : 0u);
                 }
                 mma_commit(&ms->o_full);
                 mma_commit(&ms->empty[s]);
@@ -648,6 +743,8 @@ int launch(const void* q, const void* k, const void* v, const float* g_log, cons
     uint8_t* wsb = static_cast<uint8_t*>(ws);
     if ((rc = make_tmap_3d(&tw, wsb + L.w, dt, 2, kD, kC, nbhc, 64, kC, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
     if ((rc = make_tmap_3d(&ta, wsb + L.aqk, dt, 2, kC, kC, nbhc, 64, kC, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
+    CUtensorMap tu;
+    if ((rc = make_tmap_3d(&tu, wsb + L.u, dt, 2, kD, kC, nbhc, 64, kC, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
 
     PrepParams pp;
     pp.ws = wsb;
@@ -663,7 +760,7 @@ int launch(const void* q, const void* k, const void* v, const float* g_log, cons
     pp.head_map = head_map;
     auto k1 = gdn_prep_kernel<T16>;
     B200_TRY_CUDA(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, prep::kAlloc));
-    k1<<<dim3(nch, Hv, B), prep::kThreads, prep::kAlloc, stream>>>(tq, tk, tv, pp);
+    k1<<<dim3(nch, Hv, B), prep::kThreads, prep::kAlloc, stream>>>(tq, tk, tv, tw, tu, ta, pp);
     B200_TRY_CUDA(cudaGetLastError());
 
     StateParams sp;
