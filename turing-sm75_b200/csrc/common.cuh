@@ -121,8 +121,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 }
 
 // ---- TMA -----------------------------------------------------------------
+// Untiled bulk copy global -> this CTA's shared memory (16-byte aligned, size a
+// multiple of 16), completion signalled on `bar`.  No cluster multicast.
+__device__ __forceinline__ void bulk_load_1d(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
 // 3-D tiled bulk tensor load into this CTA's shared memory, completion
 // signalled on `bar` through its transaction count.  No cluster multicast.
+
 __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
                                             int c0, int c1, int c2) {
     asm volatile(
@@ -196,7 +207,7 @@ __device__ __forceinline__ void tc_fence_after() {
 // ---- tcgen05: descriptors ------------------------------------------------
 // Shared-memory matrix descriptor (sm_100 format): start address, leading and
 // stride byte offsets (all >>4), version 1, layout type in bits 61..63.
-enum : uint32_t { kLayoutSW128 = 2, kLayoutNone = 0 };
+enum : uint32_t { kLayoutSW128 = 2, kLayoutSW64 = 4, kLayoutNone = 0 };
 
 __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes,
                                               uint32_t layout) {

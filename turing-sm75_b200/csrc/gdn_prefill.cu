@@ -93,6 +93,7 @@ constexpr int kXs = kTs + kC * kLd * 4;   // 32 x 36 fp32 scratch of the block i
 constexpr int kMisc = kXs + 32 * 36 * 4;
 constexpr int kBytes = kMisc + 2048;
 constexpr int kAlloc = kBytes + 1024;
+static_assert(kAlloc <= 232448, "state kernel shared memory above the 227 KiB per-CTA limit");
 constexpr uint32_t kTmemCols = 256;
 
 struct Misc {
@@ -448,26 +449,38 @@ __global__ void __launch_bounds__(prep::kThreads, 2)
 namespace st {
 constexpr int kThreads = 192;  // warps 0-3 compute, 4 TMA producer, 5 MMA issuer
 constexpr int kWarpProducer = 4, kWarpMma = 5;
-// one stage of chunk inputs (64 KiB):
-//   [W0|Q0|W1|Q1] A1 tile 32 KiB; [K0|K1] 16 KiB; [zero|Aqk] 16 KiB
-constexpr int kStage = 65536;
-constexpr int kA1 = 0, kKt = 32768, kZero = 49152, kAqk = 57344;
-constexpr int kStages = 2;
-constexpr int kSt = kStages * kStage;    // S tile: 32 rows (v) x 128 (k), 16-bit, 8 KiB
-constexpr int kVn = kSt + 8192;          // Vn^T tile 32 x 64, 4 KiB
-constexpr int kVt = kVn + 4096;          // decayed Vn^T tile, 4 KiB
+// one stage of chunk inputs (69 KiB):
+//   [W0|Q0|W1|Q1] A1 tile 32 KiB; [K0|K1] 16 KiB; [zero|Aqk] 16 KiB;
+//   this CTA's 32 columns of U (64-byte swizzle) 4 KiB; gcs 256 B
+// Three stages: global/TMA latency under this load is about two chunk periods.
+constexpr int kStage = 70656;
+constexpr int kA1 = 0, kKt = 32768, kZero = 49152, kAqk = 57344, kU = 65536, kG = 69632;
+constexpr int kStageTx = 7 * 8192 + 4096 + kC * 4;
+constexpr int kStages = 3;
+// B operands of the chain, MN-major with 64-byte swizzle: one 64-byte row (32 state
+// columns, 16-bit) per K index, so each thread writes its row as four 16-byte chunks
+constexpr int kSt = kStages * kStage;    // S^T tile: 128 keys x 32 v, 8 KiB
+constexpr int kVn = kSt + 8192;          // Vn tile: 64 tokens x 32 v, 4 KiB
+constexpr int kVt = kVn + 4096;          // decayed Vn tile, 4 KiB
 constexpr int kMisc = kVt + 4096;
 constexpr int kBytes = kMisc + 256;
 constexpr int kAlloc = kBytes + 1024;
-constexpr uint32_t kTmemCols = 128;
-constexpr uint32_t kColP = 0, kColOI = 32, kColDS = 64;
+constexpr uint32_t kTmemCols = 256;
+// P ([W;Q] S^T) and OI ([0;Aqk] Vn) alternate between two buffers by chunk parity so
+// the output warps may read chunk c while the chain already runs chunk c+1
+constexpr uint32_t kColP = 0, kColOI = 64, kColDS = 128;
 
 struct Misc {
     uint64_t full[kStages], empty[kStages];
-    uint64_t s_ready, p_full, v_ready, o_full, drain;
+    uint64_t s_ready, p_full, v_ready, ds_full, o_full[2], drain;
     uint32_t tmem_base;
     int abort;
 };
+
+// byte offset of 16-byte chunk q (columns 8q..8q+7) of row r in a 64-byte-swizzled tile
+__device__ __forceinline__ uint32_t sw64_chunk(int r, int q) {
+    return (uint32_t)(r * 64 + ((q ^ ((r >> 1) & 3)) << 4));
+}
 }  // namespace st
 
 struct StateParams {
@@ -503,7 +516,7 @@ template <typename T16, typename TOut>
 __global__ void __launch_bounds__(st::kThreads, 1)
     gdn_state_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmAqk,
-                     const StateParams p) {
+                     const __grid_constant__ CUtensorMap tmU, const StateParams p) {
     using namespace st;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -528,7 +541,9 @@ __global__ void __launch_bounds__(st::kThreads, 1)
         mbar_init(&ms->s_ready, 128);
         mbar_init(&ms->p_full, 1);
         mbar_init(&ms->v_ready, 64);
-        mbar_init(&ms->o_full, 1);
+        mbar_init(&ms->ds_full, 1);
+        mbar_init(&ms->o_full[0], 1);
+        mbar_init(&ms->o_full[1], 1);
         mbar_init(&ms->drain, 1);
         ms->abort = 0;
         fence_barrier_init();
@@ -551,13 +566,16 @@ __global__ void __launch_bounds__(st::kThreads, 1)
     if (warp == kWarpProducer) {
         if (lane == 0) {
             int issued = 0;
+            const float* gcs_all = reinterpret_cast<const float*>(p.ws + p.ws_gcs);
             for (int c = 0; c < p.nch; ++c) {
-                const int s = c & 1;
-                if (!mbar_wait(&ms->empty[s], ((c >> 1) & 1) ^ 1, abort, &g_err_gdn_prefill)) break;
+                const int s = c % kStages;
+                if (!mbar_wait(&ms->empty[s], ((c / kStages) & 1) ^ 1, abort, &g_err_gdn_prefill)) break;
                 uint8_t* stg = smem + s * kStage;
                 uint64_t* bar = &ms->full[s];
                 const int bhc = (int)(bh * p.nch + c);
-                mbar_arrive_expect_tx(bar, 7 * 8192);
+                mbar_arrive_expect_tx(bar, kStageTx);
+                tma_load_3d(stg + kU, &tmU, bar, c0, 0, bhc);
+                bulk_load_1d(stg + kG, gcs_all + (size_t)bhc * kC, kC * 4, bar);
                 tma_load_3d(stg + kA1 + 0, &tmW, bar, 0, 0, bhc);
                 tma_load_3d(stg + kA1 + 16384, &tmW, bar, 64, 0, bhc);
                 tma_load_4d(stg + kA1 + 8192, &tmQ, bar, 0, hq, c * kC, b);
@@ -567,47 +585,52 @@ __global__ void __launch_bounds__(st::kThreads, 1)
                 tma_load_3d(stg + kAqk, &tmAqk, bar, 0, 0, bhc);
                 issued = c + 1;
             }
-            for (int c = max(0, issued - 2); c < issued; ++c)
-                mbar_wait(&ms->full[c & 1], (c >> 1) & 1, abort, &g_err_gdn_prefill);
+            for (int c = max(0, issued - kStages); c < issued; ++c)
+                mbar_wait(&ms->full[c % kStages], (c / kStages) & 1, abort, &g_err_gdn_prefill);
         }
     } else if (warp == kWarpMma) {
         if (lane == 0) {
             constexpr uint32_t kFmt = Elem<T16>::kFmt;
-            constexpr uint32_t id_k = make_idesc(kFmt, 128, kSlice, false, false);   // both K-major
-            constexpr uint32_t id_mn = make_idesc(kFmt, 128, kSlice, true, false);   // A MN-major
-            // Descriptors built once; per K-step only the address field advances.
-            const uint64_t dS = smem_desc(smem_u32(smem + kSt), 16, 1024, kLayoutSW128);
-            const uint64_t dVn = smem_desc(smem_u32(smem + kVn), 16, 1024, kLayoutSW128);
-            const uint64_t dVt = smem_desc(smem_u32(smem + kVt), 16, 1024, kLayoutSW128);
+            constexpr uint32_t id_kb = make_idesc(kFmt, 128, kSlice, false, true);   // A K-major, B MN
+            constexpr uint32_t id_mn = make_idesc(kFmt, 128, kSlice, true, true);    // both MN-major
+            // Descriptors built once; per K-step only the address field advances. The
+            // MN-major B tiles: SBO = 512 (8 K rows of 64 B), one 32-column MN block.
+            const uint64_t dS = smem_desc(smem_u32(smem + kSt), 8192, 512, kLayoutSW64);
+            const uint64_t dVn = smem_desc(smem_u32(smem + kVn), 4096, 512, kLayoutSW64);
+            const uint64_t dVt = smem_desc(smem_u32(smem + kVt), 4096, 512, kLayoutSW64);
             const uint64_t dA1 = smem_desc(smem_u32(smem + kA1), 16, 1024, kLayoutSW128);
             const uint64_t dZ = smem_desc(smem_u32(smem + kZero), 16, 1024, kLayoutSW128);
             const uint64_t dK = smem_desc(smem_u32(smem + kKt), 8192, 1024, kLayoutSW128);
             for (int c = 0; c < p.nch; ++c) {
-                const int s = c & 1;
+                const int s = c % kStages;
                 const uint32_t so = (s * kStage) >> 4;
-                if (!mbar_wait(&ms->full[s], (c >> 1) & 1, abort, &g_err_gdn_prefill)) break;
+                if (!mbar_wait(&ms->full[s], (c / kStages) & 1, abort, &g_err_gdn_prefill)) break;
                 if (!mbar_wait(&ms->s_ready, c & 1, abort, &g_err_gdn_prefill)) break;
                 tc_fence_after();
+                const uint32_t buf = (c & 1) * 32;
                 // MMA1: [W;Q] S^T
 #pragma unroll
                 for (int kk = 0; kk < kD / 16; ++kk) {
                     const uint32_t ao = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
-                    const uint32_t bo = ((kk >> 2) * 4096 + (kk & 3) * 32) >> 4;
-                    mma_f16_ss(tmem + kColP, dA1 + so + ao, dS + bo, id_k, kk > 0 ? 1u : 0u);
+                    mma_f16_ss(tmem + kColP + buf, dA1 + so + ao, dS + ((kk * 1024) >> 4), id_kb,
+                               kk > 0 ? 1u : 0u);
                 }
                 mma_commit(&ms->p_full);
                 if (!mbar_wait(&ms->v_ready, c & 1, abort, &g_err_gdn_prefill)) break;
                 tc_fence_after();
+                // MMA3 first (it closes the chain): K^T (decayed Vn) -> state increment,
+                // lane = key index
 #pragma unroll
-                for (int kk = 0; kk < kC / 16; ++kk) {
-                    // MMA2: [0;Aqk] Vn  -> intra-chunk outputs in lanes 64-127
-                    mma_f16_ss(tmem + kColOI, dZ + so + ((kk * 32) >> 4), dVn + ((kk * 32) >> 4), id_k,
+                for (int kk = 0; kk < kC / 16; ++kk)
+                    mma_f16_ss(tmem + kColDS, dK + so + ((kk * 2048) >> 4), dVt + ((kk * 1024) >> 4), id_mn,
                                kk > 0 ? 1u : 0u);
-                    // MMA3: K^T (decayed Vn) -> state increment, lane = key index
-                    mma_f16_ss(tmem + kColDS, dK + so + ((kk * 2048) >> 4), dVt + ((kk * 32) >> 4), id_mn,
+                mma_commit(&ms->ds_full);
+                // MMA2: [0;Aqk] Vn -> intra-chunk outputs in lanes 64-127
+#pragma unroll
+                for (int kk = 0; kk < kC / 16; ++kk)
+                    mma_f16_ss(tmem + kColOI + buf, dZ + so + ((kk * 32) >> 4), dVn + ((kk * 1024) >> 4), id_kb,
                                kk > 0 ? 1u : 0u);
-                }
-                mma_commit(&ms->o_full);
+                mma_commit(&ms->o_full[c & 1]);
                 mma_commit(&ms->empty[s]);
             }
             mma_commit(&ms->drain);
@@ -622,8 +645,6 @@ __global__ void __launch_bounds__(st::kThreads, 1)
         float* Sg = p.state + (bh * kD + c0) * kD + i;
 #pragma unroll
         for (int cc = 0; cc < kSlice; ++cc) S[cc] = Sg[(size_t)cc * kD];
-        const float* gcs_all = reinterpret_cast<const float*>(p.ws + p.ws_gcs);
-        const T16* U_all = reinterpret_cast<const T16*>(p.ws + p.ws_u);
         uint8_t* sS = smem + kSt;
         uint8_t* sVn = smem + kVn;
         uint8_t* sVt = smem + kVt;
@@ -631,33 +652,58 @@ __global__ void __launch_bounds__(st::kThreads, 1)
         // chunk ahead so their latency hides behind the previous chunk
         uint4 u_nx[kSlice / 8] = {};
         float gcs_nx = 0.f, glast_nx = 0.f;
-        auto prefetch = [&](int c) {
-            const size_t bhc = bh * p.nch + c;
-            gcs_nx = gcs_all[bhc * kC + row];
-            glast_nx = gcs_all[bhc * kC + kC - 1];
+        // Reads chunk c's U row and gates out of its stage. Called one chunk ahead, before
+        // this thread's s_ready arrival that the chunk's last MMA (and so the stage's
+        // release to the producer) depends on.
+        auto prefetch = [&](int c) -> bool {
+            const int s = c % kStages;
+            if (!mbar_wait(&ms->full[s], (c / kStages) & 1, abort, &g_err_gdn_prefill)) return false;
+            const uint8_t* stg = smem + s * kStage;
+            const float* G = reinterpret_cast<const float*>(stg + kG);
+            gcs_nx = G[row];
+            glast_nx = G[kC - 1];
             if (warp < 2) {
-                const uint4* up = reinterpret_cast<const uint4*>(U_all + (bhc * kC + row) * kD + c0);
 #pragma unroll
-                for (int q8 = 0; q8 < kSlice / 8; ++q8) u_nx[q8] = up[q8];
+                for (int q8 = 0; q8 < kSlice / 8; ++q8)
+                    u_nx[q8] = *reinterpret_cast<const uint4*>(stg + kU + sw64_chunk(row, q8));
+            }
+            return true;
+        };
+        // 32 values -> one 64-byte row of an MN-major B tile (16-bit)
+        auto put_row = [&](uint8_t* tile, int r, const float* x) {
+#pragma unroll
+            for (int q = 0; q < kSlice / 8; ++q) {
+                uint4 pk;
+                pk.x = Elem<T16>::pack2(x[8 * q + 0], x[8 * q + 1]);
+                pk.y = Elem<T16>::pack2(x[8 * q + 2], x[8 * q + 3]);
+                pk.z = Elem<T16>::pack2(x[8 * q + 4], x[8 * q + 5]);
+                pk.w = Elem<T16>::pack2(x[8 * q + 6], x[8 * q + 7]);
+                *reinterpret_cast<uint4*>(tile + sw64_chunk(r, q)) = pk;
             }
         };
-        if (p.nch > 0) prefetch(0);
-        bool ok = true;
-        for (int c = 0; c < p.nch && ok; ++c) {
-            const float gcs_t = gcs_nx;
-            const float g_last = glast_nx;
-            uint4 u_raw[kSlice / 8];
-#pragma unroll
-            for (int q8 = 0; q8 < kSlice / 8; ++q8) u_raw[q8] = u_nx[q8];
-            if (c + 1 < p.nch) prefetch(c + 1);
-            // S (16-bit) -> shared, B operand of MMA1: row = v column cc, col = key i
-#pragma unroll
-            for (int cc = 0; cc < kSlice; ++cc)
-                *reinterpret_cast<T16*>(sS + (i >> 6) * 4096 + sw128_off(cc, i & 63)) =
-                    Elem<T16>::from_f(S[cc]);
+        // S (16-bit) -> shared, B operand of MMA1: K index = key i, 32 v columns
+        auto publish_S = [&]() {
+            put_row(sS, i, S);
             fence_proxy_async_smem();
             tc_fence_before();
             mbar_arrive(&ms->s_ready);
+        };
+        bool ok = true;
+        if (p.nch > 0) {
+            ok = __all_sync(0xffffffffu, prefetch(0));
+            publish_S();
+        }
+        for (int c = 0; c < p.nch && ok; ++c) {
+            const float gcs_t = gcs_nx;
+            const float g_last = glast_nx;
+            const uint32_t buf = (c & 1) * 32;
+            uint4 u_raw[kSlice / 8];
+#pragma unroll
+            for (int q8 = 0; q8 < kSlice / 8; ++q8) u_raw[q8] = u_nx[q8];
+            if (c + 1 < p.nch && !__all_sync(0xffffffffu, prefetch(c + 1))) {
+                ok = false;
+                break;
+            }
 
             if (warp < 2) {
                 float u[kSlice];
@@ -671,26 +717,42 @@ __global__ void __launch_bounds__(st::kThreads, 1)
                 if (!ok) break;
                 tc_fence_after();
                 uint32_t pr[32];
-                tmem_ld32(tmem + lane_base + kColP, pr);
+                tmem_ld32(tmem + lane_base + kColP + buf, pr);
                 tmem_ld_wait();
                 const float dec = __expf(g_last - gcs_t);
+                float vt[kSlice];
 #pragma unroll
                 for (int cc = 0; cc < kSlice; ++cc) {
-                    const float vn = u[cc] - __uint_as_float(pr[cc]);
-                    *reinterpret_cast<T16*>(sVn + sw128_off(cc, row)) = Elem<T16>::from_f(vn);
-                    *reinterpret_cast<T16*>(sVt + sw128_off(cc, row)) = Elem<T16>::from_f(vn * dec);
+                    u[cc] -= __uint_as_float(pr[cc]);
+                    vt[cc] = u[cc] * dec;
                 }
+                put_row(sVn, row, u);
+                put_row(sVt, row, vt);
                 fence_proxy_async_smem();
                 tc_fence_before();
                 mbar_arrive(&ms->v_ready);
             }
-            ok = __all_sync(0xffffffffu, mbar_wait(&ms->o_full, c & 1, abort, &g_err_gdn_prefill));
+            // close the chain first: S <- gamma S + K^T Vt, then hand S(c+1) to the MMA warp
+            ok = __all_sync(0xffffffffu, mbar_wait(&ms->ds_full, c & 1, abort, &g_err_gdn_prefill));
             if (!ok) break;
             tc_fence_after();
+            {
+                uint32_t ds[32];
+                tmem_ld32(tmem + lane_base + kColDS, ds);
+                tmem_ld_wait();
+                const float gam = __expf(g_last);
+#pragma unroll
+                for (int cc = 0; cc < kSlice; ++cc) S[cc] = fmaf(gam, S[cc], __uint_as_float(ds[cc]));
+            }
+            if (c + 1 < p.nch) publish_S();
             if (warp >= 2) {
+                ok = __all_sync(0xffffffffu,
+                                mbar_wait(&ms->o_full[c & 1], (c >> 1) & 1, abort, &g_err_gdn_prefill));
+                if (!ok) break;
+                tc_fence_after();
                 uint32_t pq[32], oi[32];
-                tmem_ld32(tmem + lane_base + kColP, pq);
-                tmem_ld32(tmem + lane_base + kColOI, oi);
+                tmem_ld32(tmem + lane_base + kColP + buf, pq);
+                tmem_ld32(tmem + lane_base + kColOI + buf, oi);
                 tmem_ld_wait();
                 const int tt = c * kC + row;
                 if (tt < p.T) {
@@ -702,12 +764,6 @@ __global__ void __launch_bounds__(st::kThreads, 1)
                     store_row32(static_cast<TOut*>(p.o) + (((size_t)b * p.T + tt) * p.Hv + h) * kD + c0, ov);
                 }
             }
-            uint32_t ds[32];
-            tmem_ld32(tmem + lane_base + kColDS, ds);
-            tmem_ld_wait();
-            const float gam = __expf(g_last);
-#pragma unroll
-            for (int cc = 0; cc < kSlice; ++cc) S[cc] = fmaf(gam, S[cc], __uint_as_float(ds[cc]));
         }
         if (ok) {
 #pragma unroll
@@ -743,8 +799,10 @@ int launch(const void* q, const void* k, const void* v, const float* g_log, cons
     uint8_t* wsb = static_cast<uint8_t*>(ws);
     if ((rc = make_tmap_3d(&tw, wsb + L.w, dt, 2, kD, kC, nbhc, 64, kC, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
     if ((rc = make_tmap_3d(&ta, wsb + L.aqk, dt, 2, kC, kC, nbhc, 64, kC, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
-    CUtensorMap tu;
+    CUtensorMap tu, tus;
     if ((rc = make_tmap_3d(&tu, wsb + L.u, dt, 2, kD, kC, nbhc, 64, kC, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
+    if ((rc = make_tmap_3d(&tus, wsb + L.u, dt, 2, kD, kC, nbhc, kSlice, kC, CU_TENSOR_MAP_SWIZZLE_64B)))
+        return rc;
 
     PrepParams pp;
     pp.ws = wsb;
@@ -777,7 +835,7 @@ int launch(const void* q, const void* k, const void* v, const float* g_log, cons
     sp.scale = scale;
     auto k2 = gdn_state_kernel<T16, TOut>;
     B200_TRY_CUDA(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, st::kAlloc));
-    k2<<<dim3(kD / kSlice, Hv, B), st::kThreads, st::kAlloc, stream>>>(tq, tk, tw, ta, sp);
+    k2<<<dim3(kD / kSlice, Hv, B), st::kThreads, st::kAlloc, stream>>>(tq, tk, tw, ta, tus, sp);
     count_launch(2);
     return cudaGetLastError() == cudaSuccess ? B200LAB_OK : B200LAB_ERR_CUDA;
 }
