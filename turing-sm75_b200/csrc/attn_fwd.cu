@@ -91,6 +91,33 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+// 2^x for a pair of values on the FMA pipe (packed f32x2 ops), so that a quarter of
+// the exponentials leave the MUFU pipe (4 lanes a clock per SM sub-partition), which
+// otherwise bounds the softmax.  x = n + f by round-to-nearest through the 1.5*2^23
+// shifter, 2^f by a degree-3 polynomial fitted for this kernel (Remez exchange,
+// minimax relative error 7.5e-5 on [-1/2, 1/2], well below the 2^-9 rounding of the
+// 16-bit P), 2^n added into the exponent field.  x is clamped to >= -125 so the
+// result stays a normal float: a masked key gives 2^-125 instead of 0, and a row
+// that never sees a key is zeroed from its max in the epilogue.  More than a quarter
+// costs more issue slots (the packed ops take two) than it saves MUFU time.
+__device__ __forceinline__ float2 exp2_fma2(float2 x) {
+    constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
+    constexpr float kP0 = 9.999280572e-01f, kP1 = 6.932609677e-01f, kP2 = 2.426111251e-01f,
+                    kP3 = 5.517166853e-02f;
+    x.x = fmaxf(x.x, -125.f);
+    x.y = fmaxf(x.y, -125.f);
+    const float2 t = __fadd2_rn(x, make_float2(kShift, kShift));
+    const float2 n = __fadd2_rn(t, make_float2(-kShift, -kShift));
+    const float2 f = __ffma2_rn(n, make_float2(-1.f, -1.f), x);
+    float2 q = __ffma2_rn(make_float2(kP3, kP3), f, make_float2(kP2, kP2));
+    q = __ffma2_rn(q, f, make_float2(kP1, kP1));
+    q = __ffma2_rn(q, f, make_float2(kP0, kP0));
+    // the shifter's low mantissa bits hold n (two's complement); its own exponent
+    // and leading bits shift out above bit 31
+    return make_float2(__uint_as_float(__float_as_uint(q.x) + (__float_as_uint(t.x) << 23)),
+                       __uint_as_float(__float_as_uint(q.y) + (__float_as_uint(t.y) << 23)));
+}
+
 template <int D, typename T, bool kSplit>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -334,11 +361,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int c2 = 0; c2 < 32; ++c2) {
                     const int c = half * 64 + 2 * c2;
-                    const float e0 = ex2(fmaf(__uint_as_float(sr[c]), sl2, neg_mb));
-                    const float e1 = ex2(fmaf(__uint_as_float(sr[c + 1]), sl2, neg_mb));
-                    rs[c & 7] += e0;
-                    rs[(c + 1) & 7] += e1;
-                    pk[c2] = Elem<T>::pack2(e0, e1);
+                    const float2 x = __ffma2_rn(make_float2(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])),
+                                                make_float2(sl2, sl2), make_float2(neg_mb, neg_mb));
+                    float2 e;
+                    if ((c2 & 7) >= 6) {  // two pairs in every eight on the FMA pipe
+                        e = exp2_fma2(x);
+                    } else {
+                        e.x = ex2(x.x);
+                        e.y = ex2(x.y);
+                    }
+                    rs[c & 7] += e.x;
+                    rs[(c + 1) & 7] += e.y;
+                    pk[c2] = Elem<T>::pack2(e.x, e.y);
                 }
                 tmem_st32(tS + half * 32, pk);
             }
@@ -373,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const size_t prow = ((size_t)(b * p.Hq + hq) * p.Sq + qrow) * p.nsplit + split;
                 float* po = p.part_o + prow * D;
                 float2 ml = make_float2(m, l);
-                if (!(ok && nkv > 0)) ml = make_float2(-INFINITY, 0.f);
+                if (!(ok && nkv > 0) || m == -INFINITY) ml = make_float2(-INFINITY, 0.f);
                 *reinterpret_cast<float2*>(p.part_ml + prow * 2) = ml;
             }
 #pragma unroll
@@ -395,7 +429,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
         } else {
-            const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
+            // a row that never saw a key (max still -inf) is 0, as with l == 0
+            const float inv_l = (l > 0.f && m != -INFINITY) ? 1.f / l : 0.f;
             T* orow = static_cast<T*>(p.O) + ((size_t)(b * p.Hq + hq) * p.Sq + qrow) * D;
 #pragma unroll
             for (int c = 0; c < D / 32; ++c) {
