@@ -20,17 +20,16 @@
 //   TMA loads K, Q, V chunk tiles; ONE M=128 tcgen05 MMA gives [K;Q] K^T
 //   (lanes 0-63: K K^T, lanes 64-127: Q K^T); the threads form A and Aqk,
 //   invert (I + A) as a 2 x 2 block inverse in fp32, and two M=128, N=128 MMAs give
-//   [T diag(beta Gam); T diag(beta)] K -> W and [...] V -> U.
-//   W, U, Aqk (16-bit) and gcs (fp32) go to the workspace.
+//   [T diag(beta Gam); T diag(beta)] K -> W and [...] V -> U.  A last MMA gives
+//   M = W K_prev^T diag(e^{gcs_last,prev - gcs_prev}) against the previous chunk's keys.
+//   W, U, Aqk, M (16-bit) and gcs (fp32) go to the workspace.
 // Kernel 2, gdn_state_kernel: one CTA per (b, v-head, 32-column slice of the
-//   state), sequential over chunks.  The fp32 state slice lives in registers
-//   (thread i holds S[c0..c0+31][i]); per chunk:
-//     MMA1  [W;Q] S^T          (M=128,N=32,K=128) -> W S^T (lanes 0-63), Q S^T (64-127)
-//     Vn  = U - W S^T           (warps 0-1, 16-bit copy to shared memory)
-//     MMA2  [0;Aqk] Vn         (M=128,N=32,K=64)  -> intra-chunk output, lanes 64-127
-//     MMA3  K^T diag(e^{..}) Vn (M=128,N=32,K=64) -> state increment, lane i = key dim
-//     o = scale (Gam * Q S^T + intra)  (warps 2-3)      S = e^{gcs_last} S + increment
-//   A TMA producer warp double-buffers the chunk inputs; one thread issues MMAs.
+//   state), sequential over chunks, with the chain carried by Vn:
+//     Vn_{c+1} = U_{c+1} - e^{gcs_last,c} W_{c+1} S_c^T - M_{c+1} Vn_c
+//   so that between Vn_c and Vn_{c+1} sits one 64-deep MMA ([Aqk_c; M_{c+1}] Vn_c,
+//   which also gives the intra-chunk output), while the 128-deep [Q_c; W_{c+1}] S_c^T
+//   and the state update S_{c+1} = e^{gcs_last} S_c + K_c^T diag(..) Vn_c run beside it
+//   on their own warps and MMA thread.
 // Every wait is bounded (common.cuh).
 #include "common.cuh"
 #include "errwords.h"
@@ -46,7 +45,7 @@ constexpr int kSlice = 32;  // state columns (v dim) per kernel-2 CTA
 
 // ---- workspace layout ------------------------------------------------------
 struct WsLayout {
-    size_t w, u, aqk, gcs, total;
+    size_t w, u, aqk, m, gcs, total;
 };
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 __host__ __device__ inline WsLayout ws_layout(size_t nbhc) {
@@ -54,7 +53,8 @@ __host__ __device__ inline WsLayout ws_layout(size_t nbhc) {
     L.w = 0;
     L.u = align_up(L.w + nbhc * kC * kD * 2, 1024);
     L.aqk = align_up(L.u + nbhc * kC * kD * 2, 1024);
-    L.gcs = align_up(L.aqk + nbhc * kC * kC * 2, 1024);
+    L.m = align_up(L.aqk + nbhc * kC * kC * 2, 1024);
+    L.gcs = align_up(L.m + nbhc * kC * kC * 2, 1024);
     L.total = align_up(L.gcs + nbhc * kC * 4, 1024);
     return L;
 }
@@ -101,7 +101,8 @@ struct Misc {
     float g2[kC];    // gcs * log2(e), for ex2
     float beta[kC];
     float colscale[2 * kC];  // [beta Gam | beta], the column scales of T' and T''
-    uint64_t bar_tma, bar_mma1, bar_mma2, drain;
+    float gprev[kC];         // cumsum of g_log over the previous chunk (for M)
+    uint64_t bar_tma, bar_mma1, bar_mma2, bar_kp, bar_m, drain;
     uint32_t tmem_base;
     int abort;
 };
@@ -205,7 +206,7 @@ __global__ void __launch_bounds__(prep::kThreads, 2)
     gdn_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmW,
                     const __grid_constant__ CUtensorMap tmU, const __grid_constant__ CUtensorMap tmAqk,
-                    const PrepParams p) {
+                    const __grid_constant__ CUtensorMap tmM, const PrepParams p) {
     using namespace prep;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -229,6 +230,8 @@ __global__ void __launch_bounds__(prep::kThreads, 2)
         mbar_init(&ms->bar_tma, 1);
         mbar_init(&ms->bar_mma1, 1);
         mbar_init(&ms->bar_mma2, 1);
+        mbar_init(&ms->bar_kp, 1);
+        mbar_init(&ms->bar_m, 1);
         mbar_init(&ms->drain, 1);
         ms->abort = 0;
         fence_barrier_init();
@@ -267,6 +270,16 @@ __global__ void __launch_bounds__(prep::kThreads, 2)
         }
         ms->gcs[tid] = g;  // per-warp inclusive scan; warp 1 adds warp 0's total below
         ms->beta[tid] = be;
+    } else if (c > 0) {
+        // warps 2-3: the same scan over the previous (always full) chunk, for M
+        const size_t gi = ((size_t)b * p.T + (t0 - kC + tid - kC)) * p.Hv + h;
+        float g = p.g_log[gi];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float y = __shfl_up_sync(0xffffffffu, g, o);
+            if (lane >= o) g += y;
+        }
+        ms->gprev[tid - kC] = g;
     }
     __syncthreads();
     if (tid < kC) {
@@ -274,6 +287,11 @@ __global__ void __launch_bounds__(prep::kThreads, 2)
         __syncwarp();
         ms->gcs[tid] = g;
         ms->g2[tid] = g * 1.4426950408889634f;
+    } else if (c > 0) {
+        const int t = tid - kC;
+        const float g = t >= 32 ? ms->gprev[t] + ms->gprev[31] : ms->gprev[t];
+        __syncwarp();
+        ms->gprev[t] = g;
     }
     __syncthreads();
 
@@ -380,6 +398,12 @@ __global__ void __launch_bounds__(prep::kThreads, 2)
     // MMA2: [T'; T''] K  -> cols 0-127, [T'; T''] V -> cols 128-255  (M=128, N=128, K=64);
     // B operands MN-major: K chunks 16 KiB apart ([K0|Q0|K1|Q1]), V chunks 8 KiB apart
     if (tid == 0 && ok) {
+        if (c > 0) {
+            // K of the previous chunk into the (now dead) A tile, for M below
+            mbar_arrive_expect_tx(&ms->bar_kp, 2 * 8192);
+            tma_load_4d(smem + kAs, &tmK, &ms->bar_kp, 0, hq, t0 - kC, b);
+            tma_load_4d(smem + kAs + 8192, &tmK, &ms->bar_kp, 64, hq, t0 - kC, b);
+        }
         tc_fence_after();
         constexpr uint32_t idesc = make_idesc(Elem<T16>::kFmt, 128, 128, false, true);
         const uint32_t a0 = smem_u32(smem + kAT);
@@ -422,12 +446,67 @@ __global__ void __launch_bounds__(prep::kThreads, 2)
         if (warp < 2)
             reinterpret_cast<float*>(p.ws + p.ws_gcs)[bhc * kC + row] = gcs_r;
     }
+    tc_fence_before();
     __syncthreads();
     if (tid == 0 && ok) {
         tma_store_3d(&tmW, smem + kTiles, 0, 0, (int)bhc);
         tma_store_3d(&tmW, smem + kTiles + 8192, 64, 0, (int)bhc);
         tma_store_3d(&tmU, smem + kTiles + 16384, 0, 0, (int)bhc);
         tma_store_3d(&tmU, smem + kTiles + 24576, 64, 0, (int)bhc);
+        bulk_commit();
+        // M = W K_prev^T (M=128, N=64, K=128): A = the staged W (K-major, its two
+        // 64-column boxes 8 KiB apart; rows 64-127 of the product are not used),
+        // B = K of the previous chunk.  Result in TMEM cols 0-63, lanes 0-63.
+        if (c > 0) {
+            ok = mbar_wait(&ms->bar_kp, 0, abort, &g_err_gdn_prefill);
+            if (ok) {
+                tc_fence_after();
+                constexpr uint32_t idesc = make_idesc(Elem<T16>::kFmt, 128, 64, false, false);
+                const uint64_t dw = smem_desc(smem_u32(smem + kTiles), 16, 1024, kLayoutSW128);
+                const uint64_t dk = smem_desc(smem_u32(smem + kAs), 16, 1024, kLayoutSW128);
+#pragma unroll
+                for (int kk = 0; kk < kD / 16; ++kk) {
+                    const uint32_t off = ((kk >> 2) * 8192 + (kk & 3) * 32) >> 4;
+                    mma_f16_ss(tmem, dw + off, dk + off, idesc, kk > 0 ? 1u : 0u);
+                }
+                mma_commit(&ms->bar_m);
+            }
+        }
+    }
+    // M[t][s] = (W K_prev^T)[t][s] e^{gprev_last - gprev_s}: the previous chunk's
+    // decayed keys as seen through this chunk's W.  Staged over AT (free since
+    // MMA2), stored next to Aqk.  Chunk 0 of a sequence stores zeros.
+    if (c > 0)
+        ok = __all_sync(0xffffffffu, mbar_wait(&ms->bar_m, 0, abort, &g_err_gdn_prefill)) && ok;
+    tc_fence_after();
+    if (warp < 2) {
+        uint32_t v[64];
+        if (c > 0 && ok) {
+            tmem_ld32(tmem + lane_base + 0, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+            tmem_ld32(tmem + lane_base + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+            tmem_ld_wait();
+        }
+        const float glast_prev = ms->gprev[kC - 1];
+        uint8_t* stg = smem + kAT + row * 128;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            uint4 pk = make_uint4(0, 0, 0, 0);
+            if (c > 0 && ok) {
+                uint32_t* pw = &pk.x;
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int s0 = q * 8 + 2 * u;
+                    pw[u] = Elem<T16>::pack2(__uint_as_float(v[s0]) * __expf(glast_prev - ms->gprev[s0]),
+                                             __uint_as_float(v[s0 + 1]) * __expf(glast_prev - ms->gprev[s0 + 1]));
+                }
+            }
+            *reinterpret_cast<uint4*>(stg + ((q ^ (row & 7)) << 4)) = pk;
+        }
+        fence_proxy_async_smem();
+    }
+    __syncthreads();
+    if (tid == 0 && ok) {
+        tma_store_3d(&tmM, smem + kAT, 0, 0, (int)bhc);
         bulk_commit();
         bulk_wait_all();
     }
@@ -446,48 +525,71 @@ __global__ void __launch_bounds__(prep::kThreads, 2)
 // ===========================================================================
 // Kernel 2: sequential state pass
 // ===========================================================================
+// The chain runs on Vn, not on S.  With R_{c+1} = W_{c+1} S_c^T and
+// M_{c+1} = W_{c+1} K_c^T diag(e^{gcs_last,c - gcs_c}) (from kernel 1),
+//   Vn_{c+1} = U_{c+1} - W_{c+1} S_{c+1}^T = U_{c+1} - e^{gcs_last,c} R_{c+1} - M_{c+1} Vn_c,
+// so the only MMA between Vn_c and Vn_{c+1} is the 64-deep M_{c+1} Vn_c; the 128-deep
+// products with S (R_{c+1} and Q_c S_c^T) run a chunk ahead, off the chain.
 namespace st {
-constexpr int kThreads = 192;  // warps 0-3 compute, 4 TMA producer, 5 MMA issuer
-constexpr int kWarpProducer = 4, kWarpMma = 5;
-// one stage of chunk inputs (69 KiB):
-//   [W0|Q0|W1|Q1] A1 tile 32 KiB; [K0|K1] 16 KiB; [zero|Aqk] 16 KiB;
-//   this CTA's 32 columns of U (64-byte swizzle) 4 KiB; gcs 256 B
-// Three stages: global/TMA latency under this load is about two chunk periods.
+// warps 0-3 state (thread = key row of the slice), 4-5 outputs (TMEM lanes 0-63),
+// 6-7 Vn (lanes 64-127), 8 TMA producer, 9 chain MMAs, 10 state MMAs
+constexpr int kThreads = 352;
+constexpr int kWarpOut = 4, kWarpVn = 6, kWarpProducer = 8, kWarpMmaA = 9, kWarpMmaB = 10;
+// one stage of chunk c (69 KiB):
+//   A1  [Q_c b0 | W_{c+1} b0 | Q_c b1 | W_{c+1} b1]  32 KiB: A of [Q_c; W_{c+1}] S_c^T
+//   Kt  [K_c b0 | K_c b1]                              16 KiB: A of K_c^T Vt_c (MN-major)
+//   AM  [Aqk_c | M_{c+1}]                              16 KiB: A of [Aqk_c; M_{c+1}] Vn_c
+//   U   this CTA's 32 columns of U_c (64-byte swizzle)  4 KiB;  G  gcs_c  256 B
+// (b0/b1: 64-column boxes).  Three stages; the prologue's W_0 borrows stage 2's A1.
 constexpr int kStage = 70656;
-constexpr int kA1 = 0, kKt = 32768, kZero = 49152, kAqk = 57344, kU = 65536, kG = 69632;
-constexpr int kStageTx = 7 * 8192 + 4096 + kC * 4;
+constexpr int kA1 = 0, kKt = 32768, kAM = 49152, kU = 65536, kG = 69632;
+constexpr int kStageTx = 8 * 8192 + 4096 + kC * 4;
 constexpr int kStages = 3;
-// B operands of the chain, MN-major with 64-byte swizzle: one 64-byte row (32 state
-// columns, 16-bit) per K index, so each thread writes its row as four 16-byte chunks
+// B operands, MN-major with 64-byte swizzle: one 64-byte row (32 state columns,
+// 16-bit) per K index, so each thread writes its row as four 16-byte chunks
 constexpr int kSt = kStages * kStage;    // S^T tile: 128 keys x 32 v, 8 KiB
 constexpr int kVn = kSt + 8192;          // Vn tile: 64 tokens x 32 v, 4 KiB
 constexpr int kVt = kVn + 4096;          // decayed Vn tile, 4 KiB
 constexpr int kMisc = kVt + 4096;
 constexpr int kBytes = kMisc + 256;
 constexpr int kAlloc = kBytes + 1024;
+static_assert(kAlloc <= 232448, "state kernel shared memory above the 227 KiB per-CTA limit");
 constexpr uint32_t kTmemCols = 256;
-// P ([W;Q] S^T) and OI ([0;Aqk] Vn) alternate between two buffers by chunk parity so
-// the output warps may read chunk c while the chain already runs chunk c+1
-constexpr uint32_t kColP = 0, kColOI = 64, kColDS = 128;
+// TMEM, two buffers each by chunk parity (32 columns a buffer):
+//   X1 = [Aqk_c; M_{c+1}] Vn_c   lanes 0-63 intra-chunk output, 64-127 chain term
+//   DS = K_c^T Vt_c              lane = key: the state increment
+//   RQ = [Q_c; W_{c+1}] S_c^T    lanes 0-63 Q S^T, 64-127 R_{c+1}
+constexpr uint32_t kColX1 = 0, kColDS = 64, kColRQ = 128;
 
 struct Misc {
     uint64_t full[kStages], empty[kStages];
-    uint64_t s_ready, p_full, v_ready, ds_full, o_full[2], drain;
+    uint64_t pro_full, pro_done;
+    uint64_t s_ready[2], v_ready;
+    uint64_t x1_full[2], ds_full[2], rq_full[2];
+    uint64_t o_done[2];  // the output warps have read X1 / RQ buffer (c & 1) of chunk c
+    uint64_t drain_a, drain_b;
     uint32_t tmem_base;
     int abort;
 };
+static_assert(sizeof(Misc) <= kBytes - kMisc, "state Misc overflows its slot");
+
+// rq_full[c & 1] completes for the prologue product (counted as c = -1, buffer 1)
+// and then for c = 0, 1, 2, ...: the parity of the completion that belongs to c
+__device__ __forceinline__ uint32_t rq_parity(int c) {
+    return c < 0 ? 0u : (uint32_t)(((c & 1) ? (c + 1) >> 1 : c >> 1) & 1);
+}
+}  // namespace st
 
 // byte offset of 16-byte chunk q (columns 8q..8q+7) of row r in a 64-byte-swizzled tile
 __device__ __forceinline__ uint32_t sw64_chunk(int r, int q) {
     return (uint32_t)(r * 64 + ((q ^ ((r >> 1) & 3)) << 4));
 }
-}  // namespace st
 
 struct StateParams {
     const uint8_t* ws;
     float* state;
     void* o;
-    size_t ws_u, ws_gcs;
+    size_t ws_gcs;
     int T, Hqk, Hv, nch, head_map;
     float scale;
 };
@@ -516,7 +618,8 @@ template <typename T16, typename TOut>
 __global__ void __launch_bounds__(st::kThreads, 1)
     gdn_state_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmAqk,
-                     const __grid_constant__ CUtensorMap tmU, const StateParams p) {
+                     const __grid_constant__ CUtensorMap tmM, const __grid_constant__ CUtensorMap tmU,
+                     const StateParams p) {
     using namespace st;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -536,25 +639,24 @@ __global__ void __launch_bounds__(st::kThreads, 1)
     if (tid == 0) {
         for (int i = 0; i < kStages; ++i) {
             mbar_init(&ms->full[i], 1);
-            mbar_init(&ms->empty[i], 1);
+            mbar_init(&ms->empty[i], 2);  // one commit from each MMA thread
         }
-        mbar_init(&ms->s_ready, 128);
-        mbar_init(&ms->p_full, 1);
+        mbar_init(&ms->pro_full, 1);
+        mbar_init(&ms->pro_done, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&ms->s_ready[i], 128);
+            mbar_init(&ms->x1_full[i], 1);
+            mbar_init(&ms->ds_full[i], 1);
+            mbar_init(&ms->rq_full[i], 1);
+            mbar_init(&ms->o_done[i], 64);
+        }
         mbar_init(&ms->v_ready, 64);
-        mbar_init(&ms->ds_full, 1);
-        mbar_init(&ms->o_full[0], 1);
-        mbar_init(&ms->o_full[1], 1);
-        mbar_init(&ms->drain, 1);
+        mbar_init(&ms->drain_a, 1);
+        mbar_init(&ms->drain_b, 1);
         ms->abort = 0;
         fence_barrier_init();
     }
-    // zero rows 0-63 of both [0;Aqk] tiles (never written by TMA)
-    for (int i = tid; i < kStages * 8192 / 16; i += blockDim.x) {
-        const int s = i / (8192 / 16), o = i % (8192 / 16);
-        reinterpret_cast<uint4*>(smem + s * kStage + kZero)[o] = make_uint4(0, 0, 0, 0);
-    }
-    fence_proxy_async_smem();
-    if (warp == kWarpMma) {
+    if (warp == kWarpMmaA) {
         tmem_alloc(&ms->tmem_base, kTmemCols);
         tmem_relinquish();
     }
@@ -562,112 +664,119 @@ __global__ void __launch_bounds__(st::kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = ms->tmem_base;
+    constexpr uint32_t kFmt = Elem<T16>::kFmt;
 
     if (warp == kWarpProducer) {
         if (lane == 0) {
-            int issued = 0;
             const float* gcs_all = reinterpret_cast<const float*>(p.ws + p.ws_gcs);
+            const int bhc0 = (int)(bh * p.nch);
+            // prologue: W_0 into the W rows of stage 2's A1 tile
+            uint8_t* pro = smem + (kStages - 1) * kStage + kA1;
+            mbar_arrive_expect_tx(&ms->pro_full, 2 * 8192);
+            tma_load_3d(pro + 8192, &tmW, &ms->pro_full, 0, 0, bhc0);
+            tma_load_3d(pro + 24576, &tmW, &ms->pro_full, 64, 0, bhc0);
+            int issued = 0;
             for (int c = 0; c < p.nch; ++c) {
                 const int s = c % kStages;
                 if (!mbar_wait(&ms->empty[s], ((c / kStages) & 1) ^ 1, abort, &g_err_gdn_prefill)) break;
+                if (c == kStages - 1 && !mbar_wait(&ms->pro_done, 0, abort, &g_err_gdn_prefill)) break;
                 uint8_t* stg = smem + s * kStage;
                 uint64_t* bar = &ms->full[s];
-                const int bhc = (int)(bh * p.nch + c);
+                const int bhc = bhc0 + c;
+                // W_{c+1}, M_{c+1} of the last chunk read the next sequence's first chunk (or
+                // zero fill past the end): those rows of the products are not used
                 mbar_arrive_expect_tx(bar, kStageTx);
-                tma_load_3d(stg + kU, &tmU, bar, c0, 0, bhc);
-                bulk_load_1d(stg + kG, gcs_all + (size_t)bhc * kC, kC * 4, bar);
-                tma_load_3d(stg + kA1 + 0, &tmW, bar, 0, 0, bhc);
-                tma_load_3d(stg + kA1 + 16384, &tmW, bar, 64, 0, bhc);
-                tma_load_4d(stg + kA1 + 8192, &tmQ, bar, 0, hq, c * kC, b);
-                tma_load_4d(stg + kA1 + 24576, &tmQ, bar, 64, hq, c * kC, b);
+                tma_load_4d(stg + kA1 + 0, &tmQ, bar, 0, hq, c * kC, b);
+                tma_load_3d(stg + kA1 + 8192, &tmW, bar, 0, 0, bhc + 1);
+                tma_load_4d(stg + kA1 + 16384, &tmQ, bar, 64, hq, c * kC, b);
+                tma_load_3d(stg + kA1 + 24576, &tmW, bar, 64, 0, bhc + 1);
                 tma_load_4d(stg + kKt, &tmK, bar, 0, hq, c * kC, b);
                 tma_load_4d(stg + kKt + 8192, &tmK, bar, 64, hq, c * kC, b);
-                tma_load_3d(stg + kAqk, &tmAqk, bar, 0, 0, bhc);
+                tma_load_3d(stg + kAM, &tmAqk, bar, 0, 0, bhc);
+                tma_load_3d(stg + kAM + 8192, &tmM, bar, 0, 0, bhc + 1);
+                tma_load_3d(stg + kU, &tmU, bar, c0, 0, bhc);
+                bulk_load_1d(stg + kG, gcs_all + (size_t)bhc * kC, kC * 4, bar);
                 issued = c + 1;
             }
+            mbar_wait(&ms->pro_full, 0, abort, &g_err_gdn_prefill);
             for (int c = max(0, issued - kStages); c < issued; ++c)
                 mbar_wait(&ms->full[c % kStages], (c / kStages) & 1, abort, &g_err_gdn_prefill);
         }
-    } else if (warp == kWarpMma) {
+    } else if (warp == kWarpMmaA) {
+        // chain MMAs: X1 = [Aqk_c; M_{c+1}] Vn_c, then DS = K_c^T Vt_c
         if (lane == 0) {
-            constexpr uint32_t kFmt = Elem<T16>::kFmt;
-            constexpr uint32_t id_kb = make_idesc(kFmt, 128, kSlice, false, true);   // A K-major, B MN
-            constexpr uint32_t id_mn = make_idesc(kFmt, 128, kSlice, true, true);    // both MN-major
-            // Descriptors built once; per K-step only the address field advances. The
-            // MN-major B tiles: SBO = 512 (8 K rows of 64 B), one 32-column MN block.
-            const uint64_t dS = smem_desc(smem_u32(smem + kSt), 8192, 512, kLayoutSW64);
+            constexpr uint32_t id_kb = make_idesc(kFmt, 128, kSlice, false, true);  // A K-major, B MN
+            constexpr uint32_t id_mn = make_idesc(kFmt, 128, kSlice, true, true);   // both MN-major
+            const uint64_t dAM = smem_desc(smem_u32(smem + kAM), 16, 1024, kLayoutSW128);
+            const uint64_t dK = smem_desc(smem_u32(smem + kKt), 8192, 1024, kLayoutSW128);
             const uint64_t dVn = smem_desc(smem_u32(smem + kVn), 4096, 512, kLayoutSW64);
             const uint64_t dVt = smem_desc(smem_u32(smem + kVt), 4096, 512, kLayoutSW64);
-            const uint64_t dA1 = smem_desc(smem_u32(smem + kA1), 16, 1024, kLayoutSW128);
-            const uint64_t dZ = smem_desc(smem_u32(smem + kZero), 16, 1024, kLayoutSW128);
-            const uint64_t dK = smem_desc(smem_u32(smem + kKt), 8192, 1024, kLayoutSW128);
             for (int c = 0; c < p.nch; ++c) {
                 const int s = c % kStages;
                 const uint32_t so = (s * kStage) >> 4;
-                if (!mbar_wait(&ms->full[s], (c / kStages) & 1, abort, &g_err_gdn_prefill)) break;
-                if (!mbar_wait(&ms->s_ready, c & 1, abort, &g_err_gdn_prefill)) break;
-                tc_fence_after();
                 const uint32_t buf = (c & 1) * 32;
-                // MMA1: [W;Q] S^T
+                if (!mbar_wait(&ms->full[s], (c / kStages) & 1, abort, &g_err_gdn_prefill)) break;
+                if (!mbar_wait(&ms->v_ready, c & 1, abort, &g_err_gdn_prefill)) break;
+                if (c >= 2 && !mbar_wait(&ms->o_done[c & 1], ((c - 2) >> 1) & 1, abort, &g_err_gdn_prefill)) break;
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < kC / 16; ++kk)
+                    mma_f16_ss(tmem + kColX1 + buf, dAM + so + ((kk * 32) >> 4), dVn + ((kk * 1024) >> 4), id_kb,
+                               kk > 0 ? 1u : 0u);
+                mma_commit(&ms->x1_full[c & 1]);
+#pragma unroll
+                for (int kk = 0; kk < kC / 16; ++kk)
+                    mma_f16_ss(tmem + kColDS + buf, dK + so + ((kk * 2048) >> 4), dVt + ((kk * 1024) >> 4), id_mn,
+                               kk > 0 ? 1u : 0u);
+                mma_commit(&ms->ds_full[c & 1]);
+                mma_commit(&ms->empty[s]);
+            }
+            mma_commit(&ms->drain_a);
+            mbar_wait(&ms->drain_a, 0, abort, &g_err_gdn_prefill);
+        }
+    } else if (warp == kWarpMmaB) {
+        // state MMAs: RQ = [Q_c; W_{c+1}] S_c^T, one chunk ahead of the chain
+        if (lane == 0) {
+            constexpr uint32_t id_kb = make_idesc(kFmt, 128, kSlice, false, true);
+            const uint64_t dA1 = smem_desc(smem_u32(smem + kA1), 16, 1024, kLayoutSW128);
+            const uint64_t dS = smem_desc(smem_u32(smem + kSt), 8192, 512, kLayoutSW64);
+            auto rq = [&](uint32_t so, uint32_t buf) {
 #pragma unroll
                 for (int kk = 0; kk < kD / 16; ++kk) {
                     const uint32_t ao = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
-                    mma_f16_ss(tmem + kColP + buf, dA1 + so + ao, dS + ((kk * 1024) >> 4), id_kb,
+                    mma_f16_ss(tmem + kColRQ + buf, dA1 + so + ao, dS + ((kk * 1024) >> 4), id_kb,
                                kk > 0 ? 1u : 0u);
                 }
-                mma_commit(&ms->p_full);
-                if (!mbar_wait(&ms->v_ready, c & 1, abort, &g_err_gdn_prefill)) break;
+            };
+            // prologue: R_0 = W_0 S_0^T (rows 64-127; rows 0-63 read stage 2's unused Q slot)
+            bool ok = mbar_wait(&ms->pro_full, 0, abort, &g_err_gdn_prefill) &&
+                      mbar_wait(&ms->s_ready[0], 0, abort, &g_err_gdn_prefill);
+            if (ok) {
                 tc_fence_after();
-                // MMA3 first (it closes the chain): K^T (decayed Vn) -> state increment,
-                // lane = key index
-#pragma unroll
-                for (int kk = 0; kk < kC / 16; ++kk)
-                    mma_f16_ss(tmem + kColDS, dK + so + ((kk * 2048) >> 4), dVt + ((kk * 1024) >> 4), id_mn,
-                               kk > 0 ? 1u : 0u);
-                mma_commit(&ms->ds_full);
-                // MMA2: [0;Aqk] Vn -> intra-chunk outputs in lanes 64-127
-#pragma unroll
-                for (int kk = 0; kk < kC / 16; ++kk)
-                    mma_f16_ss(tmem + kColOI + buf, dZ + so + ((kk * 32) >> 4), dVn + ((kk * 1024) >> 4), id_kb,
-                               kk > 0 ? 1u : 0u);
-                mma_commit(&ms->o_full[c & 1]);
+                rq(((kStages - 1) * kStage) >> 4, 32);
+                mma_commit(&ms->rq_full[1]);
+                mma_commit(&ms->pro_done);
+            }
+            for (int c = 0; ok && c < p.nch; ++c) {
+                const int s = c % kStages;
+                if (!mbar_wait(&ms->full[s], (c / kStages) & 1, abort, &g_err_gdn_prefill)) break;
+                if (c > 0 && !mbar_wait(&ms->s_ready[c & 1], (c >> 1) & 1, abort, &g_err_gdn_prefill)) break;
+                if (c >= 2 && !mbar_wait(&ms->o_done[c & 1], ((c - 2) >> 1) & 1, abort, &g_err_gdn_prefill)) break;
+                tc_fence_after();
+                rq((s * kStage) >> 4, (c & 1) * 32);
+                mma_commit(&ms->rq_full[c & 1]);
                 mma_commit(&ms->empty[s]);
             }
-            mma_commit(&ms->drain);
-            mbar_wait(&ms->drain, 0, abort, &g_err_gdn_prefill);
+            mma_commit(&ms->drain_b);
+            mbar_wait(&ms->drain_b, 0, abort, &g_err_gdn_prefill);
         }
     } else {
-        // ---------------- compute warps 0-3 -----------------------------------
-        const int i = tid;                         // key index this thread owns (0..127)
-        const int row = (warp & 1) * 32 + lane;    // token row for warps 0-1 (Vn) and 2-3 (O)
-        const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-        float S[kSlice];
-        float* Sg = p.state + (bh * kD + c0) * kD + i;
-#pragma unroll
-        for (int cc = 0; cc < kSlice; ++cc) S[cc] = Sg[(size_t)cc * kD];
-        uint8_t* sS = smem + kSt;
-        uint8_t* sVn = smem + kVn;
-        uint8_t* sVt = smem + kVt;
-        // chunk inputs read by the threads (U slice row, gates) are fetched one
-        // chunk ahead so their latency hides behind the previous chunk
-        uint4 u_nx[kSlice / 8] = {};
-        float gcs_nx = 0.f, glast_nx = 0.f;
-        // Reads chunk c's U row and gates out of its stage. Called one chunk ahead, before
-        // this thread's s_ready arrival that the chunk's last MMA (and so the stage's
-        // release to the producer) depends on.
-        auto prefetch = [&](int c) -> bool {
-            const int s = c % kStages;
-            if (!mbar_wait(&ms->full[s], (c / kStages) & 1, abort, &g_err_gdn_prefill)) return false;
-            const uint8_t* stg = smem + s * kStage;
-            const float* G = reinterpret_cast<const float*>(stg + kG);
-            gcs_nx = G[row];
-            glast_nx = G[kC - 1];
-            if (warp < 2) {
-#pragma unroll
-                for (int q8 = 0; q8 < kSlice / 8; ++q8)
-                    u_nx[q8] = *reinterpret_cast<const uint4*>(stg + kU + sw64_chunk(row, q8));
-            }
-            return true;
+        // ---------------- compute warps: three roles, each on its own chain -------
+        const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+        const float* gcs_all = reinterpret_cast<const float*>(p.ws + p.ws_gcs);
+        const size_t bhc0 = bh * p.nch;
+        auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
+            return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, &g_err_gdn_prefill));
         };
         // 32 values -> one 64-byte row of an MN-major B tile (16-bit)
         auto put_row = [&](uint8_t* tile, int r, const float* x) {
@@ -681,79 +790,61 @@ __global__ void __launch_bounds__(st::kThreads, 1)
                 *reinterpret_cast<uint4*>(tile + sw64_chunk(r, q)) = pk;
             }
         };
-        // S (16-bit) -> shared, B operand of MMA1: K index = key i, 32 v columns
-        auto publish_S = [&]() {
-            put_row(sS, i, S);
-            fence_proxy_async_smem();
-            tc_fence_before();
-            mbar_arrive(&ms->s_ready);
-        };
-        bool ok = true;
-        if (p.nch > 0) {
-            ok = __all_sync(0xffffffffu, prefetch(0));
-            publish_S();
-        }
-        for (int c = 0; c < p.nch && ok; ++c) {
-            const float gcs_t = gcs_nx;
-            const float g_last = glast_nx;
-            const uint32_t buf = (c & 1) * 32;
-            uint4 u_raw[kSlice / 8];
+        if (warp < kWarpOut) {
+            // ---- state: S_{c+1} = e^{gcs_last} S_c + K_c^T Vt_c, thread i = key i ----
+            const int i = tid;
+            float S[kSlice];
+            float* Sg = p.state + (bh * kD + c0) * kD + i;
 #pragma unroll
-            for (int q8 = 0; q8 < kSlice / 8; ++q8) u_raw[q8] = u_nx[q8];
-            if (c + 1 < p.nch && !__all_sync(0xffffffffu, prefetch(c + 1))) {
-                ok = false;
-                break;
-            }
-
-            if (warp < 2) {
-                float u[kSlice];
-#pragma unroll
-                for (int q8 = 0; q8 < kSlice / 8; ++q8) {
-                    const T16* e = reinterpret_cast<const T16*>(&u_raw[q8]);
-#pragma unroll
-                    for (int u8 = 0; u8 < 8; ++u8) u[q8 * 8 + u8] = Elem<T16>::to_f(e[u8]);
-                }
-                ok = __all_sync(0xffffffffu, mbar_wait(&ms->p_full, c & 1, abort, &g_err_gdn_prefill));
-                if (!ok) break;
-                tc_fence_after();
-                uint32_t pr[32];
-                tmem_ld32(tmem + lane_base + kColP + buf, pr);
-                tmem_ld_wait();
-                const float dec = __expf(g_last - gcs_t);
-                float vt[kSlice];
-#pragma unroll
-                for (int cc = 0; cc < kSlice; ++cc) {
-                    u[cc] -= __uint_as_float(pr[cc]);
-                    vt[cc] = u[cc] * dec;
-                }
-                put_row(sVn, row, u);
-                put_row(sVt, row, vt);
+            for (int cc = 0; cc < kSlice; ++cc) S[cc] = Sg[(size_t)cc * kD];
+            uint8_t* sS = smem + kSt;
+            // S (16-bit) -> shared (B operand of the RQ product), then S_c is announced
+            auto publish_S = [&](int c) {
+                put_row(sS, i, S);
                 fence_proxy_async_smem();
                 tc_fence_before();
-                mbar_arrive(&ms->v_ready);
-            }
-            // close the chain first: S <- gamma S + K^T Vt, then hand S(c+1) to the MMA warp
-            ok = __all_sync(0xffffffffu, mbar_wait(&ms->ds_full, c & 1, abort, &g_err_gdn_prefill));
-            if (!ok) break;
-            tc_fence_after();
-            {
+                mbar_arrive(&ms->s_ready[c & 1]);
+            };
+            bool ok = true;
+            if (p.nch > 0) publish_S(0);
+            float glast_nx = p.nch > 0 ? gcs_all[bhc0 * kC + kC - 1] : 0.f;
+            for (int c = 0; c < p.nch; ++c) {
+                const float gam = __expf(glast_nx);
+                if (c + 1 < p.nch) glast_nx = gcs_all[(bhc0 + c + 1) * kC + kC - 1];
+                if (!wait_all(&ms->ds_full[c & 1], (c >> 1) & 1)) { ok = false; break; }
+                tc_fence_after();
                 uint32_t ds[32];
-                tmem_ld32(tmem + lane_base + kColDS, ds);
+                tmem_ld32(tmem + lane_base + kColDS + (c & 1) * 32, ds);
                 tmem_ld_wait();
-                const float gam = __expf(g_last);
 #pragma unroll
                 for (int cc = 0; cc < kSlice; ++cc) S[cc] = fmaf(gam, S[cc], __uint_as_float(ds[cc]));
+                if (c + 1 < p.nch) {
+                    // the S tile is rewritten only once the RQ product that reads S_c is done
+                    if (!wait_all(&ms->rq_full[c & 1], st::rq_parity(c))) { ok = false; break; }
+                    tc_fence_after();
+                    publish_S(c + 1);
+                }
             }
-            if (c + 1 < p.nch) publish_S();
-            if (warp >= 2) {
-                ok = __all_sync(0xffffffffu,
-                                mbar_wait(&ms->o_full[c & 1], (c >> 1) & 1, abort, &g_err_gdn_prefill));
-                if (!ok) break;
+            if (ok) {
+#pragma unroll
+                for (int cc = 0; cc < kSlice; ++cc) Sg[(size_t)cc * kD] = S[cc];
+            }
+        } else if (warp < kWarpVn) {
+            // ---- outputs: o_c = scale (e^{gcs} Q_c S_c^T + Aqk_c Vn_c), token row ----
+            const int row = tid - kWarpOut * 32;  // 0..63 = TMEM lane
+            float gcs_nx = p.nch > 0 ? gcs_all[bhc0 * kC + row] : 0.f;
+            for (int c = 0; c < p.nch; ++c) {
+                const float gcs_t = gcs_nx;
+                if (c + 1 < p.nch) gcs_nx = gcs_all[(bhc0 + c + 1) * kC + row];
+                if (!wait_all(&ms->rq_full[c & 1], st::rq_parity(c))) break;
+                if (!wait_all(&ms->x1_full[c & 1], (c >> 1) & 1)) break;
                 tc_fence_after();
                 uint32_t pq[32], oi[32];
-                tmem_ld32(tmem + lane_base + kColP + buf, pq);
-                tmem_ld32(tmem + lane_base + kColOI + buf, oi);
+                tmem_ld32(tmem + lane_base + kColRQ + (c & 1) * 32, pq);
+                tmem_ld32(tmem + lane_base + kColX1 + (c & 1) * 32, oi);
                 tmem_ld_wait();
+                tc_fence_before();
+                mbar_arrive(&ms->o_done[c & 1]);
                 const int tt = c * kC + row;
                 if (tt < p.T) {
                     const float eg = __expf(gcs_t);
@@ -764,16 +855,58 @@ __global__ void __launch_bounds__(st::kThreads, 1)
                     store_row32(static_cast<TOut*>(p.o) + (((size_t)b * p.T + tt) * p.Hv + h) * kD + c0, ov);
                 }
             }
-        }
-        if (ok) {
+        } else {
+            // ---- Vn_c = U_c - e^{gcs_last,c-1} R_c - M_c Vn_{c-1}   (c = 0: U_0 - W_0 S_0^T)
+            const int row = tid - kWarpVn * 32;  // token; TMEM lane 64 + row
+            uint8_t* sVn = smem + kVn;
+            uint8_t* sVt = smem + kVt;
+            float gam_prev = 1.f;
+            for (int c = 0; c < p.nch; ++c) {
+                const int s = c % kStages;
+                // chunk c's U row and gates from its stage (released only after v_ready(c))
+                if (!wait_all(&ms->full[s], (c / kStages) & 1)) break;
+                const uint8_t* stg = smem + s * kStage;
+                const float gcs_t = reinterpret_cast<const float*>(stg + kG)[row];
+                const float g_last = reinterpret_cast<const float*>(stg + kG)[kC - 1];
+                float u[kSlice];
 #pragma unroll
-            for (int cc = 0; cc < kSlice; ++cc) Sg[(size_t)cc * kD] = S[cc];
+                for (int q8 = 0; q8 < kSlice / 8; ++q8) {
+                    const uint4 raw = *reinterpret_cast<const uint4*>(stg + kU + sw64_chunk(row, q8));
+                    const T16* e = reinterpret_cast<const T16*>(&raw);
+#pragma unroll
+                    for (int u8 = 0; u8 < 8; ++u8) u[q8 * 8 + u8] = Elem<T16>::to_f(e[u8]);
+                }
+                if (!wait_all(&ms->rq_full[(c - 1) & 1], st::rq_parity(c - 1))) break;
+                if (c > 0 && !wait_all(&ms->x1_full[(c - 1) & 1], ((c - 1) >> 1) & 1)) break;
+                tc_fence_after();
+                uint32_t rr[32], xx[32];
+                tmem_ld32(tmem + lane_base + kColRQ + ((c - 1) & 1) * 32, rr);
+                if (c > 0) tmem_ld32(tmem + lane_base + kColX1 + ((c - 1) & 1) * 32, xx);
+                tmem_ld_wait();
+                const float dec = __expf(g_last - gcs_t);
+                float vt[kSlice];
+#pragma unroll
+                for (int cc = 0; cc < kSlice; ++cc) {
+                    float vn = fmaf(-gam_prev, __uint_as_float(rr[cc]), u[cc]);
+                    if (c > 0) vn -= __uint_as_float(xx[cc]);
+                    u[cc] = vn;
+                    vt[cc] = vn * dec;
+                }
+                // the Vt tile is free once K^T Vt of chunk c-1 is done
+                if (c > 0 && !wait_all(&ms->ds_full[(c - 1) & 1], ((c - 1) >> 1) & 1)) break;
+                put_row(sVn, row, u);
+                put_row(sVt, row, vt);
+                fence_proxy_async_smem();
+                tc_fence_before();
+                mbar_arrive(&ms->v_ready);
+                gam_prev = __expf(g_last);
+            }
         }
     }
 
     tc_fence_before();
     __syncthreads();
-    if (warp == kWarpMma) {
+    if (warp == kWarpMmaA) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }
@@ -799,7 +932,8 @@ int launch(const void* q, const void* k, const void* v, const float* g_log, cons
     uint8_t* wsb = static_cast<uint8_t*>(ws);
     if ((rc = make_tmap_3d(&tw, wsb + L.w, dt, 2, kD, kC, nbhc, 64, kC, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
     if ((rc = make_tmap_3d(&ta, wsb + L.aqk, dt, 2, kC, kC, nbhc, 64, kC, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
-    CUtensorMap tu, tus;
+    CUtensorMap tu, tus, tm;
+    if ((rc = make_tmap_3d(&tm, wsb + L.m, dt, 2, kC, kC, nbhc, 64, kC, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
     if ((rc = make_tmap_3d(&tu, wsb + L.u, dt, 2, kD, kC, nbhc, 64, kC, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
     if ((rc = make_tmap_3d(&tus, wsb + L.u, dt, 2, kD, kC, nbhc, kSlice, kC, CU_TENSOR_MAP_SWIZZLE_64B)))
         return rc;
@@ -818,14 +952,13 @@ int launch(const void* q, const void* k, const void* v, const float* g_log, cons
     pp.head_map = head_map;
     auto k1 = gdn_prep_kernel<T16>;
     B200_TRY_CUDA(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, prep::kAlloc));
-    k1<<<dim3(nch, Hv, B), prep::kThreads, prep::kAlloc, stream>>>(tq, tk, tv, tw, tu, ta, pp);
+    k1<<<dim3(nch, Hv, B), prep::kThreads, prep::kAlloc, stream>>>(tq, tk, tv, tw, tu, ta, tm, pp);
     B200_TRY_CUDA(cudaGetLastError());
 
     StateParams sp;
     sp.ws = wsb;
     sp.state = state;
     sp.o = o;
-    sp.ws_u = L.u;
     sp.ws_gcs = L.gcs;
     sp.T = T;
     sp.Hqk = Hqk;
@@ -835,7 +968,7 @@ int launch(const void* q, const void* k, const void* v, const float* g_log, cons
     sp.scale = scale;
     auto k2 = gdn_state_kernel<T16, TOut>;
     B200_TRY_CUDA(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, st::kAlloc));
-    k2<<<dim3(kD / kSlice, Hv, B), st::kThreads, st::kAlloc, stream>>>(tq, tk, tw, ta, tus, sp);
+    k2<<<dim3(kD / kSlice, Hv, B), st::kThreads, st::kAlloc, stream>>>(tq, tk, tw, ta, tm, tus, sp);
     count_launch(2);
     return cudaGetLastError() == cudaSuccess ? B200LAB_OK : B200LAB_ERR_CUDA;
 }
