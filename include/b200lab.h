@@ -108,8 +108,8 @@ size_t gdn_prefill_sm100_workspace(int B, int T, int Hqk, int Hv, int dk, int dv
  * (64 MiB) that every GPU loading the prefill kernels holds until the process
  * exits.  A problem whose gdn_prefill_sm100_workspace() exceeds that size is
  * rejected with B200LAB_ERR_WORKSPACE before anything is launched (about
- * 41 KB per (sequence, v-head, 64-token chunk): B*Hv*ceil(T/64) <= 1628,
- * e.g. Hv=48 up to T=2048, Hv=32 up to T=3200).
+ * 49 KB per (sequence, v-head, 64-token chunk): B*Hv*ceil(T/64) <= 1358,
+ * e.g. Hv=48 up to T=1792, Hv=32 up to T=2688).
  * The first call on a device looks up the array's device address (with that
  * device current) and caches it; make that first call before any stream
  * capture.  All calls on a device share the one array, so calls that overlap
