@@ -468,6 +468,25 @@ def cpu_gdn_prefill(cfg, threads=0):
             "kind": "port", "sample": f"full config, fp64 serial recurrence, {dt:.2f} s"}
 
 
+def cpu_ref_gdn_cpu(T=64):
+    """The reference's own fp32 single-thread gdn_cpu (src/gdn_sm75.cu:1078-1106), compiled
+    from its sources into oracle/_ref, timed at its own shape (Hq16 Hv48 d128) and LCG
+    inputs: a second, labelled CPU figure beside the fp64 port."""
+    import oracle
+    if not oracle.ref_gdn_available():
+        return {"status": "oracle/_ref not built"}
+    q, k, v, g, b = oracle.ref_lcg_gdn_inputs(T)
+    Sv, Hq, Hv, _ = oracle.ref_gdn_shape()
+    import numpy as np
+    state = np.zeros((Hv, Sv, Sv), dtype=np.float32)
+    t0 = time.perf_counter()
+    oracle.ref_gdn_run(q, k, v, g, b, state, T, 1 / math.sqrt(Sv))
+    dt = time.perf_counter() - t0
+    return {"value": T / dt, "unit": "tok/s", "cores": 1, "kind": "reference",
+            "sample": f"reference gdn_cpu, T={T} at its own shape Hq{Hq} Hv{Hv} d{Sv}, fp32, "
+                      f"{dt:.3f} s"}
+
+
 def cpu_gdn_decode(cfg, threads=0):
     import numpy as np
     import oracle
@@ -570,6 +589,11 @@ def run_ours(args):
                             secondary[key]["cpu_baseline"] = fn(c)
                         except Exception as e:
                             secondary[key]["cpu_baseline"] = {"status": repr(e)}
+                if "value" in secondary.get("gdn_prefill", {}):
+                    try:
+                        secondary["gdn_prefill"]["cpu_baseline_reference"] = cpu_ref_gdn_cpu()
+                    except Exception as e:
+                        secondary["gdn_prefill"]["cpu_baseline_reference"] = {"status": repr(e)}
             line["secondary"] = secondary
     dist.close()
     return line
