@@ -83,18 +83,22 @@ __device__ __forceinline__ uint32_t sw128_off(int r, int j) {
 namespace prep {
 constexpr int kThreads = 128;
 // shared layout (bytes)
-constexpr int kTiles = 0;          // [K0|Q0|K1|Q1|V0|V1], 8 KiB each (64 tokens x 64 dims)
-constexpr int kK0 = 0, kQ0 = 8192, kK1 = 16384, kQ1 = 24576, kV0 = 32768, kV1 = 40960;
-constexpr int kAT = 49152;         // [T diag(beta Gam); T diag(beta)] 128 x 64, 16 KiB
+// [K0|Q0|K1|Q1], 8 KiB each (64 tokens x 64 dims); V0/V1 are loaded over Q0/Q1 once the
+// first MMA has read Q (so the first TMA wait covers K and Q only)
+constexpr int kTiles = 0;
+constexpr int kK0 = 0, kQ0 = 8192, kK1 = 16384, kQ1 = 24576, kV0 = kQ0, kV1 = kQ1;
+constexpr int kAT = 32768;         // [T diag(beta Gam); T diag(beta)] 128 x 64, 16 KiB
 constexpr int kLd = 68;            // fp32 row pitch of A and T (16-byte aligned, fewer conflicts)
-constexpr int kAs = 65536;         // A, fp32 64 x kLd
-constexpr int kTs = kAs + kC * kLd * 4;   // T = (I + A)^-1, fp32 64 x kLd
-constexpr int kXs = kTs + kC * kLd * 4;   // 32 x 36 fp32 scratch of the block inverse
-constexpr int kMisc = kXs + 32 * 36 * 4;
+constexpr int kAs = 49152;         // A, then T = (I + A)^-1 in place, fp32 64 x kLd
+constexpr int kXs = kAT;           // 32 x 36 fp32 scratch of the block inverse (AT is idle then)
+constexpr int kMisc = kAs + kC * kLd * 4;
 constexpr int kBytes = kMisc + 2048;
 constexpr int kAlloc = kBytes + 1024;
+static_assert(3 * (kAlloc + 1024) <= 233472, "three prep CTAs per SM");
 static_assert(kAlloc <= 232448, "state kernel shared memory above the 227 KiB per-CTA limit");
-constexpr uint32_t kTmemCols = 256;
+// 128 columns: three CTAs per SM fit the 512 TMEM columns without one waiting in
+// tcgen05.alloc for another to exit (W and U are produced one after the other)
+constexpr uint32_t kTmemCols = 128;
 
 struct Misc {
     float gcs[kC];   // natural log units (stored to the workspace)
@@ -102,7 +106,7 @@ struct Misc {
     float beta[kC];
     float colscale[2 * kC];  // [beta Gam | beta], the column scales of T' and T''
     float gprev[kC];         // cumsum of g_log over the previous chunk (for M)
-    uint64_t bar_tma, bar_mma1, bar_mma2, bar_kp, bar_m, drain;
+    uint64_t bar_tma, bar_v, bar_mma1, bar_mma2, bar_kp, bar_m, drain;
     uint32_t tmem_base;
     int abort;
 };
@@ -120,9 +124,11 @@ __device__ __forceinline__ float ex2f(float x) {
 //   T11 = (I + A11)^-1, T22 = (I + A22)^-1      (warp 0 / warp 1: one column per
 //                                                lane, forward substitution)
 //   T21 = -T22 (A21 T11),  T12 = 0              (all 128 threads, 8 outputs each)
-// Result in Ts (fp32, row pitch kLd); X (32 x 32) is scratch.
-__device__ __forceinline__ void lower_unit_inverse(const float* As, float* Ts, float* X, int tid) {
+// In place: T overwrites A (fp32, row pitch kLd; the upper triangle of A is zero and stays
+// so); X (32 x 32) is scratch.
+__device__ __forceinline__ void lower_unit_inverse(float* As, float* X, int tid) {
     using prep::kLd;
+    float* Ts = As;
     if (tid < 64) {
         const int o = (tid >> 5) * 32;  // diagonal block origin
         const int j = tid & 31;         // column within the block
@@ -153,12 +159,9 @@ __device__ __forceinline__ void lower_unit_inverse(const float* As, float* Ts, f
                 col[t] = t < j ? 0.f : (t == j ? 1.f : -x);
             }
         }
+        __syncwarp();  // every lane has read its block of A before any column is replaced
 #pragma unroll
         for (int t = 0; t < 32; ++t) Ts[(o + t) * kLd + o + j] = col[t];
-        if (o == 0) {
-#pragma unroll
-            for (int t = 0; t < 32; ++t) Ts[t * kLd + 32 + j] = 0.f;  // T12 = 0
-        }
     }
     __syncthreads();
     // 128 threads x 8 outputs: row r = tid / 4, columns c0 .. c0 + 7 with c0 = (tid % 4) * 8
@@ -202,7 +205,7 @@ __device__ __forceinline__ void lower_unit_inverse(const float* As, float* Ts, f
 }
 
 template <typename T16>
-__global__ void __launch_bounds__(prep::kThreads, 2)
+__global__ void __launch_bounds__(prep::kThreads, 3)
     gdn_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmW,
                     const __grid_constant__ CUtensorMap tmU, const __grid_constant__ CUtensorMap tmAqk,
@@ -213,7 +216,7 @@ __global__ void __launch_bounds__(prep::kThreads, 2)
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     Misc* ms = reinterpret_cast<Misc*>(smem + kMisc);
     float* As = reinterpret_cast<float*>(smem + kAs);
-    float* Ts = reinterpret_cast<float*>(smem + kTs);
+    const float* Ts = As;  // T replaces A in place
     float* Xs = reinterpret_cast<float*>(smem + kXs);
     volatile int* abort = &ms->abort;
 
@@ -228,6 +231,7 @@ __global__ void __launch_bounds__(prep::kThreads, 2)
 
     if (tid == 0) {
         mbar_init(&ms->bar_tma, 1);
+        mbar_init(&ms->bar_v, 1);
         mbar_init(&ms->bar_mma1, 1);
         mbar_init(&ms->bar_mma2, 1);
         mbar_init(&ms->bar_kp, 1);
@@ -246,13 +250,11 @@ __global__ void __launch_bounds__(prep::kThreads, 2)
     const uint32_t tmem = ms->tmem_base;
 
     if (tid == 0) {
-        mbar_arrive_expect_tx(&ms->bar_tma, 6 * 8192);
+        mbar_arrive_expect_tx(&ms->bar_tma, 4 * 8192);
         tma_load_4d(smem + kK0, &tmK, &ms->bar_tma, 0, hq, t0, b);
         tma_load_4d(smem + kK1, &tmK, &ms->bar_tma, 64, hq, t0, b);
         tma_load_4d(smem + kQ0, &tmQ, &ms->bar_tma, 0, hq, t0, b);
         tma_load_4d(smem + kQ1, &tmQ, &ms->bar_tma, 64, hq, t0, b);
-        tma_load_4d(smem + kV0, &tmV, &ms->bar_tma, 0, h, t0, b);
-        tma_load_4d(smem + kV1, &tmV, &ms->bar_tma, 64, h, t0, b);
     }
     // gates: gcs = inclusive prefix sum of g_log over the chunk (padded tokens: g=0, beta=0)
     if (tid < kC) {
@@ -313,6 +315,12 @@ __global__ void __launch_bounds__(prep::kThreads, 2)
         }
     }
     ok = __all_sync(0xffffffffu, mbar_wait(&ms->bar_mma1, 0, abort, &g_err_gdn_prefill));
+    if (tid == 0 && ok) {
+        // Q has been read: V goes over it (needed only by MMA2, after the solve)
+        mbar_arrive_expect_tx(&ms->bar_v, 2 * 8192);
+        tma_load_4d(smem + kV0, &tmV, &ms->bar_v, 0, h, t0, b);
+        tma_load_4d(smem + kV1, &tmV, &ms->bar_v, 64, h, t0, b);
+    }
     tc_fence_after();
     const int row = (warp & 1) * 32 + lane;  // token within the chunk
     const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
@@ -368,7 +376,7 @@ __global__ void __launch_bounds__(prep::kThreads, 2)
         const int j = tid & 63;
         ms->colscale[tid] = tid < kC ? ms->beta[j] * ex2f(ms->g2[j]) : ms->beta[j];
     }
-    lower_unit_inverse(As, Ts, Xs, tid);  // contains __syncthreads: every thread calls it
+    lower_unit_inverse(As, Xs, tid);  // contains __syncthreads: every thread calls it
     {
         // AT rows 0-63 <- T diag(beta Gam), rows 64-127 <- T diag(beta). Thread = AT row:
         // eight 16-byte swizzled chunks of 8 columns each (conflict-free row reads of Ts,
@@ -395,8 +403,15 @@ __global__ void __launch_bounds__(prep::kThreads, 2)
     tc_fence_before();
     __syncthreads();
 
-    // MMA2: [T'; T''] K  -> cols 0-127, [T'; T''] V -> cols 128-255  (M=128, N=128, K=64);
-    // B operands MN-major: K chunks 16 KiB apart ([K0|Q0|K1|Q1]), V chunks 8 KiB apart
+    // MMA2 in two steps through the same 128 TMEM columns (M=128, N=128, K=64; B operands
+    // MN-major, their two 64-column chunks 16 KiB apart, [K0|V0|K1|V1]):
+    //   [T'; T''] K -> W in lanes 0-63, then [T'; T''] V -> U in lanes 64-127
+    // (the other half of each product is not used).
+    if (tid == 0 && ok) {
+        ok = mbar_wait(&ms->bar_v, 0, abort, &g_err_gdn_prefill);
+    }
+    constexpr uint32_t idesc2 = make_idesc(Elem<T16>::kFmt, 128, 128, false, true);
+    const uint32_t a0 = smem_u32(smem + kAT);
     if (tid == 0 && ok) {
         if (c > 0) {
             // K of the previous chunk into the (now dead) A tile, for M below
@@ -405,31 +420,22 @@ __global__ void __launch_bounds__(prep::kThreads, 2)
             tma_load_4d(smem + kAs + 8192, &tmK, &ms->bar_kp, 64, hq, t0 - kC, b);
         }
         tc_fence_after();
-        constexpr uint32_t idesc = make_idesc(Elem<T16>::kFmt, 128, 128, false, true);
-        const uint32_t a0 = smem_u32(smem + kAT);
         const uint32_t bk = smem_u32(smem + kK0);
-        const uint32_t bv = smem_u32(smem + kV0);
 #pragma unroll
-        for (int kk = 0; kk < kC / 16; ++kk) {
+        for (int kk = 0; kk < kC / 16; ++kk)
             mma_f16_ss(tmem, smem_desc(a0 + kk * 32, 16, 1024, kLayoutSW128),
-                       smem_desc(bk + kk * 2048, 16384, 1024, kLayoutSW128), idesc, kk > 0 ? 1u : 0u);
-            mma_f16_ss(tmem + 128, smem_desc(a0 + kk * 32, 16, 1024, kLayoutSW128),
-                       smem_desc(bv + kk * 2048, 8192, 1024, kLayoutSW128), idesc, kk > 0 ? 1u : 0u);
-        }
+                       smem_desc(bk + kk * 2048, 16384, 1024, kLayoutSW128), idesc2, kk > 0 ? 1u : 0u);
         mma_commit(&ms->bar_mma2);
     }
-    ok = __all_sync(0xffffffffu, mbar_wait(&ms->bar_mma2, 0, abort, &g_err_gdn_prefill)) && ok;
-    tc_fence_after();
-    if (ok) {
-        // warps 0-1: W rows (lanes 0-63, cols 0-127); warps 2-3: U rows (lanes 64-127,
-        // cols 128-255), staged 128B-swizzled over the dead K/Q/V tiles (W at 0, U at 16 KiB,
-        // two 64-column boxes each) for TMA stores
-        const uint32_t col0 = warp < 2 ? 0u : 128u;
-        uint8_t* stg = smem + kTiles + (warp < 2 ? 0 : 16384) + row * 128;
+    // 64 rows x 128 columns of TMEM -> 16-bit, 128B-swizzled as two 64-column boxes 16 KiB
+    // apart, for TMA stores: W over the K boxes (free once the W product is done; V, still
+    // needed by the U product, sits in the other two), U over the V boxes afterwards
+    auto stage_rows = [&](uint8_t* base) {
+        uint8_t* stg = base + row * 128;
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc) {
             uint32_t v[32];
-            tmem_ld32(tmem + lane_base + col0 + cc * 32, v);
+            tmem_ld32(tmem + lane_base + cc * 32, v);
             tmem_ld_wait();
 #pragma unroll
             for (int q8 = 0; q8 < 4; ++q8) {
@@ -439,35 +445,54 @@ __global__ void __launch_bounds__(prep::kThreads, 2)
                 pk.z = Elem<T16>::pack2(__uint_as_float(v[q8 * 8 + 4]), __uint_as_float(v[q8 * 8 + 5]));
                 pk.w = Elem<T16>::pack2(__uint_as_float(v[q8 * 8 + 6]), __uint_as_float(v[q8 * 8 + 7]));
                 const int q = cc * 4 + q8;  // 16-byte chunk 0..15 of the 256-byte row
-                *reinterpret_cast<uint4*>(stg + (q >> 3) * 8192 + (((q & 7) ^ (row & 7)) << 4)) = pk;
+                *reinterpret_cast<uint4*>(stg + (q >> 3) * 16384 + (((q & 7) ^ (row & 7)) << 4)) = pk;
             }
         }
         fence_proxy_async_smem();
-        if (warp < 2)
-            reinterpret_cast<float*>(p.ws + p.ws_gcs)[bhc * kC + row] = gcs_r;
+    };
+    ok = __all_sync(0xffffffffu, mbar_wait(&ms->bar_mma2, 0, abort, &g_err_gdn_prefill)) && ok;
+    tc_fence_after();
+    if (ok && warp < 2) {
+        stage_rows(smem + kK0);  // W -> [K0 | . | K1 | .]
+        reinterpret_cast<float*>(p.ws + p.ws_gcs)[bhc * kC + row] = gcs_r;
     }
+    tc_fence_before();
+    __syncthreads();  // W is out of TMEM
+    if (tid == 0 && ok) {
+        tc_fence_after();
+        const uint32_t bv = smem_u32(smem + kV0);
+#pragma unroll
+        for (int kk = 0; kk < kC / 16; ++kk)
+            mma_f16_ss(tmem, smem_desc(a0 + kk * 32, 16, 1024, kLayoutSW128),
+                       smem_desc(bv + kk * 2048, 16384, 1024, kLayoutSW128), idesc2, kk > 0 ? 1u : 0u);
+        mma_commit(&ms->bar_mma2);
+    }
+    ok = __all_sync(0xffffffffu, mbar_wait(&ms->bar_mma2, 1, abort, &g_err_gdn_prefill)) && ok;
+    tc_fence_after();
+    if (ok && warp >= 2) stage_rows(smem + kV0);  // U -> [. | V0 | . | V1]
     tc_fence_before();
     __syncthreads();
     if (tid == 0 && ok) {
-        tma_store_3d(&tmW, smem + kTiles, 0, 0, (int)bhc);
-        tma_store_3d(&tmW, smem + kTiles + 8192, 64, 0, (int)bhc);
-        tma_store_3d(&tmU, smem + kTiles + 16384, 0, 0, (int)bhc);
-        tma_store_3d(&tmU, smem + kTiles + 24576, 64, 0, (int)bhc);
+        tma_store_3d(&tmW, smem + kK0, 0, 0, (int)bhc);
+        tma_store_3d(&tmW, smem + kK1, 64, 0, (int)bhc);
+        tma_store_3d(&tmU, smem + kV0, 0, 0, (int)bhc);
+        tma_store_3d(&tmU, smem + kV1, 64, 0, (int)bhc);
         bulk_commit();
         // M = W K_prev^T (M=128, N=64, K=128): A = the staged W (K-major, its two
-        // 64-column boxes 8 KiB apart; rows 64-127 of the product are not used),
+        // 64-column boxes 16 KiB apart; rows 64-127 of the product are not used),
         // B = K of the previous chunk.  Result in TMEM cols 0-63, lanes 0-63.
         if (c > 0) {
             ok = mbar_wait(&ms->bar_kp, 0, abort, &g_err_gdn_prefill);
             if (ok) {
                 tc_fence_after();
                 constexpr uint32_t idesc = make_idesc(Elem<T16>::kFmt, 128, 64, false, false);
-                const uint64_t dw = smem_desc(smem_u32(smem + kTiles), 16, 1024, kLayoutSW128);
+                const uint64_t dw = smem_desc(smem_u32(smem + kK0), 16, 1024, kLayoutSW128);
                 const uint64_t dk = smem_desc(smem_u32(smem + kAs), 16, 1024, kLayoutSW128);
 #pragma unroll
                 for (int kk = 0; kk < kD / 16; ++kk) {
-                    const uint32_t off = ((kk >> 2) * 8192 + (kk & 3) * 32) >> 4;
-                    mma_f16_ss(tmem, dw + off, dk + off, idesc, kk > 0 ? 1u : 0u);
+                    const uint32_t offw = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
+                    const uint32_t offk = ((kk >> 2) * 8192 + (kk & 3) * 32) >> 4;
+                    mma_f16_ss(tmem, dw + offw, dk + offk, idesc, kk > 0 ? 1u : 0u);
                 }
                 mma_commit(&ms->bar_m);
             }
@@ -508,7 +533,7 @@ __global__ void __launch_bounds__(prep::kThreads, 2)
     if (tid == 0 && ok) {
         tma_store_3d(&tmM, smem + kAT, 0, 0, (int)bhc);
         bulk_commit();
-        bulk_wait_all();
+        bulk_wait_all();   // the next kernel reads W, U, Aqk, M
     }
     if (tid == 0) {
         mma_commit(&ms->drain);
