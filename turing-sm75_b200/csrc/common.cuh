@@ -121,6 +121,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 }
 
 // ---- TMA -----------------------------------------------------------------
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialisation may start while the previous kernel in the stream drains; it must
+// call grid_dependency_wait() before reading anything that kernel wrote.  The
+// previous kernel lets it start early with allow_dependent_launch().
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void allow_dependent_launch() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Untiled bulk copy global -> this CTA's shared memory (16-byte aligned, size a
 // multiple of 16), completion signalled on `bar`.  No cluster multicast.
 __device__ __forceinline__ void bulk_load_1d(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {

@@ -228,6 +228,9 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
     const size_t bhc = ((size_t)b * p.Hv + h) * p.nch + c;
+    // the state pass may be scheduled once every prep CTA is running; it waits for this
+    // grid's results itself (grid_dependency_wait)
+    allow_dependent_launch();
 
     if (tid == 0) {
         mbar_init(&ms->bar_tma, 1);
@@ -695,6 +698,7 @@ __global__ void __launch_bounds__(st::kThreads, 1)
         if (lane == 0) {
             const float* gcs_all = reinterpret_cast<const float*>(p.ws + p.ws_gcs);
             const int bhc0 = (int)(bh * p.nch);
+            grid_dependency_wait();  // W, U, Aqk, M, gcs come from the prep grid
             // prologue: W_0 into the W rows of stage 2's A1 tile
             uint8_t* pro = smem + (kStages - 1) * kStage + kA1;
             mbar_arrive_expect_tx(&ms->pro_full, 2 * 8192);
@@ -800,6 +804,7 @@ __global__ void __launch_bounds__(st::kThreads, 1)
         const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
         const float* gcs_all = reinterpret_cast<const float*>(p.ws + p.ws_gcs);
         const size_t bhc0 = bh * p.nch;
+        if (warp >= kWarpOut) grid_dependency_wait();  // gcs comes from the prep grid
         auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
             return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, &g_err_gdn_prefill));
         };
@@ -822,6 +827,7 @@ __global__ void __launch_bounds__(st::kThreads, 1)
             float* Sg = p.state + (bh * kD + c0) * kD + i;
 #pragma unroll
             for (int cc = 0; cc < kSlice; ++cc) S[cc] = Sg[(size_t)cc * kD];
+            grid_dependency_wait();  // (the state itself is an input, not a prep result)
             uint8_t* sS = smem + kSt;
             // S (16-bit) -> shared (B operand of the RQ product), then S_c is announced
             auto publish_S = [&](int c) {
@@ -993,7 +999,19 @@ int launch(const void* q, const void* k, const void* v, const float* g_log, cons
     sp.scale = scale;
     auto k2 = gdn_state_kernel<T16, TOut>;
     B200_TRY_CUDA(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, st::kAlloc));
-    k2<<<dim3(kD / kSlice, Hv, B), st::kThreads, st::kAlloc, stream>>>(tq, tk, tw, ta, tm, tus, sp);
+    // launched with programmatic stream serialisation: its prologue (barriers, TMEM, the
+    // initial state) overlaps the prep grid's last CTAs
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kD / kSlice, Hv, B);
+    cfg.blockDim = dim3(st::kThreads);
+    cfg.dynamicSmemBytes = st::kAlloc;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    B200_TRY_CUDA(cudaLaunchKernelEx(&cfg, k2, tq, tk, tw, ta, tm, tus, sp));
     count_launch(2);
     return cudaGetLastError() == cudaSuccess ? B200LAB_OK : B200LAB_ERR_CUDA;
 }
