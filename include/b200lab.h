@@ -135,6 +135,21 @@ int gdn_decode_sm100(const void* q, const void* k, const void* v,
                      int B, int Hqk, int Hv, int dk, int dv, int head_map,
                      float scale, int in_dtype, int out_dtype, void* stream);
 
+/* The same decode step with a 16-bit recurrent state in HBM (state_dtype
+ * B200LAB_F16 or B200LAB_BF16; [B][Hv][dv][dk], 8-byte aligned, updated in
+ * place): half the bytes of the fp32 step, which is bound by them.  The
+ * update is done in fp32 registers and rounded once per step on the store.
+ * No C entry of the reference corresponds; the reference's own kernels keep
+ * the state in fp16 within a launch (gdn_smem_kernel, src/gdn_sm75.cu:95-133;
+ * gdn_wmma_kernel, src/gdn_sm75.cu:378, 543-573), which is the precision
+ * precedent.  fp16 keeps 3 more mantissa bits than bf16: prefer it unless the
+ * state can exceed 65504 in magnitude. */
+int gdn_decode_sm100_state16(const void* q, const void* k, const void* v,
+                             const float* g_log, const float* beta, void* state,
+                             int state_dtype, void* o, int B, int Hqk, int Hv, int dk,
+                             int dv, int head_map, float scale, int in_dtype,
+                             int out_dtype, void* stream);
+
 /* ---- utilities ----------------------------------------------------------- */
 /* Message for a status code (static storage). */
 const char* b200lab_strerror(int status);

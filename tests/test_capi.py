@@ -57,3 +57,17 @@ def test_shape_rules_rejected_before_launch():
     # decode: dk != 128, head_map 1 with Hv % Hqk != 0
     assert L.gdn_decode_sm100(p, p, p, p, p, p, p, 1, 1, 1, 64, 64, 0, 0.1, 1, 1, n) == b200lab.ERR_UNSUPPORTED
     assert L.gdn_decode_sm100(p, p, p, p, p, p, p, 1, 3, 4, 128, 128, 1, 0.1, 1, 1, n) == b200lab.ERR_INVALID
+
+
+def test_state16_decode_rules_rejected_before_launch():
+    L = b200lab.lib()
+    p = ctypes.c_void_p(16)  # never dereferenced: validation fails first
+    n = ctypes.c_void_p(0)
+    f = L.gdn_decode_sm100_state16
+    # null pointers, an fp32 state dtype (that is gdn_decode_sm100), dk != 128
+    assert f(n, n, n, n, n, n, b200lab.F16, n, 1, 1, 1, 128, 128, 0, 0.1, 1, 1, n) == b200lab.ERR_INVALID
+    assert f(p, p, p, p, p, p, b200lab.F32, p, 1, 1, 1, 128, 128, 0, 0.1, 1, 1, n) == b200lab.ERR_INVALID
+    assert f(p, p, p, p, p, p, b200lab.BF16, p, 1, 1, 1, 64, 64, 0, 0.1, 1, 1, n) == b200lab.ERR_UNSUPPORTED
+    # state not 8-byte aligned
+    odd = ctypes.c_void_p(20)
+    assert f(p, p, p, p, p, odd, b200lab.F16, p, 1, 1, 1, 128, 128, 0, 0.1, 1, 1, n) == b200lab.ERR_INVALID

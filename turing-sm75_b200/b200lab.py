@@ -34,7 +34,7 @@ F16, BF16, F32 = 0, 1, 2
 EXPORTED = (
     "attn_fwd_sm100", "attn_fwd_sm100_workspace",
     "gdn_prefill_sm100", "gdn_prefill_sm100_workspace", "gdn_prefill_sm100_noalloc",
-    "gdn_decode_sm100",
+    "gdn_decode_sm100", "gdn_decode_sm100_state16",
     "b200lab_strerror", "b200lab_device_status", "b200lab_version", "b200lab_launch_count",
 )
 
@@ -75,6 +75,8 @@ def lib() -> ctypes.CDLL:
         L.gdn_prefill_sm100_noalloc.argtypes = [vp] * 7 + [ci] * 7 + [cf, ci, ci, vp]
         L.gdn_decode_sm100.restype = ci
         L.gdn_decode_sm100.argtypes = [vp] * 7 + [ci] * 6 + [cf, ci, ci, vp]
+        L.gdn_decode_sm100_state16.restype = ci
+        L.gdn_decode_sm100_state16.argtypes = [vp] * 6 + [ci, vp] + [ci] * 6 + [cf, ci, ci, vp]
         L.b200lab_strerror.restype = ctypes.c_char_p
         L.b200lab_strerror.argtypes = [ci]
         L.b200lab_device_status.restype = ci
@@ -190,7 +192,8 @@ def gdn_prefill(q, k, v, g_log, beta, state, *, scale: float | None = None, head
 def gdn_decode(q, k, v, g_log, beta, state, *, scale: float | None = None, head_map: int = 0,
                out=None, out_dtype=None, stream=None):
     """One Gated DeltaNet decode step.  q,k [B,Hqk,dk]; v [B,Hv,dv]; g_log,beta [B,Hv] fp32;
-    state [B,Hv,dv,dk] fp32 (in place).  Returns o [B,Hv,dv]."""
+    state [B,Hv,dv,dk] fp32, or fp16/bf16 for the 16-bit-state entry (in place).
+    Returns o [B,Hv,dv]."""
     torch = _torch()
     B, Hqk, dk = q.shape
     Hv, dv = v.shape[1], v.shape[2]
@@ -198,11 +201,20 @@ def gdn_decode(q, k, v, g_log, beta, state, *, scale: float | None = None, head_
         scale = 1.0 / (dk ** 0.5)
     if out is None:
         out = torch.empty((B, Hv, dv), dtype=out_dtype or q.dtype, device=q.device)
-    st = lib().gdn_decode_sm100(_dev(q, "q"), _dev(k, "k"), _dev(v, "v"), _dev(g_log, "g_log"),
-                                _dev(beta, "beta"), _dev(state, "state"), _dev(out, "out"),
-                                B, Hqk, Hv, dk, dv, int(head_map), float(scale),
-                                _dtype_code(q), _dtype_code(out), _stream(stream))
-    _check(st, "gdn_decode_sm100")
+    if state.dtype == torch.float32:
+        st = lib().gdn_decode_sm100(_dev(q, "q"), _dev(k, "k"), _dev(v, "v"), _dev(g_log, "g_log"),
+                                    _dev(beta, "beta"), _dev(state, "state"), _dev(out, "out"),
+                                    B, Hqk, Hv, dk, dv, int(head_map), float(scale),
+                                    _dtype_code(q), _dtype_code(out), _stream(stream))
+        _check(st, "gdn_decode_sm100")
+    else:
+        # 16-bit state (fp16 / bf16): gdn_decode_sm100_state16
+        st = lib().gdn_decode_sm100_state16(_dev(q, "q"), _dev(k, "k"), _dev(v, "v"),
+                                            _dev(g_log, "g_log"), _dev(beta, "beta"),
+                                            _dev(state, "state"), _dtype_code(state), _dev(out, "out"),
+                                            B, Hqk, Hv, dk, dv, int(head_map), float(scale),
+                                            _dtype_code(q), _dtype_code(out), _stream(stream))
+        _check(st, "gdn_decode_sm100_state16")
     return out
 
 

@@ -91,6 +91,12 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float y;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(y) : "f"(a), "f"(b), "f"(c));
+    return y;
+}
+
 // 2^x for a pair of values on the FMA pipe (packed f32x2 ops), so that a quarter of
 // the exponentials leave the MUFU pipe (4 lanes a clock per SM sub-partition), which
 // otherwise bounds the softmax.  x = n + f by round-to-nearest through the 1.5*2^23
@@ -321,24 +327,21 @@ __global__ void __launch_bounds__(kThreads, 1)
 
             const int k0 = (j0 + j) * BN;
             const bool need_mask = k0 + BN - 1 > key_lim;
-            // row max as 8 independent chains
+            if (need_mask) {
+#pragma unroll
+                for (int c = 0; c < BN; ++c)
+                    if (k0 + c > key_lim) sr[c] = __float_as_uint(-INFINITY);
+            }
+            // row max: three-input max, eight independent chains (8 deep)
             float mx[8];
 #pragma unroll
             for (int u = 0; u < 8; ++u) mx[u] = -INFINITY;
-            if (need_mask) {
 #pragma unroll
-                for (int c = 0; c < BN; ++c) {
-                    float s = __uint_as_float(sr[c]);
-                    if (k0 + c > key_lim) s = -INFINITY;
-                    sr[c] = __float_as_uint(s);
-                    mx[c & 7] = fmaxf(mx[c & 7], s);
-                }
-            } else {
+            for (int c = 0; c < BN; c += 16)
 #pragma unroll
-                for (int c = 0; c < BN; ++c) mx[c & 7] = fmaxf(mx[c & 7], __uint_as_float(sr[c]));
-            }
-            const float smax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                     fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+                for (int u = 0; u < 8; ++u)
+                    mx[u] = fmax3(mx[u], __uint_as_float(sr[c + 2 * u]), __uint_as_float(sr[c + 2 * u + 1]));
+            const float smax = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
             const float mt = smax * sl2;
             float alpha = 1.f;
             bool rescale = false;

@@ -24,12 +24,18 @@ namespace {
 __device__ int g_err_gdn_decode = 0;
 
 constexpr int kD = 128;           // dk = dv
-constexpr int kRowsPerWarp = 8;   // 8 warps x 8 rows = 64 rows: half a (b, h) per CTA
-constexpr int kCtasPerHead = kD / (kRowsPerWarp * 8);
 constexpr int kThreads = 256;
+// fp32 state: 8 warps x 8 rows = 64 rows, half a (b, h) per CTA; a 16-bit state keeps
+// the same bytes in flight per warp with 16 rows a warp, a whole (b, h) per CTA
+template <typename TS>
+struct Rows {
+    static constexpr int kPerWarp = sizeof(TS) == 4 ? 8 : 16;
+    static constexpr int kCtasPerHead = kD / (kPerWarp * 8);
+};
 
-// Streaming 128-bit load / store.  asm volatile keeps the 16 row loads of a
-// warp issued back to back, ahead of the first reduction that consumes them.
+// Streaming loads / stores of four state entries (one lane's share of a row): 128-bit
+// for an fp32 state, 64-bit for a 16-bit one.  asm volatile keeps a warp's row loads
+// issued back to back, ahead of the first reduction that consumes them.
 __device__ __forceinline__ float4 ld_stream(const float* p) {
     float4 v;
     asm volatile("ld.global.cs.v4.f32 {%0, %1, %2, %3}, [%4];"
@@ -41,6 +47,20 @@ __device__ __forceinline__ void st_stream(float* p, float4 v) {
     asm volatile("st.global.cs.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(v.x), "f"(v.y),
                  "f"(v.z), "f"(v.w)
                  : "memory");
+}
+template <typename TS>
+__device__ __forceinline__ float4 ld_stream(const TS* p) {
+    uint32_t a, b;
+    asm volatile("ld.global.cs.v2.b32 {%0, %1}, [%2];" : "=r"(a), "=r"(b) : "l"(p));
+    const TS* e0 = reinterpret_cast<const TS*>(&a);
+    const TS* e1 = reinterpret_cast<const TS*>(&b);
+    return make_float4(Elem<TS>::to_f(e0[0]), Elem<TS>::to_f(e0[1]), Elem<TS>::to_f(e1[0]),
+                       Elem<TS>::to_f(e1[1]));
+}
+template <typename TS>
+__device__ __forceinline__ void st_stream(TS* p, float4 v) {
+    const uint32_t a = Elem<TS>::pack2(v.x, v.y), b = Elem<TS>::pack2(v.z, v.w);
+    asm volatile("st.global.cs.v2.b32 [%0], {%1, %2};" ::"l"(p), "r"(a), "r"(b) : "memory");
 }
 
 __device__ __forceinline__ float warp_sum(float x) {
@@ -61,11 +81,13 @@ __device__ __forceinline__ float4 load4(const T* p) {
     }
 }
 
-template <typename TIn, typename TOut>
+template <typename TIn, typename TOut, typename TS>
 __global__ void __launch_bounds__(kThreads) gdn_decode_kernel(
     const TIn* __restrict__ q, const TIn* __restrict__ k, const TIn* __restrict__ v,
-    const float* __restrict__ g_log, const float* __restrict__ beta, float* __restrict__ state,
+    const float* __restrict__ g_log, const float* __restrict__ beta, TS* __restrict__ state,
     TOut* __restrict__ o, int Hqk, int Hv, int head_map, float scale) {
+    constexpr int kRowsPerWarp = Rows<TS>::kPerWarp;
+    constexpr int kCtasPerHead = Rows<TS>::kCtasPerHead;
     const int bh = blockIdx.x / kCtasPerHead;  // b * Hv + h
     const int b = bh / Hv;
     const int h = bh - b * Hv;
@@ -74,7 +96,7 @@ __global__ void __launch_bounds__(kThreads) gdn_decode_kernel(
     const int lane = threadIdx.x & 31;
     const int row0 = (blockIdx.x % kCtasPerHead) * (kRowsPerWarp * 8) + warp * kRowsPerWarp;
 
-    float* S = state + (size_t)bh * kD * kD + (size_t)row0 * kD + 4 * lane;
+    TS* S = state + (size_t)bh * kD * kD + (size_t)row0 * kD + 4 * lane;
     float4 s[kRowsPerWarp];
 #pragma unroll
     for (int r = 0; r < kRowsPerWarp; ++r) s[r] = ld_stream(S + r * kD);
@@ -85,6 +107,7 @@ __global__ void __launch_bounds__(kThreads) gdn_decode_kernel(
     const float g = expf(g_log[bh]);
     const float be = beta[bh];
     const float vr = lane < kRowsPerWarp ? Elem<TIn>::to_f(v[(size_t)bh * kD + row0 + lane]) : 0.f;
+    static_assert(kRowsPerWarp <= 32, "one v entry per lane");
 
     float out = 0.f;
 #pragma unroll
@@ -105,31 +128,63 @@ __global__ void __launch_bounds__(kThreads) gdn_decode_kernel(
     if (lane < kRowsPerWarp) o[(size_t)bh * kD + row0 + lane] = Elem<TOut>::from_f(out);
 }
 
-template <typename TIn, typename TOut>
+template <typename TIn, typename TOut, typename TS>
 int launch(const void* q, const void* k, const void* v, const float* g_log, const float* beta,
-           float* state, void* o, int B, int Hqk, int Hv, int head_map, float scale,
+           void* state, void* o, int B, int Hqk, int Hv, int head_map, float scale,
            cudaStream_t st) {
-    gdn_decode_kernel<TIn, TOut><<<B * Hv * kCtasPerHead, kThreads, 0, st>>>(
+    gdn_decode_kernel<TIn, TOut, TS><<<B * Hv * Rows<TS>::kCtasPerHead, kThreads, 0, st>>>(
         static_cast<const TIn*>(q), static_cast<const TIn*>(k), static_cast<const TIn*>(v),
-        g_log, beta, state, static_cast<TOut*>(o), Hqk, Hv, head_map, scale);
+        g_log, beta, static_cast<TS*>(state), static_cast<TOut*>(o), Hqk, Hv, head_map, scale);
     count_launch(1);
     return cudaGetLastError() == cudaSuccess ? B200LAB_OK : B200LAB_ERR_CUDA;
 }
 
-template <typename TIn>
+template <typename TIn, typename TS>
 int dispatch_out(int out_dtype, const void* q, const void* k, const void* v, const float* g_log,
-                 const float* beta, float* state, void* o, int B, int Hqk, int Hv, int head_map,
+                 const float* beta, void* state, void* o, int B, int Hqk, int Hv, int head_map,
                  float scale, cudaStream_t st) {
     switch (out_dtype) {
         case B200LAB_F16:
-            return launch<TIn, __half>(q, k, v, g_log, beta, state, o, B, Hqk, Hv, head_map, scale, st);
+            return launch<TIn, __half, TS>(q, k, v, g_log, beta, state, o, B, Hqk, Hv, head_map, scale, st);
         case B200LAB_BF16:
-            return launch<TIn, __nv_bfloat16>(q, k, v, g_log, beta, state, o, B, Hqk, Hv, head_map,
-                                              scale, st);
+            return launch<TIn, __nv_bfloat16, TS>(q, k, v, g_log, beta, state, o, B, Hqk, Hv, head_map,
+                                                  scale, st);
         case B200LAB_F32:
-            return launch<TIn, float>(q, k, v, g_log, beta, state, o, B, Hqk, Hv, head_map, scale, st);
+            return launch<TIn, float, TS>(q, k, v, g_log, beta, state, o, B, Hqk, Hv, head_map, scale, st);
     }
     return B200LAB_ERR_UNSUPPORTED;
+}
+
+template <typename TS>
+int dispatch_in(int in_dtype, int out_dtype, const void* q, const void* k, const void* v,
+                const float* g_log, const float* beta, void* state, void* o, int B, int Hqk, int Hv,
+                int head_map, float scale, cudaStream_t st) {
+    switch (in_dtype) {
+        case B200LAB_F16:
+            return dispatch_out<__half, TS>(out_dtype, q, k, v, g_log, beta, state, o, B, Hqk, Hv,
+                                            head_map, scale, st);
+        case B200LAB_BF16:
+            return dispatch_out<__nv_bfloat16, TS>(out_dtype, q, k, v, g_log, beta, state, o, B, Hqk,
+                                                   Hv, head_map, scale, st);
+        default:
+            return dispatch_out<float, TS>(out_dtype, q, k, v, g_log, beta, state, o, B, Hqk, Hv,
+                                           head_map, scale, st);
+    }
+}
+
+// argument checks shared by both entries (state alignment checked by the caller)
+int check_args(const void* q, const void* k, const void* v, const float* g_log, const float* beta,
+               const void* state, const void* o, int B, int Hqk, int Hv, int dk, int dv, int head_map,
+               int in_dtype, int out_dtype) {
+    if (!q || !k || !v || !g_log || !beta || !state || !o) return B200LAB_ERR_INVALID;
+    if (B < 1 || Hqk < 1 || Hv < 1 || dk < 1 || dv < 1) return B200LAB_ERR_INVALID;
+    if (head_map != 0 && head_map != 1) return B200LAB_ERR_INVALID;
+    if (head_map == 1 && Hv % Hqk != 0) return B200LAB_ERR_INVALID;
+    if (in_dtype < B200LAB_F16 || in_dtype > B200LAB_F32) return B200LAB_ERR_INVALID;
+    if (out_dtype < B200LAB_F16 || out_dtype > B200LAB_F32) return B200LAB_ERR_INVALID;
+    if (dk != 128 || dv != 128) return B200LAB_ERR_UNSUPPORTED;
+    if ((long long)B * Hv > 0x7fffffffLL) return B200LAB_ERR_UNSUPPORTED;
+    return B200LAB_OK;
 }
 
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
@@ -144,29 +199,35 @@ extern "C" int gdn_decode_sm100(const void* q, const void* k, const void* v, con
                                 int dk, int dv, int head_map, float scale, int in_dtype,
                                 int out_dtype, void* stream) {
     using namespace b200;
-    if (!q || !k || !v || !g_log || !beta || !state || !o) return B200LAB_ERR_INVALID;
-    if (B < 1 || Hqk < 1 || Hv < 1 || dk < 1 || dv < 1) return B200LAB_ERR_INVALID;
-    if (head_map != 0 && head_map != 1) return B200LAB_ERR_INVALID;
-    if (head_map == 1 && Hv % Hqk != 0) return B200LAB_ERR_INVALID;
-    if (in_dtype < B200LAB_F16 || in_dtype > B200LAB_F32) return B200LAB_ERR_INVALID;
-    if (out_dtype < B200LAB_F16 || out_dtype > B200LAB_F32) return B200LAB_ERR_INVALID;
-    if (dk != 128 || dv != 128) return B200LAB_ERR_UNSUPPORTED;
-    if ((long long)B * Hv > 0x7fffffffLL) return B200LAB_ERR_UNSUPPORTED;
+    int rc = check_args(q, k, v, g_log, beta, state, o, B, Hqk, Hv, dk, dv, head_map, in_dtype, out_dtype);
+    if (rc != B200LAB_OK) return rc;
     const uintptr_t in_align = in_dtype == B200LAB_F32 ? 16 : 8;
     if (!aligned(q, in_align) || !aligned(k, in_align) || !aligned(state, 16))
         return B200LAB_ERR_INVALID;
-    int rc = check_device_sm100();
+    rc = check_device_sm100();
+    if (rc != B200LAB_OK) return rc;
+    return dispatch_in<float>(in_dtype, out_dtype, q, k, v, g_log, beta, state, o, B, Hqk, Hv, head_map,
+                              scale, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int gdn_decode_sm100_state16(const void* q, const void* k, const void* v,
+                                        const float* g_log, const float* beta, void* state,
+                                        int state_dtype, void* o, int B, int Hqk, int Hv, int dk,
+                                        int dv, int head_map, float scale, int in_dtype,
+                                        int out_dtype, void* stream) {
+    using namespace b200;
+    int rc = check_args(q, k, v, g_log, beta, state, o, B, Hqk, Hv, dk, dv, head_map, in_dtype, out_dtype);
+    if (rc != B200LAB_OK) return rc;
+    if (state_dtype != B200LAB_F16 && state_dtype != B200LAB_BF16) return B200LAB_ERR_INVALID;
+    const uintptr_t in_align = in_dtype == B200LAB_F32 ? 16 : 8;
+    if (!aligned(q, in_align) || !aligned(k, in_align) || !aligned(state, 8))
+        return B200LAB_ERR_INVALID;
+    rc = check_device_sm100();
     if (rc != B200LAB_OK) return rc;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    switch (in_dtype) {
-        case B200LAB_F16:
-            return dispatch_out<__half>(out_dtype, q, k, v, g_log, beta, state, o, B, Hqk, Hv,
-                                        head_map, scale, st);
-        case B200LAB_BF16:
-            return dispatch_out<__nv_bfloat16>(out_dtype, q, k, v, g_log, beta, state, o, B, Hqk, Hv,
-                                               head_map, scale, st);
-        default:
-            return dispatch_out<float>(out_dtype, q, k, v, g_log, beta, state, o, B, Hqk, Hv,
-                                       head_map, scale, st);
-    }
+    return state_dtype == B200LAB_F16
+               ? dispatch_in<__half>(in_dtype, out_dtype, q, k, v, g_log, beta, state, o, B, Hqk, Hv,
+                                     head_map, scale, st)
+               : dispatch_in<__nv_bfloat16>(in_dtype, out_dtype, q, k, v, g_log, beta, state, o, B,
+                                            Hqk, Hv, head_map, scale, st);
 }
