@@ -304,7 +304,9 @@ def bench_attention(name, cfg, args, dist, peaks):
     return res
 
 
-def bench_gdn_decode(cfg, args, dist, peaks):
+def bench_gdn_decode(cfg, args, dist, peaks, state_dtype=None):
+    """GDN decode over the config's 256 steps; state_dtype fp16/bf16 runs the 16-bit-state
+    entry (gdn_decode_sm100_state16), default the fp32 state."""
     import torch
     import b200lab
     import workloads
@@ -314,12 +316,15 @@ def bench_gdn_decode(cfg, args, dist, peaks):
     dtype = cfg["dtype"]
     dev = torch.device("cuda", dist.local)
     state = workloads.gdn_state(Bl, Hv, d, std=0.02, seed=3 + dist.rank, device=dev)
+    sdt = state_dtype or torch.float32
+    state = state.to(sdt)
+    ssz = state.element_size()
     steps_in = [workloads.gdn_decode_inputs(Bl, Hqk, Hv, d, dtype, seed=1000 * dist.rank + t,
                                             device=dev) for t in range(T)]
     out = torch.empty((T, Bl, Hv, d), dtype=dtype, device=dev)
     stream = torch.cuda.current_stream()
     esz = torch.tensor([], dtype=dtype).element_size()
-    bytes_step_local = (Bl * Hv * d * d * 4 * 2 + Bl * Hqk * d * esz * 2 + Bl * Hv * d * esz * 2
+    bytes_step_local = (Bl * Hv * d * d * ssz * 2 + Bl * Hqk * d * esz * 2 + Bl * Hv * d * esz * 2
                         + Bl * Hv * 4 * 2)
 
     def run_all():
@@ -332,23 +337,44 @@ def bench_gdn_decode(cfg, args, dist, peaks):
     dist.barrier()
     torch.cuda.synchronize()
     n0 = b200lab.launch_count()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(dev) as clk:
-        e0.record(stream)
-        run_all()
-        e1.record(stream)
-        torch.cuda.synchronize()
+    if ssz == 4:
+        # the fp32 state (134 MB at N=1) is larger than L2: 256 steps back to back
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(dev) as clk:
+            e0.record(stream)
+            run_all()
+            e1.record(stream)
+            torch.cuda.synchronize()
+        ms_local = e0.elapsed_time(e1) / T
+    else:
+        # a 16-bit state (67 MB at N=1) would stay in L2 between steps: flush L2 before
+        # every step and time each step alone
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(T)]
+        with ClockSampler(dev) as clk:
+            for t in range(T):
+                flush.zero_()
+                q, k, v, g, b = steps_in[t]
+                evs[t][0].record(stream)
+                b200lab.gdn_decode(q, k, v, g, b, state, out=out[t], stream=stream)
+                evs[t][1].record(stream)
+            torch.cuda.synchronize()
+        ms_local = sum(a.elapsed_time(b) for a, b in evs) / T
+        del flush
     launches = b200lab.launch_count() - n0
-    ms_local = e0.elapsed_time(e1) / T
     ms = dist.max(ms_local)
     gbs = bytes_step_local * dist.world / (ms * 1e-3) / 1e9
     achieved = bytes_step_local / (ms_local * 1e-3) / 1e9
-    traffic = profile_traffic("gdn_decode_c4")
+    traffic = profile_traffic("gdn_decode_c4") if ssz == 4 else None
+    sname = {4: "fp32", 2: str(sdt).replace("torch.", "")}[ssz]
     res = {"metric": "GDN decode GB/s", "value": gbs, "unit": "GB/s", "us_per_step": ms * 1e3,
            "steps": T, "bytes_per_step": bytes_step_local * dist.world,
-           "config": {"workload": "gdn_decode_c4", "B": cfg["B"], "Hqk": Hqk, "Hv": Hv, "d": d,
-                      "state": "fp32 [B,Hv,128,128] in place", "sharding": "sequences",
-                      "l2": "state larger than L2 (134 MB at N=1), 256 consecutive steps"},
+           "config": {"workload": "gdn_decode_c4" + ("" if ssz == 4 else f"_state_{sname}"),
+                      "B": cfg["B"], "Hqk": Hqk, "Hv": Hv, "d": d,
+                      "state": f"{sname} [B,Hv,128,128] in place", "sharding": "sequences",
+                      "l2": "state larger than L2 (134 MB at N=1), 256 consecutive steps" if ssz == 4
+                      else "L2 flushed before every step (16-bit state 67 MB at N=1)"},
            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                         "frac": achieved / peaks["hbm_gbs"], "traffic": traffic},
            "gpu_launches": int(launches), "clocks": clk.summary()}
@@ -559,7 +585,10 @@ def run_ours(args):
 
     secondary = {}
     if args.secondary and name == "attn_c5" and not args.attn_shape:
+        import torch
+        state16 = lambda c, a, d_, p: bench_gdn_decode(c, a, d_, p, state_dtype=torch.float16)  # noqa: E731
         for key, fn, c in (("gdn_decode", bench_gdn_decode, workloads.CONFIGS["gdn_decode_c4"]),
+                           ("gdn_decode_state16", state16, workloads.CONFIGS["gdn_decode_c4"]),
                            ("gdn_prefill", bench_gdn_prefill, workloads.CONFIGS["gdn_prefill_c3"])):
             try:
                 secondary[key] = fn(c, args, dist, peaks)

@@ -56,7 +56,9 @@ extern "C" {
  * separate query / key lengths and a bf16 variant.
  *   Q, O : [B][Hq ][Sq ][D]  dtype (F16 or BF16)
  *   K, V : [B][Hkv][Skv][D]  dtype
- *   D    : 64 or 128.  fp32 accumulation; O = softmax(scale*Q K^T [+mask]) V.
+ *   D    : 64, 128 or 256.  fp32 accumulation; O = softmax(scale*Q K^T [+mask]) V.
+ *          (D = 256 runs the kernel of attn_gated_fwd_sm100 without a gate; it
+ *          splits no key range and leaves the workspace unused.)
  *   causal: key j is visible to query i iff j <= i + (Skv - Sq); with
  *           Sq == Skv this is the reference's k <= q (src/attn_sm75.cu:69).
  *           A query row that sees no key is written as 0 (the reference's
@@ -69,6 +71,17 @@ int attn_fwd_sm100(const void* Q, const void* K, const void* V, void* O,
                    void* workspace, size_t ws_bytes, void* stream);
 size_t attn_fwd_sm100_workspace(int B, int Hq, int Hkv, int Sq, int Skv, int D,
                                 int causal);
+
+/* Gated softmax attention, head dim 256: O = softmax(scale*Q K^T [+mask]) V *
+ * sigmoid(G), the gate applied elementwise after the softmax.  No counterpart
+ * in the reference, which builds D = 64/128 only; this is the model layer its
+ * notes describe (24 q-heads / 4 kv-heads, head dim 256, gate after softmax,
+ * docs/qwen38-27b.md:13), with the same softmax semantics as attn_fwd_sm100.
+ *   Q, G, O : [B][Hq][Sq][256]; K, V : [B][Hkv][Skv][256]; G may be NULL (no
+ *   gate).  D must be 256.  16-byte aligned pointers.  No workspace. */
+int attn_gated_fwd_sm100(const void* Q, const void* K, const void* V, const void* G,
+                         void* O, int B, int Hq, int Hkv, int Sq, int Skv, int D,
+                         float scale, int causal, int dtype, void* stream);
 
 /* ---- Gated DeltaNet chunked prefill --------------------------------------
  * Replaces the chunked GDN kernels gdn_wmma_kernel (src/gdn_sm75.cu:361-369)

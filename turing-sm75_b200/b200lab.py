@@ -32,7 +32,7 @@ F16, BF16, F32 = 0, 1, 2
 
 # Every symbol include/b200lab.h declares (checked by tests/test_capi.py).
 EXPORTED = (
-    "attn_fwd_sm100", "attn_fwd_sm100_workspace",
+    "attn_fwd_sm100", "attn_fwd_sm100_workspace", "attn_gated_fwd_sm100",
     "gdn_prefill_sm100", "gdn_prefill_sm100_workspace", "gdn_prefill_sm100_noalloc",
     "gdn_decode_sm100", "gdn_decode_sm100_state16",
     "b200lab_strerror", "b200lab_device_status", "b200lab_version", "b200lab_launch_count",
@@ -67,6 +67,8 @@ def lib() -> ctypes.CDLL:
         L.attn_fwd_sm100.argtypes = [vp, vp, vp, vp] + [ci] * 6 + [cf, ci, ci, vp, sz, vp]
         L.attn_fwd_sm100_workspace.restype = sz
         L.attn_fwd_sm100_workspace.argtypes = [ci] * 7
+        L.attn_gated_fwd_sm100.restype = ci
+        L.attn_gated_fwd_sm100.argtypes = [vp] * 5 + [ci] * 6 + [cf, ci, ci, vp]
         L.gdn_prefill_sm100.restype = ci
         L.gdn_prefill_sm100.argtypes = [vp] * 7 + [ci] * 7 + [cf, ci, ci, vp, sz, vp]
         L.gdn_prefill_sm100_workspace.restype = sz
@@ -156,6 +158,29 @@ def attn_fwd(Q, K, V, *, scale: float | None = None, causal: bool = False, out=N
                               B, Hq, Hkv, Sq, Skv, D, float(scale), int(bool(causal)),
                               _dtype_code(Q), ws_ptr, ws_bytes, _stream(stream))
     _check(st, "attn_fwd_sm100")
+    return out
+
+
+def attn_gated_fwd(Q, K, V, G=None, *, scale: float | None = None, causal: bool = False, out=None,
+                   stream=None):
+    """Gated softmax attention, head dim 256: softmax(scale Q K^T) V * sigmoid(G).
+    Q, G [B,Hq,Sq,256], K/V [B,Hkv,Skv,256] (fp16/bf16); G None = no gate."""
+    torch = _torch()
+    B, Hq, Sq, D = Q.shape
+    _, Hkv, Skv, _ = K.shape
+    if K.shape != V.shape or K.shape[0] != B or K.shape[3] != D:
+        raise ValueError("K/V shape mismatch")
+    if G is not None and (G.shape != Q.shape or G.dtype != Q.dtype):
+        raise ValueError("G must match Q")
+    if scale is None:
+        scale = 1.0 / (D ** 0.5)
+    if out is None:
+        out = torch.empty_like(Q)
+    gp = _dev(G, "G") if G is not None else ctypes.c_void_p(0)
+    st = lib().attn_gated_fwd_sm100(_dev(Q, "Q"), _dev(K, "K"), _dev(V, "V"), gp, _dev(out, "out"),
+                                    B, Hq, Hkv, Sq, Skv, D, float(scale), int(bool(causal)),
+                                    _dtype_code(Q), _stream(stream))
+    _check(st, "attn_gated_fwd_sm100")
     return out
 
 

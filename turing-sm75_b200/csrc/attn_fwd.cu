@@ -600,6 +600,12 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 B200_DEFINE_ERR_TAKER(attn, b200::g_err_attn)
 
+namespace b200 {
+// attn_gated.cu: head dim 256 (one query tile per CTA, double-buffered S)
+int attn_d256_launch(const void* Q, const void* K, const void* V, const void* G, void* O, int B, int Hq,
+                     int Hkv, int Sq, int Skv, float scale, int causal, int dtype, void* stream);
+}  // namespace b200
+
 extern "C" size_t attn_fwd_sm100_workspace(int B, int Hq, int Hkv, int Sq, int Skv, int D,
                                            int causal) {
     (void)Hkv;
@@ -617,8 +623,10 @@ extern "C" int attn_fwd_sm100(const void* Q, const void* K, const void* V, void*
     if (dtype != B200LAB_F16 && dtype != B200LAB_BF16) return B200LAB_ERR_INVALID;
     if (causal != 0 && causal != 1) return B200LAB_ERR_INVALID;
     if (!(scale > 0.f) || !(scale < 1e30f)) return B200LAB_ERR_INVALID;
-    if (D != 64 && D != 128) return B200LAB_ERR_UNSUPPORTED;
+    if (D != 64 && D != 128 && D != 256) return B200LAB_ERR_UNSUPPORTED;
     if (B > 65535 || Hq > 65535) return B200LAB_ERR_UNSUPPORTED;
+    if (D == 256)  // no split-KV for this head dim: the workspace is not used
+        return attn_d256_launch(Q, K, V, nullptr, O, B, Hq, Hkv, Sq, Skv, scale, causal, dtype, stream);
     if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(O)) return B200LAB_ERR_INVALID;
     int rc = check_device_sm100();
     if (rc != B200LAB_OK) return rc;

@@ -5,6 +5,7 @@
 #pragma once
 namespace b200 {
 int take_err_attn();
+int take_err_attn_gated();
 int take_err_gdn_prefill();
 int take_err_gdn_decode();
 }  // namespace b200

@@ -94,7 +94,7 @@ extern "C" int b200lab_device_status(void* stream) {
     if (cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) != cudaSuccess)
         return B200LAB_ERR_CUDA;
     int worst = B200LAB_OK;
-    const int words[] = {b200::take_err_attn(), b200::take_err_gdn_prefill(),
+    const int words[] = {b200::take_err_attn(), b200::take_err_attn_gated(), b200::take_err_gdn_prefill(),
                          b200::take_err_gdn_decode()};
     for (int w : words) {
         if (w == B200LAB_ERR_CUDA) return B200LAB_ERR_CUDA;
