@@ -65,6 +65,21 @@ def profile_traffic(name):
     return None
 
 
+class L2Flush:
+    """Evicts the timed kernel's inputs from L2 between launches: writes a buffer larger
+    than L2, then reads another, so L2 is left holding clean unrelated lines (the write
+    alone would leave ~126 MB of dirty lines for the timed kernel to write back)."""
+
+    def __init__(self, dev, nbytes=256 << 20):
+        import torch
+        self.w = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        self.r = torch.ones(nbytes // 4, dtype=torch.float32, device=dev)
+
+    def __call__(self):
+        self.w.zero_()
+        self.r.sum()
+
+
 class ClockSampler:
     """Samples SM clock and clock-event reasons through NVML while running."""
 
@@ -304,6 +319,56 @@ def bench_attention(name, cfg, args, dist, peaks):
     return res
 
 
+def bench_gated_attention(cfg, args, dist, peaks):
+    """attn_gated_fwd_sm100 at the model's gated-attention shape, device-timed (inputs
+    resident, larger than L2); (batch, kv-head) sharding as for the headline."""
+    import torch
+    import b200lab
+    import workloads
+
+    B, Hq, Hkv = attn_shard(cfg, dist.world, dist.rank)
+    S, D, causal, dtype = cfg["S"], cfg["D"], cfg["causal"], cfg["dtype"]
+    dev = torch.device("cuda", dist.local)
+    Q, K, V = workloads.attn_inputs(B, Hq, Hkv, S, D, dtype, seed=52 + dist.rank, device=dev)
+    G = torch.randn(Q.shape, device=dev, dtype=torch.float32).to(dtype)
+    O = torch.empty_like(Q)
+    stream = torch.cuda.current_stream()
+    steps = max(3, min(args.steps, 10))
+
+    def step():
+        b200lab.attn_gated_fwd(Q, K, V, G, causal=causal, out=O, stream=stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    n0 = b200lab.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev) as clk:
+        e0.record(stream)
+        for _ in range(steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    launches = b200lab.launch_count() - n0
+    ms_local = e0.elapsed_time(e1) / steps
+    ms = dist.max(ms_local)
+    flops_total = attn_flops(cfg["B"], cfg["Hq"], S, D, causal)
+    achieved = attn_flops(B, Hq, S, D, causal) / (ms_local * 1e-3) / 1e12
+    res = {"metric": "gated attn fwd TFLOP/s", "value": flops_total / (ms * 1e-3) / 1e12,
+           "unit": "TFLOP/s", "ms_per_step": ms, "steps": steps,
+           "config": {"workload": "attn_gated_d256", "B": cfg["B"], "Hq": cfg["Hq"], "Hkv": cfg["Hkv"],
+                      "S": S, "D": D, "causal": causal, "gate": "sigmoid(G), G [B,Hq,S,D]",
+                      "l2": "inputs larger than L2"},
+           "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
+                        "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"], "traffic": None},
+           "gpu_launches": int(launches), "clocks": clk.summary()}
+    del Q, K, V, G, O
+    torch.cuda.empty_cache()
+    return res
+
+
 def bench_gdn_decode(cfg, args, dist, peaks, state_dtype=None):
     """GDN decode over the config's 256 steps; state_dtype fp16/bf16 runs the 16-bit-state
     entry (gdn_decode_sm100_state16), default the fp32 state."""
@@ -349,12 +414,12 @@ def bench_gdn_decode(cfg, args, dist, peaks, state_dtype=None):
     else:
         # a 16-bit state (67 MB at N=1) would stay in L2 between steps: flush L2 before
         # every step and time each step alone
-        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        flush = L2Flush(dev)
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                for _ in range(T)]
         with ClockSampler(dev) as clk:
             for t in range(T):
-                flush.zero_()
+                flush()
                 q, k, v, g, b = steps_in[t]
                 evs[t][0].record(stream)
                 b200lab.gdn_decode(q, k, v, g, b, state, out=out[t], stream=stream)
@@ -398,7 +463,7 @@ def bench_gdn_prefill(cfg, args, dist, peaks):
     stream = torch.cuda.current_stream()
     ws_bytes = b200lab.gdn_prefill_workspace_bytes(1, T, Hqk_l, Hv_l, d, d)
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
-    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    flush = L2Flush(dev)
 
     def step():
         b200lab.gdn_prefill(q, k, v, g, b, state, out=out, workspace=ws, stream=stream)
@@ -417,7 +482,7 @@ def bench_gdn_prefill(cfg, args, dist, peaks):
            for _ in range(args.steps)]
     with ClockSampler(dev) as clk:
         for e0, e1 in evs:
-            flush.zero_()  # inputs (106 MB) fit in L2: flush it between timed launches
+            flush()  # inputs (106 MB) fit in L2: flush it between timed launches
             e0.record(stream)
             step()
             e1.record(stream)
@@ -589,6 +654,7 @@ def run_ours(args):
         state16 = lambda c, a, d_, p: bench_gdn_decode(c, a, d_, p, state_dtype=torch.float16)  # noqa: E731
         for key, fn, c in (("gdn_decode", bench_gdn_decode, workloads.CONFIGS["gdn_decode_c4"]),
                            ("gdn_decode_state16", state16, workloads.CONFIGS["gdn_decode_c4"]),
+                           ("attn_gated_d256", bench_gated_attention, workloads.CONFIGS["attn_gated_d256"]),
                            ("gdn_prefill", bench_gdn_prefill, workloads.CONFIGS["gdn_prefill_c3"])):
             try:
                 secondary[key] = fn(c, args, dist, peaks)

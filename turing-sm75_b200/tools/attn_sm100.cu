@@ -115,8 +115,10 @@ static int run(int B, int H, int Hkv, int S, int D, int causal, int iters, bool 
     if (check) {
         if (D == 64)
             naive_check_kernel<T, 64><<<B * H, S>>>(Q, K, V, On, H, Hkv, S, scale, causal);
-        else
+        else if (D == 128)
             naive_check_kernel<T, 128><<<B * H, S>>>(Q, K, V, On, H, Hkv, S, scale, causal);
+        else
+            naive_check_kernel<T, 256><<<B * H, S>>>(Q, K, V, On, H, Hkv, S, scale, causal);
         CHECK_CUDA(cudaGetLastError());
         CHECK_CUDA(cudaDeviceSynchronize());
         std::vector<T> a(nq), r(nq);
@@ -173,8 +175,8 @@ int main(int argc, char** argv) {
         return 2;
     }
     if (Hkv < 0) Hkv = H;
-    if (D != 64 && D != 128) {
-        fprintf(stderr, "D=64 and D=128 only\n");
+    if (D != 64 && D != 128 && D != 256) {
+        fprintf(stderr, "D=64, 128 and 256 only\n");
         return 2;
     }
     if (B < 1 || H < 1 || S < 1 || Hkv < 1 || H % Hkv || iters < 1 || (causal != 0 && causal != 1)) {
@@ -190,7 +192,10 @@ int main(int argc, char** argv) {
     printf("GPU             : %s  (sm_%d%d)\n", prop.name, prop.major, prop.minor);
     printf("shape           : B=%d H=%d Hkv=%d S=%d D=%d  causal=%d  %s\n", B, H, Hkv, S, D, causal,
            bf16 ? "bf16" : "fp16");
-    printf("tile            : 128x128 tcgen05.mma (TMEM accumulators), TMA 128B-swizzled K/V ring\n");
+    if (D == 256)
+        printf("tile            : 128x64 tcgen05.mma, S double-buffered in TMEM, TMA 128B-swizzled K/V ring\n");
+    else
+        printf("tile            : 128x128 tcgen05.mma (TMEM accumulators), TMA 128B-swizzled K/V ring\n");
     return bf16 ? run<__nv_bfloat16>(B, H, Hkv, S, D, causal, iters, check, B200LAB_BF16)
                 : run<__half>(B, H, Hkv, S, D, causal, iters, check, B200LAB_F16);
 }

@@ -17,6 +17,8 @@ CONFIGS = {
     "attn_c2_d128": dict(B=2, Hq=8, Hkv=8, S=512, D=128, causal=True, dtype=torch.bfloat16),
     "attn_c2_d64": dict(B=2, Hq=8, Hkv=8, S=512, D=64, causal=True, dtype=torch.bfloat16),
     "attn_c5": dict(B=4, Hq=32, Hkv=8, S=16384, D=128, causal=True, dtype=torch.bfloat16),
+    # the model's gated-attention layer (24 q / 4 kv heads, head dim 256, gate after softmax)
+    "attn_gated_d256": dict(B=2, Hq=24, Hkv=4, S=16384, D=256, causal=True, dtype=torch.bfloat16),
     "gdn_prefill_c3": dict(B=1, T=4096, Hqk=16, Hv=32, d=128, dtype=torch.bfloat16),
     "gdn_decode_c4": dict(B=64, Hqk=16, Hv=32, d=128, steps=256, dtype=torch.bfloat16),
 }
