@@ -25,11 +25,11 @@ __device__ int g_err_gdn_decode = 0;
 
 constexpr int kD = 128;           // dk = dv
 constexpr int kThreads = 256;
-// fp32 state: 8 warps x 8 rows = 64 rows, half a (b, h) per CTA; a 16-bit state keeps
-// the same bytes in flight per warp with 16 rows a warp, a whole (b, h) per CTA
+// 8 warps x 8 rows = 64 rows, half a (b, h) per CTA, for either state type (a 16-bit
+// state with 16 rows a warp keeps more bytes in flight but leaves a 1.7-wave grid)
 template <typename TS>
 struct Rows {
-    static constexpr int kPerWarp = sizeof(TS) == 4 ? 8 : 16;
+    static constexpr int kPerWarp = 8;
     static constexpr int kCtasPerHead = kD / (kPerWarp * 8);
 };
 
