@@ -121,7 +121,7 @@ size_t gdn_prefill_sm100_workspace(int B, int T, int Hqk, int Hv, int dk, int dv
  * (64 MiB) that every GPU loading the prefill kernels holds until the process
  * exits.  A problem whose gdn_prefill_sm100_workspace() exceeds that size is
  * rejected with B200LAB_ERR_WORKSPACE before anything is launched (about
- * 49 KB per (sequence, v-head, 64-token chunk): B*Hv*ceil(T/64) <= 1358,
+ * 50 KB per (sequence, v-head, 64-token chunk): B*Hv*ceil(T/64) <= 1344,
  * e.g. Hv=48 up to T=1792, Hv=32 up to T=2688).
  * The first call on a device looks up the array's device address (with that
  * device current) and caches it; make that first call before any stream
@@ -136,6 +136,20 @@ int gdn_prefill_sm100_noalloc(const void* q, const void* k, const void* v,
                               int head_map, float scale, int in_dtype, int out_dtype,
                               void* stream);
 
+/* The prefill with the model's pre-processing fused in (no C entry of the
+ * reference corresponds; the steps either side of the path in the llama.cpp
+ * graph it targets, docs/ggml-turing.md:13-17), same conventions as
+ * gdn_decode_sm100_fused: q, k raw, L2-normalised over dk in the kernels
+ * (x * rsqrt(sum x^2 + 1e-6)); a, b : [B][T][Hv] fp32 logits,
+ * g_log = -exp(A_log[h]) * softplus(a + dt_bias[h]), beta = sigmoid(b);
+ * A_log, dt_bias : [Hv] fp32 or NULL.  Workspace as gdn_prefill_sm100. */
+int gdn_prefill_sm100_fused(const void* q, const void* k, const void* v,
+                            const float* a, const float* b, const float* A_log,
+                            const float* dt_bias, float* state, void* o, int B, int T,
+                            int Hqk, int Hv, int dk, int dv, int head_map, float scale,
+                            int in_dtype, int out_dtype, void* workspace, size_t ws_bytes,
+                            void* stream);
+
 /* ---- Gated DeltaNet single-token decode ----------------------------------
  * Replaces the token-serial kernels with T = 1, e.g. gdn_occ8_kernel
  * (src/gdn_sm75.cu:722-730) and gdn_occ_kernel (src/gdn_sm75.cu:135-145),
@@ -147,6 +161,21 @@ int gdn_decode_sm100(const void* q, const void* k, const void* v,
                      const float* g_log, const float* beta, float* state, void* o,
                      int B, int Hqk, int Hv, int dk, int dv, int head_map,
                      float scale, int in_dtype, int out_dtype, void* stream);
+
+/* The decode step with the model's pre-processing fused in (the steps either
+ * side of the path in the llama.cpp graph the reference targets,
+ * docs/ggml-turing.md:13-17; no C entry of the reference corresponds):
+ *   q, k raw; each is L2-normalised over dk in the kernel,
+ *       x * rsqrt(sum x^2 + 1e-6);
+ *   a, b : [B][Hv] fp32 logits; g_log = -exp(A_log[h]) * softplus(a + dt_bias[h])
+ *       (softplus(x) = x for x > 20), beta = sigmoid(b);
+ *   A_log, dt_bias : [Hv] fp32, either may be NULL (taken as 0).
+ * Otherwise as gdn_decode_sm100 (fp32 state in place). */
+int gdn_decode_sm100_fused(const void* q, const void* k, const void* v,
+                           const float* a, const float* b, const float* A_log,
+                           const float* dt_bias, float* state, void* o, int B, int Hqk,
+                           int Hv, int dk, int dv, int head_map, float scale, int in_dtype,
+                           int out_dtype, void* stream);
 
 /* The same decode step with a 16-bit recurrent state in HBM (state_dtype
  * B200LAB_F16 or B200LAB_BF16; [B][Hv][dv][dk], 8-byte aligned, updated in

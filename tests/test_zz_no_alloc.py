@@ -63,7 +63,7 @@ def test_noalloc_rejects_problems_beyond_its_scratch(cuda):
     L = b200lab.lib()
     p = ctypes.c_void_p(256)  # never dereferenced: the size check fails first
     stream = ctypes.c_void_p(0)
-    B, T, Hqk, Hv = 1, 3264, 16, 32   # 32 v-heads x 51 chunks > the scratch's 1358 chunk-heads
+    B, T, Hqk, Hv = 1, 3264, 16, 32   # 32 v-heads x 51 chunks > the scratch's 1344 chunk-heads
     assert b200lab.gdn_prefill_workspace_bytes(B, T, Hqk, Hv) > (64 << 20)
     st = L.gdn_prefill_sm100_noalloc(p, p, p, p, p, p, p, B, T, Hqk, Hv, 128, 128, 0, 0.088,
                                      b200lab.BF16, b200lab.BF16, stream)

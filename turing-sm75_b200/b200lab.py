@@ -34,7 +34,8 @@ F16, BF16, F32 = 0, 1, 2
 EXPORTED = (
     "attn_fwd_sm100", "attn_fwd_sm100_workspace", "attn_gated_fwd_sm100",
     "gdn_prefill_sm100", "gdn_prefill_sm100_workspace", "gdn_prefill_sm100_noalloc",
-    "gdn_decode_sm100", "gdn_decode_sm100_state16",
+    "gdn_prefill_sm100_fused",
+    "gdn_decode_sm100", "gdn_decode_sm100_state16", "gdn_decode_sm100_fused",
     "b200lab_strerror", "b200lab_device_status", "b200lab_version", "b200lab_launch_count",
 )
 
@@ -77,6 +78,10 @@ def lib() -> ctypes.CDLL:
         L.gdn_prefill_sm100_noalloc.argtypes = [vp] * 7 + [ci] * 7 + [cf, ci, ci, vp]
         L.gdn_decode_sm100.restype = ci
         L.gdn_decode_sm100.argtypes = [vp] * 7 + [ci] * 6 + [cf, ci, ci, vp]
+        L.gdn_prefill_sm100_fused.restype = ci
+        L.gdn_prefill_sm100_fused.argtypes = [vp] * 9 + [ci] * 7 + [cf, ci, ci, vp, sz, vp]
+        L.gdn_decode_sm100_fused.restype = ci
+        L.gdn_decode_sm100_fused.argtypes = [vp] * 9 + [ci] * 6 + [cf, ci, ci, vp]
         L.gdn_decode_sm100_state16.restype = ci
         L.gdn_decode_sm100_state16.argtypes = [vp] * 6 + [ci, vp] + [ci] * 6 + [cf, ci, ci, vp]
         L.b200lab_strerror.restype = ctypes.c_char_p
@@ -214,6 +219,33 @@ def gdn_prefill(q, k, v, g_log, beta, state, *, scale: float | None = None, head
     return out
 
 
+def gdn_prefill_fused(q, k, v, a, b, state, *, A_log=None, dt_bias=None, scale: float | None = None,
+                      head_map: int = 0, out=None, out_dtype=None, workspace=None, stream=None):
+    """Chunked prefill with the pre-processing fused: raw q,k [B,T,Hqk,dk] (L2-normalised in the
+    kernels); a, b [B,T,Hv] fp32 logits (g_log = -exp(A_log) softplus(a + dt_bias), beta =
+    sigmoid(b)); A_log, dt_bias [Hv] fp32 or None; fp32 state in place."""
+    torch = _torch()
+    B, T, Hqk, dk = q.shape
+    Hv, dv = v.shape[2], v.shape[3]
+    if scale is None:
+        scale = 1.0 / (dk ** 0.5)
+    if out is None:
+        out = torch.empty((B, T, Hv, dv), dtype=out_dtype or q.dtype, device=q.device)
+    need = gdn_prefill_workspace_bytes(B, T, Hqk, Hv, dk, dv)
+    ws_ptr, ws_bytes = ctypes.c_void_p(0), 0
+    if need:
+        if workspace is None:
+            workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+        ws_ptr, ws_bytes = _dev(workspace, "workspace"), workspace.numel() * workspace.element_size()
+    opt = lambda t, n: _dev(t, n) if t is not None else ctypes.c_void_p(0)  # noqa: E731
+    st = lib().gdn_prefill_sm100_fused(_dev(q, "q"), _dev(k, "k"), _dev(v, "v"), _dev(a, "a"), _dev(b, "b"),
+                                       opt(A_log, "A_log"), opt(dt_bias, "dt_bias"), _dev(state, "state"),
+                                       _dev(out, "out"), B, T, Hqk, Hv, dk, dv, int(head_map), float(scale),
+                                       _dtype_code(q), _dtype_code(out), ws_ptr, ws_bytes, _stream(stream))
+    _check(st, "gdn_prefill_sm100_fused")
+    return out
+
+
 def gdn_decode(q, k, v, g_log, beta, state, *, scale: float | None = None, head_map: int = 0,
                out=None, out_dtype=None, stream=None):
     """One Gated DeltaNet decode step.  q,k [B,Hqk,dk]; v [B,Hv,dv]; g_log,beta [B,Hv] fp32;
@@ -240,6 +272,27 @@ def gdn_decode(q, k, v, g_log, beta, state, *, scale: float | None = None, head_
                                             B, Hqk, Hv, dk, dv, int(head_map), float(scale),
                                             _dtype_code(q), _dtype_code(out), _stream(stream))
         _check(st, "gdn_decode_sm100_state16")
+    return out
+
+
+def gdn_decode_fused(q, k, v, a, b, state, *, A_log=None, dt_bias=None, scale: float | None = None,
+                     head_map: int = 0, out=None, out_dtype=None, stream=None):
+    """Decode step with the pre-processing fused: raw q,k [B,Hqk,dk] (L2-normalised in the
+    kernel); a, b [B,Hv] fp32 logits (g_log = -exp(A_log) softplus(a + dt_bias), beta =
+    sigmoid(b)); A_log, dt_bias [Hv] fp32 or None; fp32 state [B,Hv,dv,dk] in place."""
+    torch = _torch()
+    B, Hqk, dk = q.shape
+    Hv, dv = v.shape[1], v.shape[2]
+    if scale is None:
+        scale = 1.0 / (dk ** 0.5)
+    if out is None:
+        out = torch.empty((B, Hv, dv), dtype=out_dtype or q.dtype, device=q.device)
+    opt = lambda t, n: _dev(t, n) if t is not None else ctypes.c_void_p(0)  # noqa: E731
+    st = lib().gdn_decode_sm100_fused(_dev(q, "q"), _dev(k, "k"), _dev(v, "v"), _dev(a, "a"), _dev(b, "b"),
+                                      opt(A_log, "A_log"), opt(dt_bias, "dt_bias"), _dev(state, "state"),
+                                      _dev(out, "out"), B, Hqk, Hv, dk, dv, int(head_map), float(scale),
+                                      _dtype_code(q), _dtype_code(out), _stream(stream))
+    _check(st, "gdn_decode_sm100_fused")
     return out
 
 

@@ -81,11 +81,23 @@ __device__ __forceinline__ float4 load4(const T* p) {
     }
 }
 
-template <typename TIn, typename TOut, typename TS>
-__global__ void __launch_bounds__(kThreads) gdn_decode_kernel(
+// Fused pre-processing (gdn_decode_sm100_fused): q and k arrive raw and are L2-normalised
+// here, x * rsqrt(sum x^2 + kNormEps) over dk; g_log and beta then carry the logits a and b,
+// g = -exp(A_log[h]) * softplus(a + dt_bias[h]), beta = sigmoid(b).
+struct Pre {
+    const float* A_log;    // [Hv] or null (0)
+    const float* dt_bias;  // [Hv] or null (0)
+    int fused;
+};
+constexpr float kNormEps = 1e-6f;
+
+__device__ __forceinline__ float softplus(float x) { return x > 20.f ? x : log1pf(__expf(x)); }
+
+template <typename TIn, typename TOut, typename TS, bool kFused>
+__global__ void __launch_bounds__(kThreads, 4) gdn_decode_kernel(
     const TIn* __restrict__ q, const TIn* __restrict__ k, const TIn* __restrict__ v,
     const float* __restrict__ g_log, const float* __restrict__ beta, TS* __restrict__ state,
-    TOut* __restrict__ o, int Hqk, int Hv, int head_map, float scale) {
+    TOut* __restrict__ o, int Hqk, int Hv, int head_map, float scale, Pre pre) {
     constexpr int kRowsPerWarp = Rows<TS>::kPerWarp;
     constexpr int kCtasPerHead = Rows<TS>::kCtasPerHead;
     const int bh = blockIdx.x / kCtasPerHead;  // b * Hv + h
@@ -102,10 +114,22 @@ __global__ void __launch_bounds__(kThreads) gdn_decode_kernel(
     for (int r = 0; r < kRowsPerWarp; ++r) s[r] = ld_stream(S + r * kD);
 
     const size_t qk_off = ((size_t)b * Hqk + hq) * kD + 4 * lane;
-    const float4 kk = load4(k + qk_off);
-    const float4 qq = load4(q + qk_off);
-    const float g = expf(g_log[bh]);
-    const float be = beta[bh];
+    float4 kk = load4(k + qk_off);
+    float4 qq = load4(q + qk_off);
+    float g, be;
+    if constexpr (kFused) {
+        const float kr = rsqrtf(warp_sum(kk.x * kk.x + kk.y * kk.y + kk.z * kk.z + kk.w * kk.w) + kNormEps);
+        const float qr = rsqrtf(warp_sum(qq.x * qq.x + qq.y * qq.y + qq.z * qq.z + qq.w * qq.w) + kNormEps);
+        kk = make_float4(kk.x * kr, kk.y * kr, kk.z * kr, kk.w * kr);
+        qq = make_float4(qq.x * qr, qq.y * qr, qq.z * qr, qq.w * qr);
+        const float a = g_log[bh] + (pre.dt_bias ? pre.dt_bias[h] : 0.f);
+        const float decay = pre.A_log ? __expf(pre.A_log[h]) : 1.f;
+        g = __expf(-decay * softplus(a));
+        be = 1.f / (1.f + __expf(-beta[bh]));
+    } else {
+        g = expf(g_log[bh]);
+        be = beta[bh];
+    }
     const float vr = lane < kRowsPerWarp ? Elem<TIn>::to_f(v[(size_t)bh * kD + row0 + lane]) : 0.f;
     static_assert(kRowsPerWarp <= 32, "one v entry per lane");
 
@@ -131,10 +155,12 @@ __global__ void __launch_bounds__(kThreads) gdn_decode_kernel(
 template <typename TIn, typename TOut, typename TS>
 int launch(const void* q, const void* k, const void* v, const float* g_log, const float* beta,
            void* state, void* o, int B, int Hqk, int Hv, int head_map, float scale,
-           cudaStream_t st) {
-    gdn_decode_kernel<TIn, TOut, TS><<<B * Hv * Rows<TS>::kCtasPerHead, kThreads, 0, st>>>(
+           cudaStream_t st, Pre pre) {
+    // the fused pre-processing is its own instantiation: the plain step keeps its registers
+    auto kern = pre.fused ? gdn_decode_kernel<TIn, TOut, TS, true> : gdn_decode_kernel<TIn, TOut, TS, false>;
+    kern<<<B * Hv * Rows<TS>::kCtasPerHead, kThreads, 0, st>>>(
         static_cast<const TIn*>(q), static_cast<const TIn*>(k), static_cast<const TIn*>(v),
-        g_log, beta, static_cast<TS*>(state), static_cast<TOut*>(o), Hqk, Hv, head_map, scale);
+        g_log, beta, static_cast<TS*>(state), static_cast<TOut*>(o), Hqk, Hv, head_map, scale, pre);
     count_launch(1);
     return cudaGetLastError() == cudaSuccess ? B200LAB_OK : B200LAB_ERR_CUDA;
 }
@@ -142,15 +168,15 @@ int launch(const void* q, const void* k, const void* v, const float* g_log, cons
 template <typename TIn, typename TS>
 int dispatch_out(int out_dtype, const void* q, const void* k, const void* v, const float* g_log,
                  const float* beta, void* state, void* o, int B, int Hqk, int Hv, int head_map,
-                 float scale, cudaStream_t st) {
+                 float scale, cudaStream_t st, Pre pre) {
     switch (out_dtype) {
         case B200LAB_F16:
-            return launch<TIn, __half, TS>(q, k, v, g_log, beta, state, o, B, Hqk, Hv, head_map, scale, st);
+            return launch<TIn, __half, TS>(q, k, v, g_log, beta, state, o, B, Hqk, Hv, head_map, scale, st, pre);
         case B200LAB_BF16:
             return launch<TIn, __nv_bfloat16, TS>(q, k, v, g_log, beta, state, o, B, Hqk, Hv, head_map,
-                                                  scale, st);
+                                                  scale, st, pre);
         case B200LAB_F32:
-            return launch<TIn, float, TS>(q, k, v, g_log, beta, state, o, B, Hqk, Hv, head_map, scale, st);
+            return launch<TIn, float, TS>(q, k, v, g_log, beta, state, o, B, Hqk, Hv, head_map, scale, st, pre);
     }
     return B200LAB_ERR_UNSUPPORTED;
 }
@@ -158,17 +184,17 @@ int dispatch_out(int out_dtype, const void* q, const void* k, const void* v, con
 template <typename TS>
 int dispatch_in(int in_dtype, int out_dtype, const void* q, const void* k, const void* v,
                 const float* g_log, const float* beta, void* state, void* o, int B, int Hqk, int Hv,
-                int head_map, float scale, cudaStream_t st) {
+                int head_map, float scale, cudaStream_t st, Pre pre = Pre{nullptr, nullptr, 0}) {
     switch (in_dtype) {
         case B200LAB_F16:
             return dispatch_out<__half, TS>(out_dtype, q, k, v, g_log, beta, state, o, B, Hqk, Hv,
-                                            head_map, scale, st);
+                                            head_map, scale, st, pre);
         case B200LAB_BF16:
             return dispatch_out<__nv_bfloat16, TS>(out_dtype, q, k, v, g_log, beta, state, o, B, Hqk,
-                                                   Hv, head_map, scale, st);
+                                                   Hv, head_map, scale, st, pre);
         default:
             return dispatch_out<float, TS>(out_dtype, q, k, v, g_log, beta, state, o, B, Hqk, Hv,
-                                           head_map, scale, st);
+                                           head_map, scale, st, pre);
     }
 }
 
@@ -230,4 +256,21 @@ extern "C" int gdn_decode_sm100_state16(const void* q, const void* k, const void
                                      head_map, scale, st)
                : dispatch_in<__nv_bfloat16>(in_dtype, out_dtype, q, k, v, g_log, beta, state, o, B,
                                             Hqk, Hv, head_map, scale, st);
+}
+
+extern "C" int gdn_decode_sm100_fused(const void* q, const void* k, const void* v, const float* a,
+                                      const float* b, const float* A_log, const float* dt_bias,
+                                      float* state, void* o, int B, int Hqk, int Hv, int dk, int dv,
+                                      int head_map, float scale, int in_dtype, int out_dtype,
+                                      void* stream) {
+    using namespace b200;
+    int rc = check_args(q, k, v, a, b, state, o, B, Hqk, Hv, dk, dv, head_map, in_dtype, out_dtype);
+    if (rc != B200LAB_OK) return rc;
+    const uintptr_t in_align = in_dtype == B200LAB_F32 ? 16 : 8;
+    if (!aligned(q, in_align) || !aligned(k, in_align) || !aligned(state, 16))
+        return B200LAB_ERR_INVALID;
+    rc = check_device_sm100();
+    if (rc != B200LAB_OK) return rc;
+    return dispatch_in<float>(in_dtype, out_dtype, q, k, v, a, b, state, o, B, Hqk, Hv, head_map, scale,
+                              static_cast<cudaStream_t>(stream), Pre{A_log, dt_bias, 1});
 }

@@ -45,7 +45,7 @@ constexpr int kSlice = 32;  // state columns (v dim) per kernel-2 CTA
 
 // ---- workspace layout ------------------------------------------------------
 struct WsLayout {
-    size_t w, u, aqk, m, gcs, total;
+    size_t w, u, aqk, m, gcs, rq, rk, total;
 };
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 __host__ __device__ inline WsLayout ws_layout(size_t nbhc) {
@@ -55,17 +55,54 @@ __host__ __device__ inline WsLayout ws_layout(size_t nbhc) {
     L.aqk = align_up(L.u + nbhc * kC * kD * 2, 1024);
     L.m = align_up(L.aqk + nbhc * kC * kC * 2, 1024);
     L.gcs = align_up(L.m + nbhc * kC * kC * 2, 1024);
-    L.total = align_up(L.gcs + nbhc * kC * 4, 1024);
+    L.rq = align_up(L.gcs + nbhc * kC * 4, 1024);   // 1/|q_t|, 1/|k_t| (fused entry only)
+    L.rk = align_up(L.rq + nbhc * kC * 4, 1024);
+    L.total = align_up(L.rk + nbhc * kC * 4, 1024);
     return L;
 }
 
 struct PrepParams {
     uint8_t* ws;
-    const float* g_log;
-    const float* beta;
-    size_t ws_u, ws_aqk, ws_gcs;
+    const float* g_log;    // fused: the gate logits a
+    const float* beta;     // fused: the beta logits b
+    const float* A_log;    // fused: [Hv] or null
+    const float* dt_bias;  // fused: [Hv] or null
+    size_t ws_u, ws_aqk, ws_gcs, ws_rq, ws_rk;
     int T, Hqk, Hv, nch, head_map;
 };
+
+// Fused pre-processing (gdn_prefill_sm100_fused): q, k arrive raw and are L2-normalised,
+// x * rsqrt(sum x^2 + kNormEps) over dk; the gates come as logits,
+// g_log = -exp(A_log[h]) softplus(a + dt_bias[h]), beta = sigmoid(b).  The tensor-core
+// tiles stay the raw 16-bit q, k: the per-token factors 1/|q_t|, 1/|k_t| enter where the
+// products are scaled anyway (A, Aqk, the column scale of W, M, the decayed V_new rows and
+// the Q S^T output term).
+constexpr float kNormEps = 1e-6f;
+__device__ __forceinline__ float softplus(float x) { return x > 20.f ? x : log1pf(__expf(x)); }
+__device__ __forceinline__ float fused_gate(float a, const PrepParams& p, int h) {
+    const float decay = p.A_log ? __expf(p.A_log[h]) : 1.f;
+    return -decay * softplus(a + (p.dt_bias ? p.dt_bias[h] : 0.f));
+}
+// 1/|row| of a 64-token x 128-dim 16-bit tile held as two 128B-swizzled 64-column boxes
+template <typename T16>
+__device__ __forceinline__ float row_rnorm(const uint8_t* box0, const uint8_t* box1, int r) {
+    float acc = 0.f;
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+        const uint8_t* row = (b ? box1 : box0) + r * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const uint4 raw = *reinterpret_cast<const uint4*>(row + ((c ^ (r & 7)) << 4));
+            const T16* e = reinterpret_cast<const T16*>(&raw);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const float x = Elem<T16>::to_f(e[u]);
+                acc = fmaf(x, x, acc);
+            }
+        }
+    }
+    return rsqrtf(acc + kNormEps);
+}
 
 __device__ __forceinline__ int qk_head(int h, int Hqk, int Hv, int head_map) {
     return head_map == 0 ? h % Hqk : h / (Hv / Hqk);
@@ -92,7 +129,7 @@ constexpr int kLd = 68;            // fp32 row pitch of A and T (16-byte aligned
 constexpr int kAs = 49152;         // A, then T = (I + A)^-1 in place, fp32 64 x kLd
 constexpr int kXs = kAT;           // 32 x 36 fp32 scratch of the block inverse (AT is idle then)
 constexpr int kMisc = kAs + kC * kLd * 4;
-constexpr int kBytes = kMisc + 2048;
+constexpr int kBytes = kMisc + 3072;
 constexpr int kAlloc = kBytes + 1024;
 static_assert(3 * (kAlloc + 1024) <= 233472, "three prep CTAs per SM");
 static_assert(kAlloc <= 232448, "state kernel shared memory above the 227 KiB per-CTA limit");
@@ -106,6 +143,8 @@ struct Misc {
     float beta[kC];
     float colscale[2 * kC];  // [beta Gam | beta], the column scales of T' and T''
     float gprev[kC];         // cumsum of g_log over the previous chunk (for M)
+    float rk[kC], rq[kC];    // 1/|k_t|, 1/|q_t| (fused; else 1)
+    float rkp[kC];           // 1/|k_s| of the previous chunk (fused; else 1)
     uint64_t bar_tma, bar_v, bar_mma1, bar_mma2, bar_kp, bar_m, drain;
     uint32_t tmem_base;
     int abort;
@@ -204,7 +243,7 @@ __device__ __forceinline__ void lower_unit_inverse(float* As, float* X, int tid)
     __syncthreads();
 }
 
-template <typename T16>
+template <typename T16, bool kFused>
 __global__ void __launch_bounds__(prep::kThreads, 3)
     gdn_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmW,
@@ -267,6 +306,10 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
         if (tt < p.T) {
             g = p.g_log[gi];
             be = p.beta[gi];
+            if constexpr (kFused) {
+                g = fused_gate(g, p, h);
+                be = 1.f / (1.f + __expf(-be));
+            }
         }
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -279,6 +322,7 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
         // warps 2-3: the same scan over the previous (always full) chunk, for M
         const size_t gi = ((size_t)b * p.T + (t0 - kC + tid - kC)) * p.Hv + h;
         float g = p.g_log[gi];
+        if constexpr (kFused) g = fused_gate(g, p, h);
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const float y = __shfl_up_sync(0xffffffffu, g, o);
@@ -318,6 +362,14 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
         }
     }
     ok = __all_sync(0xffffffffu, mbar_wait(&ms->bar_mma1, 0, abort, &g_err_gdn_prefill));
+    if constexpr (kFused) {
+        // per-token 1/|k_t| and 1/|q_t| from the tiles, before V is loaded over Q
+        ok = __all_sync(0xffffffffu, mbar_wait(&ms->bar_tma, 0, abort, &g_err_gdn_prefill)) && ok;
+        if (tid < kC) ms->rk[tid] = row_rnorm<T16>(smem + kK0, smem + kK1, tid);
+        else ms->rq[tid - kC] = row_rnorm<T16>(smem + kQ0, smem + kQ1, tid - kC);
+        fence_proxy_async_smem();  // these reads of Q come before the V load's writes
+        __syncthreads();
+    }
     if (tid == 0 && ok) {
         // Q has been read: V goes over it (needed only by MMA2, after the solve)
         mbar_arrive_expect_tx(&ms->bar_v, 2 * 8192);
@@ -344,7 +396,9 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     const int ss = s + u;
-                    pa[u] = ss < row ? be * __uint_as_float(v[ss]) * ex2f(g2_r - ms->g2[ss]) : 0.f;
+                    float x = be * __uint_as_float(v[ss]) * ex2f(g2_r - ms->g2[ss]);
+                    if constexpr (kFused) x *= ms->rk[row] * ms->rk[ss];
+                    pa[u] = ss < row ? x : 0.f;
                 }
                 *reinterpret_cast<float4*>(As + row * kLd + s) = a;
             }
@@ -359,8 +413,12 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     const int s0 = s + 2 * u, s1 = s0 + 1;
-                    const float a0 = s0 <= row ? __uint_as_float(v[s0]) * ex2f(g2_r - ms->g2[s0]) : 0.f;
-                    const float a1 = s1 <= row ? __uint_as_float(v[s1]) * ex2f(g2_r - ms->g2[s1]) : 0.f;
+                    float a0 = s0 <= row ? __uint_as_float(v[s0]) * ex2f(g2_r - ms->g2[s0]) : 0.f;
+                    float a1 = s1 <= row ? __uint_as_float(v[s1]) * ex2f(g2_r - ms->g2[s1]) : 0.f;
+                    if constexpr (kFused) {
+                        a0 *= ms->rq[row] * ms->rk[s0];
+                        a1 *= ms->rq[row] * ms->rk[s1];
+                    }
                     pw[u] = Elem<T16>::pack2(a0, a1);
                 }
                 *reinterpret_cast<uint4*>(stg + (((s >> 3) ^ (row & 7)) << 4)) = pk;
@@ -377,7 +435,10 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
 
     {
         const int j = tid & 63;
-        ms->colscale[tid] = tid < kC ? ms->beta[j] * ex2f(ms->g2[j]) : ms->beta[j];
+        float sc = tid < kC ? ms->beta[j] * ex2f(ms->g2[j]) : ms->beta[j];
+        if constexpr (kFused)
+            if (tid < kC) sc *= ms->rk[j];  // W = T diag(beta Gam / |k|) K
+        ms->colscale[tid] = sc;
     }
     lower_unit_inverse(As, Xs, tid);  // contains __syncthreads: every thread calls it
     {
@@ -458,6 +519,10 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
     if (ok && warp < 2) {
         stage_rows(smem + kK0);  // W -> [K0 | . | K1 | .]
         reinterpret_cast<float*>(p.ws + p.ws_gcs)[bhc * kC + row] = gcs_r;
+        if constexpr (kFused) {
+            reinterpret_cast<float*>(p.ws + p.ws_rk)[bhc * kC + row] = ms->rk[row];
+            reinterpret_cast<float*>(p.ws + p.ws_rq)[bhc * kC + row] = ms->rq[row];
+        }
     }
     tc_fence_before();
     __syncthreads();  // W is out of TMEM
@@ -504,6 +569,14 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
     // M[t][s] = (W K_prev^T)[t][s] e^{gprev_last - gprev_s}: the previous chunk's
     // decayed keys as seen through this chunk's W.  Staged over AT (free since
     // MMA2), stored next to Aqk.  Chunk 0 of a sequence stores zeros.
+    if constexpr (kFused) {
+        // 1/|k_s| of the previous chunk's keys, from its tile
+        if (c > 0) {
+            ok = __all_sync(0xffffffffu, mbar_wait(&ms->bar_kp, 0, abort, &g_err_gdn_prefill)) && ok;
+            if (tid < kC) ms->rkp[tid] = row_rnorm<T16>(smem + kAs, smem + kAs + 8192, tid);
+        }
+        __syncthreads();
+    }
     if (c > 0)
         ok = __all_sync(0xffffffffu, mbar_wait(&ms->bar_m, 0, abort, &g_err_gdn_prefill)) && ok;
     tc_fence_after();
@@ -524,8 +597,13 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     const int s0 = q * 8 + 2 * u;
-                    pw[u] = Elem<T16>::pack2(__uint_as_float(v[s0]) * __expf(glast_prev - ms->gprev[s0]),
-                                             __uint_as_float(v[s0 + 1]) * __expf(glast_prev - ms->gprev[s0 + 1]));
+                    float m0 = __uint_as_float(v[s0]) * __expf(glast_prev - ms->gprev[s0]);
+                    float m1 = __uint_as_float(v[s0 + 1]) * __expf(glast_prev - ms->gprev[s0 + 1]);
+                    if constexpr (kFused) {
+                        m0 *= ms->rkp[s0];
+                        m1 *= ms->rkp[s0 + 1];
+                    }
+                    pw[u] = Elem<T16>::pack2(m0, m1);
                 }
             }
             *reinterpret_cast<uint4*>(stg + ((q ^ (row & 7)) << 4)) = pk;
@@ -617,7 +695,7 @@ struct StateParams {
     const uint8_t* ws;
     float* state;
     void* o;
-    size_t ws_gcs;
+    size_t ws_gcs, ws_rq, ws_rk;
     int T, Hqk, Hv, nch, head_map;
     float scale;
 };
@@ -642,7 +720,7 @@ __device__ __forceinline__ void store_row32(TOut* dst, const float (&v)[32]) {
     }
 }
 
-template <typename T16, typename TOut>
+template <typename T16, typename TOut, bool kFused>
 __global__ void __launch_bounds__(st::kThreads, 1)
     gdn_state_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmAqk,
@@ -863,10 +941,16 @@ __global__ void __launch_bounds__(st::kThreads, 1)
         } else if (warp < kWarpVn) {
             // ---- outputs: o_c = scale (e^{gcs} Q_c S_c^T + Aqk_c Vn_c), token row ----
             const int row = tid - kWarpOut * 32;  // 0..63 = TMEM lane
+            const float* rq_all = reinterpret_cast<const float*>(p.ws + p.ws_rq);
             float gcs_nx = p.nch > 0 ? gcs_all[bhc0 * kC + row] : 0.f;
+            float rq_nx = (kFused && p.nch > 0) ? rq_all[bhc0 * kC + row] : 1.f;
             for (int c = 0; c < p.nch; ++c) {
                 const float gcs_t = gcs_nx;
-                if (c + 1 < p.nch) gcs_nx = gcs_all[(bhc0 + c + 1) * kC + row];
+                const float rq_t = rq_nx;  // 1/|q_t| (fused pre-processing)
+                if (c + 1 < p.nch) {
+                    gcs_nx = gcs_all[(bhc0 + c + 1) * kC + row];
+                    if constexpr (kFused) rq_nx = rq_all[(bhc0 + c + 1) * kC + row];
+                }
                 if (!wait_all(&ms->rq_full[c & 1], st::rq_parity(c))) break;
                 if (!wait_all(&ms->x1_full[c & 1], (c >> 1) & 1)) break;
                 tc_fence_after();
@@ -878,7 +962,7 @@ __global__ void __launch_bounds__(st::kThreads, 1)
                 mbar_arrive(&ms->o_done[c & 1]);
                 const int tt = c * kC + row;
                 if (tt < p.T) {
-                    const float eg = __expf(gcs_t);
+                    const float eg = __expf(gcs_t) * rq_t;
                     float ov[kSlice];
 #pragma unroll
                     for (int cc = 0; cc < kSlice; ++cc)
@@ -891,8 +975,12 @@ __global__ void __launch_bounds__(st::kThreads, 1)
             const int row = tid - kWarpVn * 32;  // token; TMEM lane 64 + row
             uint8_t* sVn = smem + kVn;
             uint8_t* sVt = smem + kVt;
+            const float* rk_all = reinterpret_cast<const float*>(p.ws + p.ws_rk);
+            float rk_nx = (kFused && p.nch > 0) ? rk_all[bhc0 * kC + row] : 1.f;
             float gam_prev = 1.f;
             for (int c = 0; c < p.nch; ++c) {
+                const float rk_t = rk_nx;  // 1/|k_t|: K^T diag(1/|k|) Vt is the normalised keys' product
+                if (kFused && c + 1 < p.nch) rk_nx = rk_all[(bhc0 + c + 1) * kC + row];
                 const int s = c % kStages;
                 // chunk c's U row and gates from its stage (released only after v_ready(c))
                 if (!wait_all(&ms->full[s], (c / kStages) & 1)) break;
@@ -914,7 +1002,7 @@ __global__ void __launch_bounds__(st::kThreads, 1)
                 tmem_ld32(tmem + lane_base + kColRQ + ((c - 1) & 1) * 32, rr);
                 if (c > 0) tmem_ld32(tmem + lane_base + kColX1 + ((c - 1) & 1) * 32, xx);
                 tmem_ld_wait();
-                const float dec = __expf(g_last - gcs_t);
+                const float dec = __expf(g_last - gcs_t) * rk_t;
                 float vt[kSlice];
 #pragma unroll
                 for (int cc = 0; cc < kSlice; ++cc) {
@@ -946,10 +1034,17 @@ __global__ void __launch_bounds__(st::kThreads, 1)
 // ===========================================================================
 // host side
 // ===========================================================================
+// Pre-processing options of the fused entry (A_log, dt_bias may be null)
+struct Fuse {
+    bool on;
+    const float* A_log;
+    const float* dt_bias;
+};
+
 template <typename T16, typename TOut>
 int launch(const void* q, const void* k, const void* v, const float* g_log, const float* beta,
            float* state, void* o, int B, int T, int Hqk, int Hv, int head_map, float scale,
-           void* ws, cudaStream_t stream) {
+           void* ws, cudaStream_t stream, Fuse fuse) {
     const int nch = (T + kC - 1) / kC;
     const size_t nbhc = (size_t)B * Hv * nch;
     const WsLayout L = ws_layout(nbhc);
@@ -976,12 +1071,16 @@ int launch(const void* q, const void* k, const void* v, const float* g_log, cons
     pp.ws_u = L.u;
     pp.ws_aqk = L.aqk;
     pp.ws_gcs = L.gcs;
+    pp.ws_rq = L.rq;
+    pp.ws_rk = L.rk;
+    pp.A_log = fuse.A_log;
+    pp.dt_bias = fuse.dt_bias;
     pp.T = T;
     pp.Hqk = Hqk;
     pp.Hv = Hv;
     pp.nch = nch;
     pp.head_map = head_map;
-    auto k1 = gdn_prep_kernel<T16>;
+    auto k1 = fuse.on ? gdn_prep_kernel<T16, true> : gdn_prep_kernel<T16, false>;
     B200_TRY_CUDA(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, prep::kAlloc));
     k1<<<dim3(nch, Hv, B), prep::kThreads, prep::kAlloc, stream>>>(tq, tk, tv, tw, tu, ta, tm, pp);
     B200_TRY_CUDA(cudaGetLastError());
@@ -991,13 +1090,15 @@ int launch(const void* q, const void* k, const void* v, const float* g_log, cons
     sp.state = state;
     sp.o = o;
     sp.ws_gcs = L.gcs;
+    sp.ws_rq = L.rq;
+    sp.ws_rk = L.rk;
     sp.T = T;
     sp.Hqk = Hqk;
     sp.Hv = Hv;
     sp.nch = nch;
     sp.head_map = head_map;
     sp.scale = scale;
-    auto k2 = gdn_state_kernel<T16, TOut>;
+    auto k2 = fuse.on ? gdn_state_kernel<T16, TOut, true> : gdn_state_kernel<T16, TOut, false>;
     B200_TRY_CUDA(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, st::kAlloc));
     // launched with programmatic stream serialisation: its prologue (barriers, TMEM, the
     // initial state) overlaps the prep grid's last CTAs
@@ -1019,12 +1120,14 @@ int launch(const void* q, const void* k, const void* v, const float* g_log, cons
 template <typename T16>
 int dispatch_out(int out_dtype, const void* q, const void* k, const void* v, const float* g,
                  const float* be, float* state, void* o, int B, int T, int Hqk, int Hv, int hm,
-                 float scale, void* ws, cudaStream_t s) {
+                 float scale, void* ws, cudaStream_t s, Fuse f) {
     switch (out_dtype) {
-        case B200LAB_F16: return launch<T16, __half>(q, k, v, g, be, state, o, B, T, Hqk, Hv, hm, scale, ws, s);
+        case B200LAB_F16:
+            return launch<T16, __half>(q, k, v, g, be, state, o, B, T, Hqk, Hv, hm, scale, ws, s, f);
         case B200LAB_BF16:
-            return launch<T16, __nv_bfloat16>(q, k, v, g, be, state, o, B, T, Hqk, Hv, hm, scale, ws, s);
-        case B200LAB_F32: return launch<T16, float>(q, k, v, g, be, state, o, B, T, Hqk, Hv, hm, scale, ws, s);
+            return launch<T16, __nv_bfloat16>(q, k, v, g, be, state, o, B, T, Hqk, Hv, hm, scale, ws, s, f);
+        case B200LAB_F32:
+            return launch<T16, float>(q, k, v, g, be, state, o, B, T, Hqk, Hv, hm, scale, ws, s, f);
     }
     return B200LAB_ERR_UNSUPPORTED;
 }
@@ -1045,11 +1148,12 @@ extern "C" size_t gdn_prefill_sm100_workspace(int B, int T, int Hqk, int Hv, int
     return b200::ws_layout((size_t)B * Hv * nch).total;
 }
 
-extern "C" int gdn_prefill_sm100(const void* q, const void* k, const void* v, const float* g_log,
-                                 const float* beta, float* state, void* o, int B, int T, int Hqk,
-                                 int Hv, int dk, int dv, int head_map, float scale, int in_dtype,
-                                 int out_dtype, void* workspace, size_t ws_bytes, void* stream) {
-    using namespace b200;
+namespace b200 {
+namespace {
+int prefill_entry(const void* q, const void* k, const void* v, const float* g_log, const float* beta,
+                  float* state, void* o, int B, int T, int Hqk, int Hv, int dk, int dv, int head_map,
+                  float scale, int in_dtype, int out_dtype, void* workspace, size_t ws_bytes, void* stream,
+                  Fuse fuse) {
     if (!q || !k || !v || !g_log || !beta || !state || !o) return B200LAB_ERR_INVALID;
     if (B < 1 || T < 0 || Hqk < 1 || Hv < 1 || dk < 1 || dv < 1) return B200LAB_ERR_INVALID;
     if (head_map != 0 && head_map != 1) return B200LAB_ERR_INVALID;
@@ -1070,9 +1174,29 @@ extern "C" int gdn_prefill_sm100(const void* q, const void* k, const void* v, co
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (in_dtype == B200LAB_BF16)
         return dispatch_out<__nv_bfloat16>(out_dtype, q, k, v, g_log, beta, state, o, B, T, Hqk, Hv,
-                                           head_map, scale, workspace, s);
+                                           head_map, scale, workspace, s, fuse);
     return dispatch_out<__half>(out_dtype, q, k, v, g_log, beta, state, o, B, T, Hqk, Hv, head_map,
-                                scale, workspace, s);
+                                scale, workspace, s, fuse);
+}
+}  // namespace
+}  // namespace b200
+
+extern "C" int gdn_prefill_sm100(const void* q, const void* k, const void* v, const float* g_log,
+                                 const float* beta, float* state, void* o, int B, int T, int Hqk,
+                                 int Hv, int dk, int dv, int head_map, float scale, int in_dtype,
+                                 int out_dtype, void* workspace, size_t ws_bytes, void* stream) {
+    return b200::prefill_entry(q, k, v, g_log, beta, state, o, B, T, Hqk, Hv, dk, dv, head_map, scale,
+                               in_dtype, out_dtype, workspace, ws_bytes, stream,
+                               b200::Fuse{false, nullptr, nullptr});
+}
+
+extern "C" int gdn_prefill_sm100_fused(const void* q, const void* k, const void* v, const float* a,
+                                       const float* b, const float* A_log, const float* dt_bias,
+                                       float* state, void* o, int B, int T, int Hqk, int Hv, int dk,
+                                       int dv, int head_map, float scale, int in_dtype, int out_dtype,
+                                       void* workspace, size_t ws_bytes, void* stream) {
+    return b200::prefill_entry(q, k, v, a, b, state, o, B, T, Hqk, Hv, dk, dv, head_map, scale, in_dtype,
+                               out_dtype, workspace, ws_bytes, stream, b200::Fuse{true, A_log, dt_bias});
 }
 
 // ===========================================================================
