@@ -72,6 +72,18 @@ int attn_fwd_sm100(const void* Q, const void* K, const void* V, void* O,
 size_t attn_fwd_sm100_workspace(int B, int Hq, int Hkv, int Sq, int Skv, int D,
                                 int causal);
 
+/* Packed variable-length sequences (the cu_seqlens convention serving callers
+ * use; no counterpart in the reference, whose batches are dense):
+ *   Q, O : [total_q][Hq][D] token-major; K, V : [total_k][Hkv][D]
+ *   cu_seqlens_q, cu_seqlens_k : [B+1] device int32 prefix sums; sequence b is
+ *   tokens [cu[b], cu[b+1]) of each; max_seqlen_q bounds the grid.
+ *   Causal is aligned per sequence: key j visible to query i iff
+ *   j <= i + (Skv_b - Sq_b).  D = 64 or 128; no workspace (no key splits). */
+int attn_fwd_sm100_varlen(const void* Q, const void* K, const void* V, void* O,
+                          const int* cu_seqlens_q, const int* cu_seqlens_k,
+                          int max_seqlen_q, int total_q, int total_k, int B, int Hq,
+                          int Hkv, int D, float scale, int causal, int dtype, void* stream);
+
 /* Gated softmax attention, head dim 256: O = softmax(scale*Q K^T [+mask]) V *
  * sigmoid(G), the gate applied elementwise after the softmax.  No counterpart
  * in the reference, which builds D = 64/128 only; this is the model layer its
@@ -176,6 +188,17 @@ int gdn_decode_sm100_fused(const void* q, const void* k, const void* v,
                            const float* dt_bias, float* state, void* o, int B, int Hqk,
                            int Hv, int dk, int dv, int head_map, float scale, int in_dtype,
                            int out_dtype, void* stream);
+
+/* The decode step for continuous batching (no C entry of the reference
+ * corresponds; the paged batching serving callers need): the states live in a
+ * pool [n_slots][Hv][dv][dk] fp32 and sequence b uses state_pool[slots[b]]
+ * (slots: B device ints); slots[b] < 0 marks a padding entry, whose state and
+ * output are not touched.  Otherwise as gdn_decode_sm100. */
+int gdn_decode_sm100_slots(const void* q, const void* k, const void* v,
+                           const float* g_log, const float* beta, float* state_pool,
+                           const int* slots, void* o, int B, int Hqk, int Hv, int dk,
+                           int dv, int head_map, float scale, int in_dtype, int out_dtype,
+                           void* stream);
 
 /* The same decode step with a 16-bit recurrent state in HBM (state_dtype
  * B200LAB_F16 or B200LAB_BF16; [B][Hv][dv][dk], 8-byte aligned, updated in

@@ -58,3 +58,32 @@ def test_decode_equals_prefill_oracle_chain(cuda):
                                         np.zeros((B, Hv, 128, 128)), 1.0 / np.sqrt(128))
     assert_close(to_np(o), o_ref, "outputs")
     assert_close(to_np(S), S_ref, "state")
+
+
+def test_slots_pool_matches_dense_and_skips_padding(cuda):
+    """Continuous batching: sequences read / write their states in a pool through slot ids,
+    in any order; a slot of -1 leaves its state and output untouched."""
+    dev = torch.device("cuda:0")
+    B, Hqk, Hv, n_pool = 5, 2, 4, 8
+    slots = torch.tensor([6, 1, -1, 3, 0], dtype=torch.int32)
+    pool = workloads.gdn_state(n_pool, Hv, 128, std=0.02, seed=31)
+    pool_dev = pool.clone().to(dev)
+    q, k, v, g, b = workloads.gdn_decode_inputs(B, Hqk, Hv, 128, torch.bfloat16, seed=32)
+    sentinel = 7.0
+    out = torch.full((B, Hv, 128), sentinel, dtype=torch.float32, device=dev)
+    b200lab.gdn_decode_slots(q.to(dev), k.to(dev), v.to(dev), g.to(dev), b.to(dev), pool_dev,
+                             slots.to(dev), out=out)
+    assert b200lab.device_status() == b200lab.OK
+    scale = 1.0 / np.sqrt(128)
+    live = [i for i in range(B) if slots[i] >= 0]
+    S_in = pool[slots[live].long()].double().numpy()
+    o_ref, S_ref = oracle.gdn_recurrent(to_np(q)[live][:, None], to_np(k)[live][:, None],
+                                        to_np(v)[live][:, None], to_np(g)[live][:, None],
+                                        to_np(b)[live][:, None], S_in, scale)
+    o = to_np(out)
+    assert_close(o[live], o_ref[:, 0], "slot outputs")
+    assert np.all(o[2] == sentinel)  # padding row untouched
+    pool_out = to_np(pool_dev)
+    assert_close(pool_out[slots[live].long().numpy()], S_ref, "slot states")
+    untouched = [s for s in range(n_pool) if s not in set(slots.tolist())]
+    assert np.array_equal(pool_out[untouched], to_np(pool)[untouched])

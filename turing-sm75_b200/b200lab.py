@@ -32,10 +32,11 @@ F16, BF16, F32 = 0, 1, 2
 
 # Every symbol include/b200lab.h declares (checked by tests/test_capi.py).
 EXPORTED = (
-    "attn_fwd_sm100", "attn_fwd_sm100_workspace", "attn_gated_fwd_sm100",
+    "attn_fwd_sm100", "attn_fwd_sm100_workspace", "attn_gated_fwd_sm100", "attn_fwd_sm100_varlen",
     "gdn_prefill_sm100", "gdn_prefill_sm100_workspace", "gdn_prefill_sm100_noalloc",
     "gdn_prefill_sm100_fused",
     "gdn_decode_sm100", "gdn_decode_sm100_state16", "gdn_decode_sm100_fused",
+    "gdn_decode_sm100_slots",
     "b200lab_strerror", "b200lab_device_status", "b200lab_version", "b200lab_launch_count",
 )
 
@@ -68,6 +69,8 @@ def lib() -> ctypes.CDLL:
         L.attn_fwd_sm100.argtypes = [vp, vp, vp, vp] + [ci] * 6 + [cf, ci, ci, vp, sz, vp]
         L.attn_fwd_sm100_workspace.restype = sz
         L.attn_fwd_sm100_workspace.argtypes = [ci] * 7
+        L.attn_fwd_sm100_varlen.restype = ci
+        L.attn_fwd_sm100_varlen.argtypes = [vp] * 6 + [ci] * 7 + [cf, ci, ci, vp]
         L.attn_gated_fwd_sm100.restype = ci
         L.attn_gated_fwd_sm100.argtypes = [vp] * 5 + [ci] * 6 + [cf, ci, ci, vp]
         L.gdn_prefill_sm100.restype = ci
@@ -80,6 +83,8 @@ def lib() -> ctypes.CDLL:
         L.gdn_decode_sm100.argtypes = [vp] * 7 + [ci] * 6 + [cf, ci, ci, vp]
         L.gdn_prefill_sm100_fused.restype = ci
         L.gdn_prefill_sm100_fused.argtypes = [vp] * 9 + [ci] * 7 + [cf, ci, ci, vp, sz, vp]
+        L.gdn_decode_sm100_slots.restype = ci
+        L.gdn_decode_sm100_slots.argtypes = [vp] * 8 + [ci] * 6 + [cf, ci, ci, vp]
         L.gdn_decode_sm100_fused.restype = ci
         L.gdn_decode_sm100_fused.argtypes = [vp] * 9 + [ci] * 6 + [cf, ci, ci, vp]
         L.gdn_decode_sm100_state16.restype = ci
@@ -189,6 +194,28 @@ def attn_gated_fwd(Q, K, V, G=None, *, scale: float | None = None, causal: bool 
     return out
 
 
+def attn_fwd_varlen(Q, K, V, cu_seqlens_q, cu_seqlens_k, max_seqlen_q: int, *, scale: float | None = None,
+                    causal: bool = False, out=None, stream=None):
+    """Packed sequences: Q [total_q,Hq,D], K/V [total_k,Hkv,D] (fp16/bf16), cu_seqlens int32 [B+1]
+    on the device.  Returns O like Q."""
+    torch = _torch()
+    total_q, Hq, D = Q.shape
+    total_k, Hkv, _ = K.shape
+    B = cu_seqlens_q.numel() - 1
+    if cu_seqlens_q.dtype != torch.int32 or cu_seqlens_k.dtype != torch.int32 or cu_seqlens_k.numel() != B + 1:
+        raise ValueError("cu_seqlens must be int32 [B+1]")
+    if scale is None:
+        scale = 1.0 / (D ** 0.5)
+    if out is None:
+        out = torch.empty_like(Q)
+    st = lib().attn_fwd_sm100_varlen(_dev(Q, "Q"), _dev(K, "K"), _dev(V, "V"), _dev(out, "out"),
+                                     _dev(cu_seqlens_q, "cu_seqlens_q"), _dev(cu_seqlens_k, "cu_seqlens_k"),
+                                     int(max_seqlen_q), total_q, total_k, B, Hq, Hkv, D, float(scale),
+                                     int(bool(causal)), _dtype_code(Q), _stream(stream))
+    _check(st, "attn_fwd_sm100_varlen")
+    return out
+
+
 def gdn_prefill_workspace_bytes(B, T, Hqk, Hv, dk=128, dv=128) -> int:
     return int(lib().gdn_prefill_sm100_workspace(B, T, Hqk, Hv, dk, dv))
 
@@ -293,6 +320,27 @@ def gdn_decode_fused(q, k, v, a, b, state, *, A_log=None, dt_bias=None, scale: f
                                       _dev(out, "out"), B, Hqk, Hv, dk, dv, int(head_map), float(scale),
                                       _dtype_code(q), _dtype_code(out), _stream(stream))
     _check(st, "gdn_decode_sm100_fused")
+    return out
+
+
+def gdn_decode_slots(q, k, v, g_log, beta, state_pool, slots, *, scale: float | None = None,
+                     head_map: int = 0, out=None, out_dtype=None, stream=None):
+    """Decode step over a state pool: sequence b uses state_pool[slots[b]] (slots: int32 [B] on
+    the device; < 0 = padding, skipped).  state_pool [n,Hv,dv,dk] fp32 updated in place."""
+    torch = _torch()
+    B, Hqk, dk = q.shape
+    Hv, dv = v.shape[1], v.shape[2]
+    if slots.dtype != torch.int32 or slots.numel() != B:
+        raise ValueError("slots must be int32 [B]")
+    if scale is None:
+        scale = 1.0 / (dk ** 0.5)
+    if out is None:
+        out = torch.zeros((B, Hv, dv), dtype=out_dtype or q.dtype, device=q.device)
+    st = lib().gdn_decode_sm100_slots(_dev(q, "q"), _dev(k, "k"), _dev(v, "v"), _dev(g_log, "g_log"),
+                                      _dev(beta, "beta"), _dev(state_pool, "state_pool"), _dev(slots, "slots"),
+                                      _dev(out, "out"), B, Hqk, Hv, dk, dv, int(head_map), float(scale),
+                                      _dtype_code(q), _dtype_code(out), _stream(stream))
+    _check(st, "gdn_decode_sm100_slots")
     return out
 
 

@@ -78,6 +78,8 @@ struct Layout {
 
 struct Params {
     void* O;
+    const int* cu_q;  // varlen: [B+1] token offsets of the sequences in Q/O (device)
+    const int* cu_k;  // varlen: [B+1] token offsets in K/V
     float* part_o;   // split-KV partials: [B*Hq*Sq][nsplit][D] fp32 (unnormalised)
     float* part_ml;  // [B*Hq*Sq][nsplit][2]: running max (log2 units), row sum
     int Hq, Sq, Skv, group, n_ctas, causal;
@@ -124,10 +126,16 @@ __device__ __forceinline__ float2 exp2_fma2(float2 x) {
                        __uint_as_float(__float_as_uint(q.y) + (__float_as_uint(t.y) << 23)));
 }
 
-template <int D, typename T, bool kSplit>
+// kVarlen: packed sequences in the token-major layout Q/O [total_q][Hq][D], K/V
+// [total_k][Hkv][D] with per-sequence offsets cu_q / cu_k (blockIdx.z = sequence); the
+// tensor maps are (D, heads, tokens) with (64, 1, rows) boxes, which land in shared
+// memory exactly like the head-major boxes.  Rows of a box past the sequence belong to the
+// next one: keys there are masked, query rows there are not stored.
+template <int D, typename T, bool kSplit, bool kVarlen = false>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const Params p) {
+    static_assert(!(kSplit && kVarlen), "no key splits for packed sequences");
     using L = Layout<D>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -139,18 +147,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int lane = threadIdx.x & 31;
     const int split = (int)blockIdx.x % p.nsplit;
     const int cta_lin = (int)blockIdx.x / p.nsplit;
-    const int cta = p.causal ? (p.n_ctas - 1 - cta_lin) : cta_lin;
     const int hq = blockIdx.y;
     const int b = blockIdx.z;
+    int Sq = p.Sq, Skv = p.Skv, n_ctas = p.n_ctas;  // this sequence's lengths
+    int q_tok0 = 0, k_tok0 = 0;                      // varlen: its first token in Q/O, K/V
+    if constexpr (kVarlen) {
+        q_tok0 = p.cu_q[b];
+        k_tok0 = p.cu_k[b];
+        Sq = p.cu_q[b + 1] - q_tok0;
+        Skv = p.cu_k[b + 1] - k_tok0;
+        n_ctas = (Sq + kQTiles * BM - 1) / (kQTiles * BM);
+        if (cta_lin >= n_ctas) return;  // the grid covers the longest sequence
+    }
+    const int cta = p.causal ? (n_ctas - 1 - cta_lin) : cta_lin;
     const int q0 = cta * (kQTiles * BM);
-    const int off = p.Skv - p.Sq;
+    const int off = Skv - Sq;
 
     // key tiles this CTA needs: enough for its last valid query row, then the
     // part [j0, j0 + nkv) of them that belongs to this CTA's key split
-    const int nkv_all = (p.Skv + BN - 1) / BN;
+    const int nkv_all = (Skv + BN - 1) / BN;
     int nkv_need = nkv_all;
     if (p.causal) {
-        const long long last_row = min(q0 + kQTiles * BM, p.Sq) - 1;
+        const long long last_row = min(q0 + kQTiles * BM, Sq) - 1;
         const long long lim = last_row + off;  // last visible key of that row
         nkv_need = lim < 0 ? 0 : min(nkv_all, (int)(lim / BN) + 1);
     }
@@ -199,8 +217,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int t = 0; t < kQTiles; ++t)
 #pragma unroll
                 for (int a = 0; a < D / 64; ++a)
-                    tma_load_3d(smem + L::kQ + t * L::kQTileBytes + a * BM * 128, &tmQ, &bars->q_full,
-                                a * 64, q0 + t * BM, bh_q);
+                    if constexpr (kVarlen)
+                        tma_load_4d(smem + L::kQ + t * L::kQTileBytes + a * BM * 128, &tmQ, &bars->q_full,
+                                    a * 64, hq, q_tok0 + q0 + t * BM, 0);
+                    else
+                        tma_load_3d(smem + L::kQ + t * L::kQTileBytes + a * BM * 128, &tmQ, &bars->q_full,
+                                    a * 64, q0 + t * BM, bh_q);
             int issued = 0;
             for (int j = 0; j < nkv; ++j) {
                 const int st = j & 1;
@@ -209,8 +231,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_arrive_expect_tx(&bars->k_full[st], L::kKVBytes);
 #pragma unroll
                 for (int a = 0; a < D / 64; ++a)
-                    tma_load_3d(smem + L::kK + st * L::kKVBytes + a * BN * 128, &tmK,
-                                &bars->k_full[st], a * 64, (j0 + j) * BN, bh_kv);
+                    if constexpr (kVarlen)
+                        tma_load_4d(smem + L::kK + st * L::kKVBytes + a * BN * 128, &tmK,
+                                    &bars->k_full[st], a * 64, hq / p.group, k_tok0 + j * BN, 0);
+                    else
+                        tma_load_3d(smem + L::kK + st * L::kKVBytes + a * BN * 128, &tmK,
+                                    &bars->k_full[st], a * 64, (j0 + j) * BN, bh_kv);
                 if (!mbar_wait(&bars->v_empty[st], ph ^ 1, abort, &g_err_attn)) {
                     issued = -(j + 1);  // K_j issued, V_j not
                     break;
@@ -218,8 +244,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_arrive_expect_tx(&bars->v_full[st], L::kKVBytes);
 #pragma unroll
                 for (int a = 0; a < D / 64; ++a)
-                    tma_load_3d(smem + L::kV + st * L::kKVBytes + a * BN * 128, &tmV,
-                                &bars->v_full[st], a * 64, (j0 + j) * BN, bh_kv);
+                    if constexpr (kVarlen)
+                        tma_load_4d(smem + L::kV + st * L::kKVBytes + a * BN * 128, &tmV,
+                                    &bars->v_full[st], a * 64, hq / p.group, k_tok0 + j * BN, 0);
+                    else
+                        tma_load_3d(smem + L::kV + st * L::kKVBytes + a * BN * 128, &tmV,
+                                    &bars->v_full[st], a * 64, (j0 + j) * BN, bh_kv);
                 issued = j + 1;
             }
             // Drain: every TMA load this thread issued has landed before exit.
@@ -308,7 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t tS = tmem + lane_base + t * BN;
         const uint32_t tO = tmem + lane_base + L::kTmemO + t * D;
         const int qrow = q0 + t * BM + r;
-        const int key_lim = p.causal ? min(p.Skv - 1, qrow + off) : (p.Skv - 1);
+        const int key_lim = p.causal ? min(Skv - 1, qrow + off) : (Skv - 1);
         const float sl2 = p.scale_log2;
         float m = -INFINITY;  // running max of scaled scores, log2 units
         float l = 0.f;
@@ -434,7 +464,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
             // a row that never saw a key (max still -inf) is 0, as with l == 0
             const float inv_l = (l > 0.f && m != -INFINITY) ? 1.f / l : 0.f;
-            T* orow = static_cast<T*>(p.O) + ((size_t)(b * p.Hq + hq) * p.Sq + qrow) * D;
+            T* orow = static_cast<T*>(p.O) +
+                      (kVarlen ? ((size_t)(q_tok0 + qrow) * p.Hq + hq) * D
+                               : ((size_t)(b * p.Hq + hq) * p.Sq + qrow) * D);
 #pragma unroll
             for (int c = 0; c < D / 32; ++c) {
                 uint32_t o[32];
@@ -445,7 +477,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int u = 0; u < 32; ++u) o[u] = 0u;
                 }
-                if (qrow < p.Sq) {
+                if (qrow < Sq) {
 #pragma unroll
                     for (int v4 = 0; v4 < 4; ++v4) {
                         uint4 q4;
@@ -507,6 +539,46 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restri
         const uint32_t pk = Elem<T>::pack2(acc[u] * inv, acc[u + 1] * inv);
         *reinterpret_cast<uint32_t*>(orow + u) = pk;
     }
+}
+
+// Packed sequences (token-major Q/O [total_q][Hq][D], K/V [total_k][Hkv][D]): tensor
+// maps over (D, heads, tokens) with one head's rows per box; one grid column per
+// sequence, sized for the longest one.
+template <int D, typename T>
+int launch_varlen(const void* Q, const void* K, const void* V, void* O, const int* cu_q, const int* cu_k,
+                  int max_sq, int total_q, int total_k, int B, int Hq, int Hkv, float scale, int causal,
+                  cudaStream_t st) {
+    using L = Layout<D>;
+    const CUtensorMapDataType dt = Elem<T>::kFmt == 0 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                      : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    CUtensorMap tq, tk, tv;
+    int rc = make_tmap_4d(&tq, Q, dt, 2, D, Hq, total_q, 1, 64, 1, BM, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    rc = make_tmap_4d(&tk, K, dt, 2, D, Hkv, total_k, 1, 64, 1, BN, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    rc = make_tmap_4d(&tv, V, dt, 2, D, Hkv, total_k, 1, 64, 1, BN, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    Params p;
+    p.O = O;
+    p.cu_q = cu_q;
+    p.cu_k = cu_k;
+    p.part_o = nullptr;
+    p.part_ml = nullptr;
+    p.Hq = Hq;
+    p.Sq = 0;   // per sequence, from cu_q
+    p.Skv = 0;  // per sequence, from cu_k
+    p.group = Hq / Hkv;
+    p.n_ctas = (max_sq + kQTiles * BM - 1) / (kQTiles * BM);
+    p.causal = causal;
+    p.nsplit = 1;
+    p.tiles_per_split = 1 << 30;
+    p.scale_log2 = scale * 1.4426950408889634f;
+    auto kern = attn_fwd_kernel<D, T, false, true>;
+    B200_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc));
+    kern<<<dim3(p.n_ctas, Hq, B), kThreads, L::kAlloc, st>>>(tq, tk, tv, p);
+    count_launch(1);
+    B200_TRY_CUDA(cudaGetLastError());
+    return B200LAB_OK;
 }
 
 inline size_t align_up_floats(size_t n) { return (n + 63) / 64 * 64; }  // 256-byte steps
@@ -637,4 +709,31 @@ extern "C" int attn_fwd_sm100(const void* Q, const void* K, const void* V, void*
     }
     return D == 128 ? launch<128, __half>(Q, K, V, O, B, Hq, Hkv, Sq, Skv, scale, causal, workspace, ws_bytes, st)
                     : launch<64, __half>(Q, K, V, O, B, Hq, Hkv, Sq, Skv, scale, causal, workspace, ws_bytes, st);
+}
+
+extern "C" int attn_fwd_sm100_varlen(const void* Q, const void* K, const void* V, void* O, const int* cu_seqlens_q,
+                                     const int* cu_seqlens_k, int max_seqlen_q, int total_q, int total_k, int B,
+                                     int Hq, int Hkv, int D, float scale, int causal, int dtype, void* stream) {
+    using namespace b200;
+    if (!Q || !K || !V || !O || !cu_seqlens_q || !cu_seqlens_k) return B200LAB_ERR_INVALID;
+    if (B < 1 || Hq < 1 || Hkv < 1 || Hq % Hkv != 0 || max_seqlen_q < 1 || total_q < 1 || total_k < 1)
+        return B200LAB_ERR_INVALID;
+    if (dtype != B200LAB_F16 && dtype != B200LAB_BF16) return B200LAB_ERR_INVALID;
+    if (causal != 0 && causal != 1) return B200LAB_ERR_INVALID;
+    if (!(scale > 0.f) || !(scale < 1e30f)) return B200LAB_ERR_INVALID;
+    if (D != 64 && D != 128) return B200LAB_ERR_UNSUPPORTED;
+    if (B > 65535 || Hq > 65535) return B200LAB_ERR_UNSUPPORTED;
+    if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(O)) return B200LAB_ERR_INVALID;
+    int rc = check_device_sm100();
+    if (rc != B200LAB_OK) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (dtype == B200LAB_BF16)
+        return D == 128 ? launch_varlen<128, __nv_bfloat16>(Q, K, V, O, cu_seqlens_q, cu_seqlens_k, max_seqlen_q,
+                                                            total_q, total_k, B, Hq, Hkv, scale, causal, st)
+                        : launch_varlen<64, __nv_bfloat16>(Q, K, V, O, cu_seqlens_q, cu_seqlens_k, max_seqlen_q,
+                                                           total_q, total_k, B, Hq, Hkv, scale, causal, st);
+    return D == 128 ? launch_varlen<128, __half>(Q, K, V, O, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, total_q,
+                                                 total_k, B, Hq, Hkv, scale, causal, st)
+                    : launch_varlen<64, __half>(Q, K, V, O, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, total_q,
+                                                total_k, B, Hq, Hkv, scale, causal, st);
 }

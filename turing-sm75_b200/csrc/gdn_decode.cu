@@ -88,6 +88,9 @@ struct Pre {
     const float* A_log;    // [Hv] or null (0)
     const float* dt_bias;  // [Hv] or null (0)
     int fused;
+    // Continuous batching (gdn_decode_sm100_slots): sequence b's state is
+    // state[slots[b]] of a pool of [Hv][dv][dk] states; slots[b] < 0 is padding (skipped).
+    const int* slots = nullptr;
 };
 constexpr float kNormEps = 1e-6f;
 
@@ -108,7 +111,13 @@ __global__ void __launch_bounds__(kThreads, 4) gdn_decode_kernel(
     const int lane = threadIdx.x & 31;
     const int row0 = (blockIdx.x % kCtasPerHead) * (kRowsPerWarp * 8) + warp * kRowsPerWarp;
 
-    TS* S = state + (size_t)bh * kD * kD + (size_t)row0 * kD + 4 * lane;
+    size_t sh = (size_t)bh;  // state index of (b, h)
+    if (pre.slots) {
+        const int slot = pre.slots[b];
+        if (slot < 0) return;  // padding entry: no state, no output (uniform over the CTA)
+        sh = (size_t)slot * Hv + h;
+    }
+    TS* S = state + sh * kD * kD + (size_t)row0 * kD + 4 * lane;
     float4 s[kRowsPerWarp];
 #pragma unroll
     for (int r = 0; r < kRowsPerWarp; ++r) s[r] = ld_stream(S + r * kD);
@@ -273,4 +282,24 @@ extern "C" int gdn_decode_sm100_fused(const void* q, const void* k, const void* 
     if (rc != B200LAB_OK) return rc;
     return dispatch_in<float>(in_dtype, out_dtype, q, k, v, a, b, state, o, B, Hqk, Hv, head_map, scale,
                               static_cast<cudaStream_t>(stream), Pre{A_log, dt_bias, 1});
+}
+
+extern "C" int gdn_decode_sm100_slots(const void* q, const void* k, const void* v, const float* g_log,
+                                      const float* beta, float* state_pool, const int* slots, void* o,
+                                      int B, int Hqk, int Hv, int dk, int dv, int head_map, float scale,
+                                      int in_dtype, int out_dtype, void* stream) {
+    using namespace b200;
+    if (!slots) return B200LAB_ERR_INVALID;
+    int rc = check_args(q, k, v, g_log, beta, state_pool, o, B, Hqk, Hv, dk, dv, head_map, in_dtype,
+                        out_dtype);
+    if (rc != B200LAB_OK) return rc;
+    const uintptr_t in_align = in_dtype == B200LAB_F32 ? 16 : 8;
+    if (!aligned(q, in_align) || !aligned(k, in_align) || !aligned(state_pool, 16))
+        return B200LAB_ERR_INVALID;
+    rc = check_device_sm100();
+    if (rc != B200LAB_OK) return rc;
+    Pre pre{nullptr, nullptr, 0};
+    pre.slots = slots;
+    return dispatch_in<float>(in_dtype, out_dtype, q, k, v, g_log, beta, state_pool, o, B, Hqk, Hv,
+                              head_map, scale, static_cast<cudaStream_t>(stream), pre);
 }
