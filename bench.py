@@ -2,7 +2,7 @@
 """Benchmark of the B200-native attention / Gated DeltaNet hot path.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload attn_c5|attn_c1|attn_c2|gdn_decode|gdn_prefill]
+                    [--workload attn_c5|attn_c1|attn_c2|attn_gated_d256|gdn_decode|gdn_decode_state16|gdn_prefill]
 
 One JSON line on stdout (rank 0).  The headline workload is the long-context
 causal GQA attention config (B4 Hq32 Hkv8 S16384 D128 bf16), the config the
@@ -634,17 +634,21 @@ def run_ours(args):
     dist.init()
     peaks, peaks_src = load_peaks()
     name = args.workload
-    cfgname = {"attn_c2": "attn_c2_d128", "gdn_decode": "gdn_decode_c4",
+    cfgname = {"attn_c2": "attn_c2_d128", "gdn_decode": "gdn_decode_c4", "gdn_decode_state16": "gdn_decode_c4",
                "gdn_prefill": "gdn_prefill_c3"}.get(name, name)
     cfg = dict(workloads.CONFIGS[cfgname])
     if args.attn_shape:
         # smaller instance of the same kernel, for ncu captures that must stay small
         cfg["B"], cfg["Hq"], cfg["Hkv"], cfg["S"], cfg["D"] = (int(x) for x in args.attn_shape.split(","))
         name = name + "_custom"
-    if name.startswith("attn"):
+    if name.startswith("attn_gated"):
+        main = bench_gated_attention(cfg, args, dist, peaks)
+    elif name.startswith("attn"):
         main = bench_attention(name, cfg, args, dist, peaks)
     elif name == "gdn_decode":
         main = bench_gdn_decode(cfg, args, dist, peaks)
+    elif name == "gdn_decode_state16":
+        main = bench_gdn_decode(cfg, args, dist, peaks, state_dtype=torch.float16)
     else:
         main = bench_gdn_prefill(cfg, args, dist, peaks)
 
@@ -701,7 +705,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="attn_c5",
-                    choices=["attn_c5", "attn_c1", "attn_c2", "gdn_decode", "gdn_prefill"])
+                    choices=["attn_c5", "attn_c1", "attn_c2", "attn_gated_d256", "gdn_decode",
+                             "gdn_decode_state16", "gdn_prefill"])
     ap.add_argument("--no-secondary", dest="secondary", action="store_false")
     ap.add_argument("--attn-shape", default=None, metavar="B,Hq,Hkv,S,D",
                     help="override the attention shape (profiling a smaller case)")

@@ -201,8 +201,9 @@ int gdn_decode_sm100_slots(const void* q, const void* k, const void* v,
                            void* stream);
 
 /* The same decode step with a 16-bit recurrent state in HBM (state_dtype
- * B200LAB_F16 or B200LAB_BF16; [B][Hv][dv][dk], 8-byte aligned, updated in
- * place): half the bytes of the fp32 step, which is bound by them.  The
+ * B200LAB_F16 or B200LAB_BF16; [B][Hv][dv][dk], updated in place; q, k and
+ * state 16-byte aligned): half the bytes of the fp32 step,
+ * which is bound by them.  The
  * update is done in fp32 registers and rounded once per step on the store.
  * No C entry of the reference corresponds; the reference's own kernels keep
  * the state in fp16 within a launch (gdn_smem_kernel, src/gdn_sm75.cu:95-133;

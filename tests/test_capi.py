@@ -68,6 +68,6 @@ def test_state16_decode_rules_rejected_before_launch():
     assert f(n, n, n, n, n, n, b200lab.F16, n, 1, 1, 1, 128, 128, 0, 0.1, 1, 1, n) == b200lab.ERR_INVALID
     assert f(p, p, p, p, p, p, b200lab.F32, p, 1, 1, 1, 128, 128, 0, 0.1, 1, 1, n) == b200lab.ERR_INVALID
     assert f(p, p, p, p, p, p, b200lab.BF16, p, 1, 1, 1, 64, 64, 0, 0.1, 1, 1, n) == b200lab.ERR_UNSUPPORTED
-    # state not 8-byte aligned
-    odd = ctypes.c_void_p(20)
+    # state not 16-byte aligned
+    odd = ctypes.c_void_p(24)
     assert f(p, p, p, p, p, odd, b200lab.F16, p, 1, 1, 1, 128, 128, 0, 0.1, 1, 1, n) == b200lab.ERR_INVALID

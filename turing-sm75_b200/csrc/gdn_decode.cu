@@ -161,10 +161,102 @@ __global__ void __launch_bounds__(kThreads, 4) gdn_decode_kernel(
     if (lane < kRowsPerWarp) o[(size_t)bh * kD + row0 + lane] = Elem<TOut>::from_f(out);
 }
 
+// ---------------------------------------------------------------------------
+// 16-bit state: a 256-byte row is one 16-byte load for each of 16 lanes, so a warp
+// works on two rows at a time (lanes 0-15 / 16-31) with 16-lane reductions, and each
+// lane converts 8 entries a load.  CTA = 8 warps x 8 rows = half a (b, h).
+__device__ __forceinline__ uint4 ld_stream16(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.cs.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ void st_stream16(void* p, uint4 v) {
+    asm volatile("st.global.cs.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+__device__ __forceinline__ float half_warp_sum(float x) {
+#pragma unroll
+    for (int m = 8; m > 0; m >>= 1) x += __shfl_xor_sync(0xffffffffu, x, m);
+    return x;
+}
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float (&x)[8]) {
+    if constexpr (sizeof(T) == 4) {
+        const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+    } else {
+        const uint4 raw = *reinterpret_cast<const uint4*>(p);
+        const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) x[u] = Elem<T>::to_f(e[u]);
+    }
+}
+
+template <typename TIn, typename TOut, typename TS>
+__global__ void __launch_bounds__(kThreads, 4) gdn_decode16_kernel(
+    const TIn* __restrict__ q, const TIn* __restrict__ k, const TIn* __restrict__ v,
+    const float* __restrict__ g_log, const float* __restrict__ beta, TS* __restrict__ state,
+    TOut* __restrict__ o, int Hqk, int Hv, int head_map, float scale) {
+    constexpr int kRows = 8;  // per warp, as 4 pairs
+    const int bh = blockIdx.x / 2;
+    const int b = bh / Hv;
+    const int h = bh - b * Hv;
+    const int hq = head_map == 0 ? h % Hqk : h / (Hv / Hqk);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int half = lane >> 4, l16 = lane & 15;
+    const int row0 = (blockIdx.x % 2) * (kRows * 8) + warp * kRows;
+    TS* S = state + (size_t)bh * kD * kD + (size_t)(row0 + half) * kD + 8 * l16;
+    uint4 raw[kRows / 2];
+#pragma unroll
+    for (int i = 0; i < kRows / 2; ++i) raw[i] = ld_stream16(S + (size_t)(2 * i) * kD);
+    const size_t qk_off = ((size_t)b * Hqk + hq) * kD + 8 * l16;
+    float kk[8], qq[8];
+    load8(k + qk_off, kk);
+    load8(q + qk_off, qq);
+    const float g = expf(g_log[bh]);
+    const float be = beta[bh];
+    const float vr = lane < kRows ? Elem<TIn>::to_f(v[(size_t)bh * kD + row0 + lane]) : 0.f;
+#pragma unroll
+    for (int i = 0; i < kRows / 2; ++i) {
+        const TS* e = reinterpret_cast<const TS*>(&raw[i]);
+        float sv[8];
+        float kv = 0.f;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            sv[u] = Elem<TS>::to_f(e[u]);
+            kv = fmaf(sv[u], kk[u], kv);
+        }
+        kv = half_warp_sum(kv);
+        const float vv = __shfl_sync(0xffffffffu, vr, 2 * i + half);
+        const float d = (vv - g * kv) * be;
+        float od = 0.f;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            sv[u] = fmaf(g, sv[u], kk[u] * d);
+            od = fmaf(sv[u], qq[u], od);
+        }
+        od = half_warp_sum(od);
+        uint4 w;
+        w.x = Elem<TS>::pack2(sv[0], sv[1]);
+        w.y = Elem<TS>::pack2(sv[2], sv[3]);
+        w.z = Elem<TS>::pack2(sv[4], sv[5]);
+        w.w = Elem<TS>::pack2(sv[6], sv[7]);
+        st_stream16(S + (size_t)(2 * i) * kD, w);
+        if (l16 == 0) o[(size_t)bh * kD + row0 + 2 * i + half] = Elem<TOut>::from_f(od * scale);
+    }
+}
+
 template <typename TIn, typename TOut, typename TS>
 int launch(const void* q, const void* k, const void* v, const float* g_log, const float* beta,
            void* state, void* o, int B, int Hqk, int Hv, int head_map, float scale,
            cudaStream_t st, Pre pre) {
+    if constexpr (sizeof(TS) == 2) {
+        gdn_decode16_kernel<TIn, TOut, TS><<<B * Hv * 2, kThreads, 0, st>>>(
+            static_cast<const TIn*>(q), static_cast<const TIn*>(k), static_cast<const TIn*>(v), g_log, beta,
+            static_cast<TS*>(state), static_cast<TOut*>(o), Hqk, Hv, head_map, scale);
+        count_launch(1);
+        return cudaGetLastError() == cudaSuccess ? B200LAB_OK : B200LAB_ERR_CUDA;
+    }
     // the fused pre-processing is its own instantiation: the plain step keeps its registers
     auto kern = pre.fused ? gdn_decode_kernel<TIn, TOut, TS, true> : gdn_decode_kernel<TIn, TOut, TS, false>;
     kern<<<B * Hv * Rows<TS>::kCtasPerHead, kThreads, 0, st>>>(
@@ -254,9 +346,8 @@ extern "C" int gdn_decode_sm100_state16(const void* q, const void* k, const void
     int rc = check_args(q, k, v, g_log, beta, state, o, B, Hqk, Hv, dk, dv, head_map, in_dtype, out_dtype);
     if (rc != B200LAB_OK) return rc;
     if (state_dtype != B200LAB_F16 && state_dtype != B200LAB_BF16) return B200LAB_ERR_INVALID;
-    const uintptr_t in_align = in_dtype == B200LAB_F32 ? 16 : 8;
-    if (!aligned(q, in_align) || !aligned(k, in_align) || !aligned(state, 8))
-        return B200LAB_ERR_INVALID;
+    // 16-byte loads of q, k and the state rows
+    if (!aligned(q, 16) || !aligned(k, 16) || !aligned(state, 16)) return B200LAB_ERR_INVALID;
     rc = check_device_sm100();
     if (rc != B200LAB_OK) return rc;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
