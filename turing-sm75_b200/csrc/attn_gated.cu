@@ -9,17 +9,24 @@
 // kv-heads, head dim 256, docs/qwen38-27b.md:13), which the reference does not build.
 //
 // Design: one CTA per (128-row query tile, q-head, batch), 192 threads.
-//   TMEM (512 columns): S in two 64-column buffers (64 keys a tile) and O in 256.
+//   TMEM (512 columns): S in two 64-column buffers (64 keys a tile), O in 256, and Q in
+//   128 (copied there once by the softmax warps, so QK^T reads only K from shared memory).
 //   Two query tiles would need 768 columns, so the overlap comes from S instead: the
 //   tensor core computes S(j+1) while the softmax works on S(j), and PV(j) runs as soon
 //   as P(j) is in TMEM.  Per 64-key tile the tensor work (QK^T and PV, 8.4 MFLOP) is
 //   ~1024 cycles against ~950 of softmax, so the two can keep each other busy.
-//   warp 4: TMA producer (Q once; K_j, V_j into two-stage rings of 128-byte-swizzled
-//           64-column boxes).
+//   warp 4: TMA producer (Q once; K(0), K(1); then per tile the stage {V(j), K(j+2)} into
+//           slot j & 1 of two rings of 128-byte-swizzled 64-column boxes).
 //   warp 5: TMEM owner and MMA issuer: QK(0), QK(1), then per tile PV(j), QK(j+2).
 //   warps 0-3: softmax, thread = query row = TMEM lane; P(j) packed to 16 bits over the
 //           first 32 columns of its S buffer; lazy O rescale (max grows by > 2^8) after
 //           waiting for PV(j-1); epilogue O / l * sigmoid(G).
+// The issuing thread keeps the tensor pipe busy only while it is issuing: its issue queue
+// is about one instruction deep, so every barrier wait or commit between two MMAs leaves
+// the pipe idle for ~50-150 cycles.  Per tile the MMA thread therefore waits twice (the
+// stage, P(j)) and commits once: done[j & 1] marks PV(j) and QK(j+2) complete, which is
+// at once "S(j+2) ready" for the softmax, "slots of V(j) and K(j+2) free" for the
+// producer, and "PV(j) done" for a rescale of O.
 // Every mbarrier wait is bounded (common.cuh).
 #include "common.cuh"
 #include "errwords.h"
@@ -35,7 +42,9 @@ constexpr int BN = 64;    // keys per tile
 constexpr int kThreads = 192;
 constexpr int kWarpProducer = 4, kWarpMma = 5;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS = 0, kColO = 128;  // S buffers at 0 and 64, O at 128..383
+// S buffers at 0 and 64, O at 128..383, Q at 384..511 (two 16-bit values a column): the
+// QK^T products take Q from TMEM, so per key tile shared memory carries only K and V
+constexpr uint32_t kColS = 0, kColO = 128, kColQ = 384;
 constexpr float kRescaleThreshold = 8.0f;
 
 // shared layout: Q [4 boxes of 128 rows x 64 cols], K and V rings [2][4 boxes of 64 x 64]
@@ -43,11 +52,16 @@ constexpr int kQBytes = BM * D * 2;      // 64 KiB
 constexpr int kKVBytes = BN * D * 2;     // 32 KiB a stage
 constexpr int kQ = 0, kK = kQ + kQBytes, kV = kK + 2 * kKVBytes, kBar = kV + 2 * kKVBytes;
 
+// done[s] completes its n-th phase when QK(s + 2n) has completed, together with every MMA
+// issued before it (PV(s + 2n - 2) among them); the prologue commits QK(0) and QK(1).
 struct Bars {
     uint64_t q_full;
-    uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
-    uint64_t s_full[2], p_full[2];
-    uint64_t pv_done, o_final, drain;
+    uint64_t k_pro;       // K(0) and K(1) landed
+    uint64_t kv_full[2];  // stage j: V(j) (and K(j+2)) landed in slot j & 1
+    uint64_t done[2];
+    uint64_t p_full[2];
+    uint64_t q_tmem;  // the softmax warps have copied Q into TMEM
+    uint64_t o_final, drain;
     uint32_t tmem_base;
     int abort;
 };
@@ -93,15 +107,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (threadIdx.x == 0) {
         mbar_init(&bars->q_full, 1);
+        mbar_init(&bars->k_pro, 1);
         for (int i = 0; i < 2; ++i) {
-            mbar_init(&bars->k_full[i], 1);
-            mbar_init(&bars->k_empty[i], 1);
-            mbar_init(&bars->v_full[i], 1);
-            mbar_init(&bars->v_empty[i], 1);
-            mbar_init(&bars->s_full[i], 1);
+            mbar_init(&bars->kv_full[i], 1);
+            mbar_init(&bars->done[i], 1);
             mbar_init(&bars->p_full[i], 4);  // one arrival per softmax warp
         }
-        mbar_init(&bars->pv_done, 1);
+        mbar_init(&bars->q_tmem, 4);
         mbar_init(&bars->o_final, 1);
         mbar_init(&bars->drain, 1);
         bars->abort = 0;
@@ -127,64 +139,74 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int a = 0; a < D / 64; ++a)
                 tma_load_3d(smem + kQ + a * BM * 128, &tmQ, &bars->q_full, a * 64, q0, bh_q);
-            int nk = 0, nv = 0;
+            auto load_k = [&](int j, int slot, uint64_t* bar) {
+#pragma unroll
+                for (int a = 0; a < D / 64; ++a)
+                    tma_load_3d(smem + kK + slot * kKVBytes + a * BN * 128, &tmK, bar, a * 64, j * BN, bh_kv);
+            };
+            const int npro = min(2, nkv);
+            if (npro > 0) {
+                mbar_arrive_expect_tx(&bars->k_pro, npro * kKVBytes);
+                for (int j = 0; j < npro; ++j) load_k(j, j, &bars->k_pro);
+            }
+            int issued = 0;  // stages whose loads were issued
             for (int j = 0; j < nkv; ++j) {
                 const int st = j & 1;
-                const uint32_t ph = (j >> 1) & 1;
-                if (!mbar_wait(&bars->k_empty[st], ph ^ 1, abort, &g_err_attn_gated)) break;
-                mbar_arrive_expect_tx(&bars->k_full[st], kKVBytes);
+                const bool with_k = j + 2 < nkv;
+                // slot st of V held V(j-2) (read by PV(j-2)) and slot st of K holds K(j)
+                // (read by QK(j)): both are free once done[st] has completed phase j >> 1
+                if (j >= 2 && !mbar_wait(&bars->done[st], (j >> 1) & 1, abort, &g_err_attn_gated)) break;
+                mbar_arrive_expect_tx(&bars->kv_full[st], with_k ? 2 * kKVBytes : kKVBytes);
 #pragma unroll
                 for (int a = 0; a < D / 64; ++a)
-                    tma_load_3d(smem + kK + st * kKVBytes + a * BN * 128, &tmK, &bars->k_full[st], a * 64,
+                    tma_load_3d(smem + kV + st * kKVBytes + a * BN * 128, &tmV, &bars->kv_full[st], a * 64,
                                 j * BN, bh_kv);
-                nk = j + 1;
-                if (!mbar_wait(&bars->v_empty[st], ph ^ 1, abort, &g_err_attn_gated)) break;
-                mbar_arrive_expect_tx(&bars->v_full[st], kKVBytes);
-#pragma unroll
-                for (int a = 0; a < D / 64; ++a)
-                    tma_load_3d(smem + kV + st * kKVBytes + a * BN * 128, &tmV, &bars->v_full[st], a * 64,
-                                j * BN, bh_kv);
-                nv = j + 1;
+                issued = j + 1;
+                if (with_k) {
+                    if (j < 2 && !mbar_wait(&bars->done[st], 0, abort, &g_err_attn_gated)) break;
+                    load_k(j + 2, st, &bars->kv_full[st]);
+                }
             }
-            // drain: every TMA load issued has landed before exit
+            // drain: every TMA load issued has landed before exit (a stage whose K load was
+            // skipped by an abort never completes; its wait gives up on the abort flag)
             mbar_wait(&bars->q_full, 0, abort, &g_err_attn_gated);
-            for (int j = max(0, nk - 2); j < nk; ++j)
-                mbar_wait(&bars->k_full[j & 1], (j >> 1) & 1, abort, &g_err_attn_gated);
-            for (int j = max(0, nv - 2); j < nv; ++j)
-                mbar_wait(&bars->v_full[j & 1], (j >> 1) & 1, abort, &g_err_attn_gated);
+            if (npro > 0) mbar_wait(&bars->k_pro, 0, abort, &g_err_attn_gated);
+            for (int j = max(0, issued - 2); j < issued; ++j)
+                mbar_wait(&bars->kv_full[j & 1], (j >> 1) & 1, abort, &g_err_attn_gated);
         }
     } else if (warp == kWarpMma) {
         if (lane == 0) {
             constexpr uint32_t kFmt = Elem<T>::kFmt;
             constexpr uint32_t idesc_qk = make_idesc(kFmt, BM, BN, false, false);
             constexpr uint32_t idesc_pv = make_idesc(kFmt, BM, D, false, true);
-            const uint64_t dq = smem_desc(smem_u32(smem + kQ), 16, 1024, kLayoutSW128);
             const uint64_t dk = smem_desc(smem_u32(smem + kK), 16, 1024, kLayoutSW128);
             const uint64_t dv = smem_desc(smem_u32(smem + kV), BN * 128, 1024, kLayoutSW128);
-            auto qk = [&](int j) {  // S[j & 1] = Q K_j^T  (M=128, N=64, K=256)
+            auto qk = [&](int j) {  // S[j & 1] = Q K_j^T  (M=128, N=64, K=256), Q from TMEM
                 const uint64_t ka = dk + (((j & 1) * kKVBytes) >> 4);
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
-                    const uint32_t qo = ((kk >> 2) * (BM * 128) + (kk & 3) * 32) >> 4;
                     const uint32_t ko = ((kk >> 2) * (BN * 128) + (kk & 3) * 32) >> 4;
-                    mma_f16_ss(tmem + kColS + (j & 1) * BN, dq + qo, ka + ko, idesc_qk, kk > 0 ? 1u : 0u);
+                    mma_f16_ts(tmem + kColS + (j & 1) * BN, tmem + kColQ + kk * 8, ka + ko, idesc_qk,
+                               kk > 0 ? 1u : 0u);
                 }
-                mma_commit(&bars->s_full[j & 1]);
-                mma_commit(&bars->k_empty[j & 1]);
             };
-            bool ok = mbar_wait(&bars->q_full, 0, abort, &g_err_attn_gated);
-            for (int j = 0; ok && j < min(2, nkv); ++j) {
-                ok = mbar_wait(&bars->k_full[j & 1], (j >> 1) & 1, abort, &g_err_attn_gated);
-                if (ok) {
-                    tc_fence_after();
-                    qk(j);
+            // (no key tile: the softmax warps copy no Q and nothing waits for it)
+            bool ok = nkv == 0 || (mbar_wait(&bars->q_tmem, 0, abort, &g_err_attn_gated) &&
+                                   mbar_wait(&bars->k_pro, 0, abort, &g_err_attn_gated));
+            if (ok && nkv > 0) {
+                tc_fence_after();
+                qk(0);
+                mma_commit(&bars->done[0]);
+                if (nkv > 1) {
+                    qk(1);
+                    mma_commit(&bars->done[1]);
                 }
             }
             for (int j = 0; ok && j < nkv; ++j) {
                 const int st = j & 1;
                 const uint32_t ph = (j >> 1) & 1;
+                if (!mbar_wait(&bars->kv_full[st], ph, abort, &g_err_attn_gated)) break;
                 if (!mbar_wait(&bars->p_full[st], ph, abort, &g_err_attn_gated)) break;
-                if (!mbar_wait(&bars->v_full[st], ph, abort, &g_err_attn_gated)) break;
                 tc_fence_after();
                 // O += P(j) V_j: P from TMEM (16 keys = 8 packed columns a step), V MN-major,
                 // its four 64-column boxes BN*128 bytes apart
@@ -193,14 +215,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int kk = 0; kk < BN / 16; ++kk)
                     mma_f16_ts(tmem + kColO, tmem + kColS + st * BN + kk * 8, va + ((kk * 16 * 128) >> 4),
                                idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
-                mma_commit(&bars->v_empty[st]);
-                mma_commit(&bars->pv_done);
                 // S buffer st is free once PV(j) has read P(j); the tensor pipe runs in order
-                if (j + 2 < nkv) {
-                    if (!mbar_wait(&bars->k_full[st], ((j + 2) >> 1) & 1, abort, &g_err_attn_gated)) break;
-                    tc_fence_after();
-                    qk(j + 2);
-                }
+                if (j + 2 < nkv) qk(j + 2);
+                mma_commit(&bars->done[st]);
             }
             mma_commit(&bars->o_final);
             mma_commit(&bars->drain);
@@ -215,9 +232,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float sl2 = p.scale_log2;
         float m = -INFINITY, l = 0.f;
         bool ok = true;
-        for (int j = 0; j < nkv; ++j) {
+        if (nkv > 0) {
+            // Q row r (four 128B-swizzled 64-column boxes) -> TMEM columns kColQ.., two 16-bit
+            // values a column (low half = even k), the A layout of the QK^T MMAs
+            ok = __all_sync(0xffffffffu, mbar_wait(&bars->q_full, 0, abort, &g_err_attn_gated));
+#pragma unroll
+            for (int a = 0; a < D / 64; ++a) {
+                uint32_t w[32];
+                const uint8_t* qrow_s = smem + kQ + a * BM * 128 + r * 128;
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    const uint4 v4 = *reinterpret_cast<const uint4*>(qrow_s + ((c ^ (r & 7)) << 4));
+                    w[4 * c + 0] = v4.x;
+                    w[4 * c + 1] = v4.y;
+                    w[4 * c + 2] = v4.z;
+                    w[4 * c + 3] = v4.w;
+                }
+                tmem_st32(tmem + lane_base + kColQ + a * 32, w);
+            }
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->q_tmem);
+        }
+        for (int j = 0; ok && j < nkv; ++j) {
             const int st = j & 1;
-            if (!__all_sync(0xffffffffu, mbar_wait(&bars->s_full[st], (j >> 1) & 1, abort, &g_err_attn_gated))) {
+            // S(j) = QK(j) complete: phase j >> 1 of done[st]
+            if (!__all_sync(0xffffffffu, mbar_wait(&bars->done[st], (j >> 1) & 1, abort, &g_err_attn_gated))) {
                 ok = false;
                 break;
             }
@@ -261,7 +302,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_st32(tS, pk);
             // O may be rescaled only once PV(j-1) has finished (S(j) was computed earlier)
             if (j > 0 && __any_sync(0xffffffffu, rescale)) {
-                if (!__all_sync(0xffffffffu, mbar_wait(&bars->pv_done, (j - 1) & 1, abort, &g_err_attn_gated))) {
+                // PV(j-1) complete: phase ((j - 1) >> 1) + 1 of done[(j - 1) & 1]
+                const int jp = j - 1;
+                if (!__all_sync(0xffffffffu, mbar_wait(&bars->done[jp & 1], ((jp >> 1) + 1) & 1, abort,
+                                                       &g_err_attn_gated))) {
                     ok = false;
                     break;
                 }
