@@ -127,9 +127,10 @@ constexpr int kK0 = 0, kQ0 = 8192, kK1 = 16384, kQ1 = 24576, kV0 = kQ0, kV1 = kQ
 constexpr int kAT = 32768;         // [T diag(beta Gam); T diag(beta)] 128 x 64, 16 KiB
 constexpr int kLd = 68;            // fp32 row pitch of A and T (16-byte aligned, fewer conflicts)
 constexpr int kAs = 49152;         // A, then T = (I + A)^-1 in place, fp32 64 x kLd
-constexpr int kXs = kAT;           // 32 x 36 fp32 scratch of the block inverse (AT is idle then)
 constexpr int kMisc = kAs + kC * kLd * 4;
-constexpr int kBytes = kMisc + 3072;
+constexpr int kXs = kMisc + 3072;  // 32 x 36 fp32 scratch of the block inverse (its own
+                                   // slot: AT is still being read by the Aqk store then)
+constexpr int kBytes = kXs + 32 * 36 * 4;
 constexpr int kAlloc = kBytes + 1024;
 static_assert(3 * (kAlloc + 1024) <= 233472, "three prep CTAs per SM");
 static_assert(kAlloc <= 232448, "state kernel shared memory above the 227 KiB per-CTA limit");
@@ -145,11 +146,12 @@ struct Misc {
     float gprev[kC];         // cumsum of g_log over the previous chunk (for M)
     float rk[kC], rq[kC];    // 1/|k_t|, 1/|q_t| (fused; else 1)
     float rkp[kC];           // 1/|k_s| of the previous chunk (fused; else 1)
+    float mdecay[kC];        // e^{gprev_last - gprev_s}, the column decay of M
     uint64_t bar_tma, bar_v, bar_mma1, bar_mma2, bar_kp, bar_m, drain;
     uint32_t tmem_base;
     int abort;
 };
-static_assert(sizeof(Misc) <= kBytes - kMisc, "prep Misc overflows its slot");
+static_assert(sizeof(Misc) <= kXs - kMisc, "prep Misc overflows its slot");
 }  // namespace prep
 
 __device__ __forceinline__ float ex2f(float x) {
@@ -164,13 +166,15 @@ __device__ __forceinline__ float ex2f(float x) {
 //                                                lane, forward substitution)
 //   T21 = -T22 (A21 T11),  T12 = 0              (all 128 threads, 8 outputs each)
 // In place: T overwrites A (fp32, row pitch kLd; the upper triangle of A is zero and stays
-// so); X (32 x 32) is scratch.
-__device__ __forceinline__ void lower_unit_inverse(float* As, float* X, int tid) {
+// so); X (32 x 32) is scratch.  The diagonal blocks are done by the warp that built their
+// rows of A (diag_block_inverse, right after that warp's rows are written, while the other
+// two warps still build Aqk); the off-diagonal block after a CTA barrier.
+__device__ __forceinline__ void diag_block_inverse(float* As, int warp, int lane) {
     using prep::kLd;
     float* Ts = As;
-    if (tid < 64) {
-        const int o = (tid >> 5) * 32;  // diagonal block origin
-        const int j = tid & 31;         // column within the block
+    {
+        const int o = warp * 32;  // diagonal block origin
+        const int j = lane;       // column within the block
         float col[32];
 #pragma unroll
         for (int b = 0; b < 4; ++b) {   // rows in blocks of 8: 8 independent chains
@@ -202,7 +206,13 @@ __device__ __forceinline__ void lower_unit_inverse(float* As, float* X, int tid)
 #pragma unroll
         for (int t = 0; t < 32; ++t) Ts[(o + t) * kLd + o + j] = col[t];
     }
-    __syncthreads();
+}
+
+// T21 = -T22 (A21 T11) once both diagonal blocks are inverted (all 128 threads; the caller
+// has synchronised the CTA after diag_block_inverse).
+__device__ __forceinline__ void offdiag_block_inverse(float* As, float* X, int tid) {
+    using prep::kLd;
+    float* Ts = As;
     // 128 threads x 8 outputs: row r = tid / 4, columns c0 .. c0 + 7 with c0 = (tid % 4) * 8
     const int r = tid >> 2, c0 = (tid & 3) * 8;
     {   // X = A21 T11
@@ -270,6 +280,19 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
     // the state pass may be scheduled once every prep CTA is running; it waits for this
     // grid's results itself (grid_dependency_wait)
     allow_dependent_launch();
+    // gate inputs, loaded first so their latency overlaps the setup: threads 0-63 this
+    // chunk's g_log and beta (padded tokens keep g = 0, beta = 0), threads 64-127 the
+    // previous (always full) chunk's g_log, for M
+    float g_in = 0.f, be_in = 0.f;
+    if (tid < kC) {
+        if (t0 + tid < p.T) {
+            const size_t gi = ((size_t)b * p.T + t0 + tid) * p.Hv + h;
+            g_in = p.g_log[gi];
+            be_in = p.beta[gi];
+        }
+    } else if (c > 0) {
+        g_in = p.g_log[((size_t)b * p.T + (t0 - kC + tid - kC)) * p.Hv + h];
+    }
 
     if (tid == 0) {
         mbar_init(&ms->bar_tma, 1);
@@ -300,13 +323,9 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
     }
     // gates: gcs = inclusive prefix sum of g_log over the chunk (padded tokens: g=0, beta=0)
     if (tid < kC) {
-        const int tt = t0 + tid;
-        const size_t gi = ((size_t)b * p.T + tt) * p.Hv + h;
-        float g = 0.f, be = 0.f;
-        if (tt < p.T) {
-            g = p.g_log[gi];
-            be = p.beta[gi];
-            if constexpr (kFused) {
+        float g = g_in, be = be_in;
+        if constexpr (kFused) {
+            if (t0 + tid < p.T) {
                 g = fused_gate(g, p, h);
                 be = 1.f / (1.f + __expf(-be));
             }
@@ -320,8 +339,7 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
         ms->beta[tid] = be;
     } else if (c > 0) {
         // warps 2-3: the same scan over the previous (always full) chunk, for M
-        const size_t gi = ((size_t)b * p.T + (t0 - kC + tid - kC)) * p.Hv + h;
-        float g = p.g_log[gi];
+        float g = g_in;
         if constexpr (kFused) g = fused_gate(g, p, h);
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -343,6 +361,7 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
         ms->gprev[t] = g;
     }
     __syncthreads();
+    if (tid >= kC && c > 0) ms->mdecay[tid - kC] = __expf(ms->gprev[kC - 1] - ms->gprev[tid - kC]);
 
     // MMA1: [K;Q] K^T  (M=128, N=64, K=128)
     bool ok = true;
@@ -402,6 +421,8 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
                 }
                 *reinterpret_cast<float4*>(As + row * kLd + s) = a;
             }
+            __syncwarp();  // this warp's 32 rows of A, which hold its whole diagonal block
+            diag_block_inverse(As, warp, lane);
         } else {
             // Aqk row (lower incl. diagonal), 16-bit, staged 128B-swizzled in the (not yet
             // used) AT tile and written to the workspace by one TMA store
@@ -430,7 +451,6 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
     if (tid == 64 && ok) {
         tma_store_3d(&tmAqk, smem + kAT, 0, 0, (int)bhc);
         bulk_commit();
-        bulk_wait_read();  // the AT tile is rewritten after the solve
     }
 
     {
@@ -440,7 +460,11 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
             if (tid < kC) sc *= ms->rk[j];  // W = T diag(beta Gam / |k|) K
         ms->colscale[tid] = sc;
     }
-    lower_unit_inverse(As, Xs, tid);  // contains __syncthreads: every thread calls it
+    offdiag_block_inverse(As, Xs, tid);  // contains __syncthreads: every thread calls it
+    if (tid == 64 && ok) {
+        bulk_wait_read();  // the Aqk store has read the AT tile, which is rewritten next
+    }
+    __syncthreads();
     {
         // AT rows 0-63 <- T diag(beta Gam), rows 64-127 <- T diag(beta). Thread = AT row:
         // eight 16-byte swizzled chunks of 8 columns each (conflict-free row reads of Ts,
@@ -587,7 +611,6 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
             tmem_ld32(tmem + lane_base + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
             tmem_ld_wait();
         }
-        const float glast_prev = ms->gprev[kC - 1];
         uint8_t* stg = smem + kAT + row * 128;
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
@@ -597,8 +620,8 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     const int s0 = q * 8 + 2 * u;
-                    float m0 = __uint_as_float(v[s0]) * __expf(glast_prev - ms->gprev[s0]);
-                    float m1 = __uint_as_float(v[s0 + 1]) * __expf(glast_prev - ms->gprev[s0 + 1]);
+                    float m0 = __uint_as_float(v[s0]) * ms->mdecay[s0];
+                    float m1 = __uint_as_float(v[s0 + 1]) * ms->mdecay[s0 + 1];
                     if constexpr (kFused) {
                         m0 *= ms->rkp[s0];
                         m1 *= ms->rkp[s0 + 1];
