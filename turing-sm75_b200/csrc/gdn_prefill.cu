@@ -693,7 +693,9 @@ constexpr uint32_t kColX1 = 0, kColDS = 64, kColRQ = 128;
 struct Misc {
     uint64_t full[kStages], empty[kStages];
     uint64_t pro_full, pro_done;
-    uint64_t s_ready[2], v_ready;
+    uint64_t s_ready[2];
+    uint64_t vn_ready;  // Vn_c written: the chain product X1(c) may run
+    uint64_t vt_ready;  // decayed Vn_c written: the state increment DS(c) may run
     uint64_t x1_full[2], ds_full[2], rq_full[2];
     uint64_t o_done[2];  // the output warps have read X1 / RQ buffer (c & 1) of chunk c
     uint64_t drain_a, drain_b;
@@ -773,13 +775,14 @@ __global__ void __launch_bounds__(st::kThreads, 1)
         mbar_init(&ms->pro_full, 1);
         mbar_init(&ms->pro_done, 1);
         for (int i = 0; i < 2; ++i) {
-            mbar_init(&ms->s_ready[i], 128);
+            mbar_init(&ms->s_ready[i], 4);  // one arrival per state warp
             mbar_init(&ms->x1_full[i], 1);
             mbar_init(&ms->ds_full[i], 1);
             mbar_init(&ms->rq_full[i], 1);
-            mbar_init(&ms->o_done[i], 64);
+            mbar_init(&ms->o_done[i], 2);   // one per output warp
         }
-        mbar_init(&ms->v_ready, 64);
+        mbar_init(&ms->vn_ready, 2);        // one per Vn warp
+        mbar_init(&ms->vt_ready, 2);
         mbar_init(&ms->drain_a, 1);
         mbar_init(&ms->drain_b, 1);
         ms->abort = 0;
@@ -845,15 +848,19 @@ __global__ void __launch_bounds__(st::kThreads, 1)
                 const int s = c % kStages;
                 const uint32_t so = (s * kStage) >> 4;
                 const uint32_t buf = (c & 1) * 32;
+                // Vn_c is the chain dependency, so it is waited for last: every wait between
+                // it and the MMAs would lengthen the chain
                 if (!mbar_wait(&ms->full[s], (c / kStages) & 1, abort, &g_err_gdn_prefill)) break;
-                if (!mbar_wait(&ms->v_ready, c & 1, abort, &g_err_gdn_prefill)) break;
                 if (c >= 2 && !mbar_wait(&ms->o_done[c & 1], ((c - 2) >> 1) & 1, abort, &g_err_gdn_prefill)) break;
+                if (!mbar_wait(&ms->vn_ready, c & 1, abort, &g_err_gdn_prefill)) break;
                 tc_fence_after();
 #pragma unroll
                 for (int kk = 0; kk < kC / 16; ++kk)
                     mma_f16_ss(tmem + kColX1 + buf, dAM + so + ((kk * 32) >> 4), dVn + ((kk * 1024) >> 4), id_kb,
                                kk > 0 ? 1u : 0u);
                 mma_commit(&ms->x1_full[c & 1]);
+                if (!mbar_wait(&ms->vt_ready, c & 1, abort, &g_err_gdn_prefill)) break;
+                tc_fence_after();
 #pragma unroll
                 for (int kk = 0; kk < kC / 16; ++kk)
                     mma_f16_ss(tmem + kColDS + buf, dK + so + ((kk * 2048) >> 4), dVt + ((kk * 1024) >> 4), id_mn,
@@ -935,7 +942,8 @@ __global__ void __launch_bounds__(st::kThreads, 1)
                 put_row(sS, i, S);
                 fence_proxy_async_smem();
                 tc_fence_before();
-                mbar_arrive(&ms->s_ready[c & 1]);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ms->s_ready[c & 1]);
             };
             bool ok = true;
             if (p.nch > 0) publish_S(0);
@@ -982,7 +990,8 @@ __global__ void __launch_bounds__(st::kThreads, 1)
                 tmem_ld32(tmem + lane_base + kColX1 + (c & 1) * 32, oi);
                 tmem_ld_wait();
                 tc_fence_before();
-                mbar_arrive(&ms->o_done[c & 1]);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ms->o_done[c & 1]);
                 const int tt = c * kC + row;
                 if (tt < p.T) {
                     const float eg = __expf(gcs_t) * rq_t;
@@ -1005,7 +1014,7 @@ __global__ void __launch_bounds__(st::kThreads, 1)
                 const float rk_t = rk_nx;  // 1/|k_t|: K^T diag(1/|k|) Vt is the normalised keys' product
                 if (kFused && c + 1 < p.nch) rk_nx = rk_all[(bhc0 + c + 1) * kC + row];
                 const int s = c % kStages;
-                // chunk c's U row and gates from its stage (released only after v_ready(c))
+                // chunk c's U row and gates from its stage (released only after vt_ready(c))
                 if (!wait_all(&ms->full[s], (c / kStages) & 1)) break;
                 const uint8_t* stg = smem + s * kStage;
                 const float gcs_t = reinterpret_cast<const float*>(stg + kG)[row];
@@ -1034,13 +1043,19 @@ __global__ void __launch_bounds__(st::kThreads, 1)
                     u[cc] = vn;
                     vt[cc] = vn * dec;
                 }
-                // the Vt tile is free once K^T Vt of chunk c-1 is done
-                if (c > 0 && !wait_all(&ms->ds_full[(c - 1) & 1], ((c - 1) >> 1) & 1)) break;
+                // Vn_c first (its tile was read by X1(c-1), whose result is in hand), so the
+                // chain product X1(c) can start; then decayed Vn_c, once K^T Vt of chunk c-1
+                // has read the Vt tile
                 put_row(sVn, row, u);
-                put_row(sVt, row, vt);
                 fence_proxy_async_smem();
                 tc_fence_before();
-                mbar_arrive(&ms->v_ready);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ms->vn_ready);
+                if (c > 0 && !wait_all(&ms->ds_full[(c - 1) & 1], ((c - 1) >> 1) & 1)) break;
+                put_row(sVt, row, vt);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ms->vt_ready);
                 gam_prev = __expf(g_last);
             }
         }
