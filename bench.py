@@ -250,12 +250,8 @@ def bench_attention(name, cfg, args, dist, peaks):
     Oh = torch.empty(O.shape, dtype=O.dtype, pin_memory=True)
     e2e_steps = max(3, min(args.steps, 10))
 
-    def e2e_step():
-        Q.copy_(Qh, non_blocking=True)
-        K.copy_(Kh, non_blocking=True)
-        V.copy_(Vh, non_blocking=True)
-        b200lab.attn_fwd(Q, K, V, causal=causal, out=O, stream=stream)
-        Oh.copy_(O, non_blocking=True)
+    def e2e_step():  # the host-buffer entry: copies in, compute and copies out pipelined by chunk
+        b200lab.attn_fwd_host(Qh, Kh, Vh, Oh, Q, K, V, O, causal=causal, stream=stream)
 
     e2e_step()
     torch.cuda.synchronize()

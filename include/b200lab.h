@@ -72,6 +72,21 @@ int attn_fwd_sm100(const void* Q, const void* K, const void* V, void* O,
 size_t attn_fwd_sm100_workspace(int B, int Hq, int Hkv, int Sq, int Skv, int D,
                                 int causal);
 
+/* Host-buffer form of attn_fwd_sm100 (no counterpart in the reference, whose
+ * main() copies whole tensors in, launches, and copies O back, serially,
+ * src/attn_sm75.cu:404, 489-497): Qh, Kh, Vh, Oh are HOST buffers in the same
+ * layouts (pinned memory lets the copies overlap), Qd, Kd, Vd, Od caller-owned
+ * device buffers of the full sizes.  The (batch, kv-head) units are cut into
+ * about eight contiguous chunks; chunk i+1 is copied in while chunk i is
+ * computed and chunk i-1 copied out (two internal streams, joined back into
+ * `stream` before return; no device memory is allocated).  Oh is complete once
+ * `stream` reaches the point of the call.  Same arguments and status codes as
+ * attn_fwd_sm100, no workspace (no key splits). */
+int attn_fwd_sm100_host(const void* Qh, const void* Kh, const void* Vh, void* Oh,
+                        void* Qd, void* Kd, void* Vd, void* Od,
+                        int B, int Hq, int Hkv, int Sq, int Skv, int D,
+                        float scale, int causal, int dtype, void* stream);
+
 /* Packed variable-length sequences (the cu_seqlens convention serving callers
  * use; no counterpart in the reference, whose batches are dense):
  *   Q, O : [total_q][Hq][D] token-major; K, V : [total_k][Hkv][D]

@@ -132,3 +132,24 @@ def test_split_kv_without_workspace_runs_unsplit(cuda):
     assert st == b200lab.OK
     assert b200lab.device_status() == b200lab.OK
     assert_close(to_np(O2), to_np(O1), "unsplit vs split")
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,S,D,dtype", [(2, 8, 4, 384, 128, torch.bfloat16),   # 8 chunks of 1 kv-head
+                                                (3, 6, 2, 200, 64, torch.float16),     # 3 batches x 2 chunks
+                                                (1, 4, 1, 300, 256, torch.bfloat16),   # one chunk, head dim 256
+                                                (9, 2, 2, 64, 128, torch.bfloat16)])   # more batches than 8
+def test_host_buffer_pipeline_equals_device_path(cuda, B, Hq, Hkv, S, D, dtype):
+    """attn_fwd_sm100_host (host in/out, copies pipelined with the chunked launches) gives the
+    device entry's bits, and matches the oracle."""
+    dev = torch.device("cuda:0")
+    Q, K, V = workloads.attn_inputs(B, Hq, Hkv, S, D, dtype, seed=B * 100 + D, device="cpu")
+    Qh, Kh, Vh = (t.pin_memory() for t in (Q, K, V))
+    Oh = torch.full(Q.shape, 7.0, dtype=dtype).pin_memory()
+    Qd, Kd, Vd, Od = (torch.empty_like(t, device=dev) for t in (Q, K, V, Q))
+    b200lab.attn_fwd_host(Qh, Kh, Vh, Oh, Qd, Kd, Vd, Od, causal=True)
+    torch.cuda.synchronize()
+    assert b200lab.device_status() == b200lab.OK
+    O_dev = b200lab.attn_fwd(Q.to(dev), K.to(dev), V.to(dev), causal=True)
+    assert torch.equal(Oh, O_dev.cpu())
+    ref = oracle.attn_fwd(to_np(Q), to_np(K), to_np(V), 1.0 / np.sqrt(D), True)
+    assert_close(to_np(Oh), ref, "host pipeline")

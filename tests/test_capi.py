@@ -40,6 +40,8 @@ def test_null_pointers_rejected_before_launch():
     assert L.gdn_decode_sm100(n, n, n, n, n, n, n, 1, 1, 1, 128, 128, 0, 0.1, 1, 1, n) == b200lab.ERR_INVALID
     assert L.gdn_prefill_sm100(n, n, n, n, n, n, n, 1, 8, 1, 1, 128, 128, 0, 0.1, 1, 1, n, 0, n) \
         in (b200lab.ERR_INVALID, b200lab.ERR_UNSUPPORTED)
+    assert L.attn_fwd_sm100_host(n, n, n, n, n, n, n, n, 1, 1, 1, 16, 16, 128, 0.1, 0, 1, n) \
+        == b200lab.ERR_INVALID
 
 
 def test_shape_rules_rejected_before_launch():
@@ -54,6 +56,13 @@ def test_shape_rules_rejected_before_launch():
     assert L.attn_fwd_sm100(p, p, p, p, 1, 2, 2, 16, 16, 128, 0.1, 0, 7, n, 0, n) == b200lab.ERR_INVALID
     assert L.attn_fwd_sm100(p, p, p, p, 1, 2, 2, 16, 16, 128, 0.1, 2, 1, n, 0, n) == b200lab.ERR_INVALID
     assert L.attn_fwd_sm100(p, p, p, p, 1, 2, 2, 16, 16, 128, -1.0, 0, 1, n, 0, n) == b200lab.ERR_INVALID
+    # the host-buffer form applies the same rules before creating any stream
+    assert L.attn_fwd_sm100_host(p, p, p, p, p, p, p, p, 1, 3, 2, 16, 16, 128, 0.1, 0, 1, n) == b200lab.ERR_INVALID
+    assert L.attn_fwd_sm100_host(p, p, p, p, p, p, p, p, 1, 2, 2, 16, 16, 96, 0.1, 0, 1, n) \
+        == b200lab.ERR_UNSUPPORTED
+    assert L.attn_fwd_sm100_host(p, p, p, p, p, p, p, p, 1, 2, 2, 16, 16, 128, 0.1, 2, 1, n) == b200lab.ERR_INVALID
+    assert L.attn_fwd_sm100_host(p, p, p, p, p, p, p, p, 1, 2, 2, 16, 16, 128, -1.0, 0, 1, n) \
+        == b200lab.ERR_INVALID
     # decode: dk != 128, head_map 1 with Hv % Hqk != 0
     assert L.gdn_decode_sm100(p, p, p, p, p, p, p, 1, 1, 1, 64, 64, 0, 0.1, 1, 1, n) == b200lab.ERR_UNSUPPORTED
     assert L.gdn_decode_sm100(p, p, p, p, p, p, p, 1, 3, 4, 128, 128, 1, 0.1, 1, 1, n) == b200lab.ERR_INVALID

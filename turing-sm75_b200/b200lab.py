@@ -33,6 +33,7 @@ F16, BF16, F32 = 0, 1, 2
 # Every symbol include/b200lab.h declares (checked by tests/test_capi.py).
 EXPORTED = (
     "attn_fwd_sm100", "attn_fwd_sm100_workspace", "attn_gated_fwd_sm100", "attn_fwd_sm100_varlen",
+    "attn_fwd_sm100_host",
     "gdn_prefill_sm100", "gdn_prefill_sm100_workspace", "gdn_prefill_sm100_noalloc",
     "gdn_prefill_sm100_fused",
     "gdn_decode_sm100", "gdn_decode_sm100_state16", "gdn_decode_sm100_fused",
@@ -69,6 +70,8 @@ def lib() -> ctypes.CDLL:
         L.attn_fwd_sm100.argtypes = [vp, vp, vp, vp] + [ci] * 6 + [cf, ci, ci, vp, sz, vp]
         L.attn_fwd_sm100_workspace.restype = sz
         L.attn_fwd_sm100_workspace.argtypes = [ci] * 7
+        L.attn_fwd_sm100_host.restype = ci
+        L.attn_fwd_sm100_host.argtypes = [vp] * 8 + [ci] * 6 + [cf, ci, ci, vp]
         L.attn_fwd_sm100_varlen.restype = ci
         L.attn_fwd_sm100_varlen.argtypes = [vp] * 6 + [ci] * 7 + [cf, ci, ci, vp]
         L.attn_gated_fwd_sm100.restype = ci
@@ -192,6 +195,31 @@ def attn_gated_fwd(Q, K, V, G=None, *, scale: float | None = None, causal: bool 
                                     _dtype_code(Q), _stream(stream))
     _check(st, "attn_gated_fwd_sm100")
     return out
+
+
+def attn_fwd_host(Qh, Kh, Vh, Oh, Qd, Kd, Vd, Od, *, scale: float | None = None, causal: bool = False,
+                  stream=None):
+    """attn_fwd from HOST tensors (pinned for overlap): copies in, computes and copies O back
+    to Oh, pipelined over chunks of (batch, kv-head) units; Qd..Od are device tensors of the
+    same shapes used as the staging buffers.  Oh is complete when `stream` reaches this point."""
+    B, Hq, Sq, D = Qh.shape
+    _, Hkv, Skv, _ = Kh.shape
+    if Kh.shape != Vh.shape or Oh.shape != Qh.shape:
+        raise ValueError("attn_fwd_host: K/V or O shape mismatch")
+    for h, d, n in ((Qh, Qd, "Q"), (Kh, Kd, "K"), (Vh, Vd, "V"), (Oh, Od, "O")):
+        if h.device.type != "cpu" or not h.is_contiguous():
+            raise ValueError(f"attn_fwd_host: {n} host tensor must be contiguous CPU memory")
+        if d.shape != h.shape or d.dtype != h.dtype:
+            raise ValueError(f"attn_fwd_host: {n} device buffer must match the host tensor")
+    if scale is None:
+        scale = 1.0 / (D ** 0.5)
+    st = lib().attn_fwd_sm100_host(ctypes.c_void_p(Qh.data_ptr()), ctypes.c_void_p(Kh.data_ptr()),
+                                   ctypes.c_void_p(Vh.data_ptr()), ctypes.c_void_p(Oh.data_ptr()),
+                                   _dev(Qd, "Qd"), _dev(Kd, "Kd"), _dev(Vd, "Vd"), _dev(Od, "Od"),
+                                   B, Hq, Hkv, Sq, Skv, D, float(scale), int(bool(causal)), _dtype_code(Qh),
+                                   _stream(stream))
+    _check(st, "attn_fwd_sm100_host")
+    return Oh
 
 
 def attn_fwd_varlen(Q, K, V, cu_seqlens_q, cu_seqlens_k, max_seqlen_q: int, *, scale: float | None = None,

@@ -444,7 +444,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             // split-KV partial: unnormalised O, running max and sum, fp32
             if (qrow < p.Sq) {
                 const size_t prow = ((size_t)(b * p.Hq + hq) * p.Sq + qrow) * p.nsplit + split;
-                float* po = p.part_o + prow * D;
                 float2 ml = make_float2(m, l);
                 if (!(ok && nkv > 0) || m == -INFINITY) ml = make_float2(-INFINITY, 0.f);
                 *reinterpret_cast<float2*>(p.part_ml + prow * 2) = ml;
@@ -715,6 +714,98 @@ extern "C" int attn_fwd_sm100(const void* Q, const void* K, const void* V, void*
     }
     return D == 128 ? launch<128, __half>(Q, K, V, O, B, Hq, Hkv, Sq, Skv, scale, causal, workspace, ws_bytes, st)
                     : launch<64, __half>(Q, K, V, O, B, Hq, Hkv, Sq, Skv, scale, causal, workspace, ws_bytes, st);
+}
+
+// Host-buffer pipeline over attn_fwd_sm100: chunks of whole (batch, kv-head) units, each a
+// contiguous slab of Q/O ([B][Hq][Sq][D], the q-heads of a kv group adjacent) and of K/V.
+extern "C" int attn_fwd_sm100_host(const void* Qh, const void* Kh, const void* Vh, void* Oh, void* Qd, void* Kd,
+                                   void* Vd, void* Od, int B, int Hq, int Hkv, int Sq, int Skv, int D, float scale,
+                                   int causal, int dtype, void* stream) {
+    using namespace b200;
+    if (!Qh || !Kh || !Vh || !Oh || !Qd || !Kd || !Vd || !Od) return B200LAB_ERR_INVALID;
+    if (B < 1 || Hq < 1 || Hkv < 1 || Sq < 1 || Skv < 1 || Hq % Hkv != 0) return B200LAB_ERR_INVALID;
+    if (dtype != B200LAB_F16 && dtype != B200LAB_BF16) return B200LAB_ERR_INVALID;
+    if (causal != 0 && causal != 1) return B200LAB_ERR_INVALID;
+    if (!(scale > 0.f) || !(scale < 1e30f)) return B200LAB_ERR_INVALID;
+    if (D != 64 && D != 128 && D != 256) return B200LAB_ERR_UNSUPPORTED;
+    if (B > 65535 || Hq > 65535) return B200LAB_ERR_UNSUPPORTED;
+    int rc = check_device_sm100();
+    if (rc != B200LAB_OK) return rc;
+    const int group = Hq / Hkv;
+    // kv-heads per chunk: split each batch's heads only as far as needed for ~8 chunks (16
+    // measured the same on C5: the copies in, not the pipeline's fill, bound the call)
+    constexpr int kTargetChunks = 8;
+    int m = 1;  // chunks per batch, a divisor of Hkv
+    for (int d = 1; d <= Hkv; ++d)
+        if (Hkv % d == 0 && (long long)B * d <= kTargetChunks) m = d;
+    const int hc = Hkv / m;
+    const int nchunks = B * m;
+    const size_t esz = 2;
+    const size_t q_chunk = (size_t)hc * group * Sq * D * esz;  // Q or O bytes of a chunk
+    const size_t kv_chunk = (size_t)hc * Skv * D * esz;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaStream_t s_in = nullptr, s_out = nullptr;
+    cudaEvent_t ev_start = nullptr, ev_end = nullptr;
+    cudaEvent_t ev_in[64] = {}, ev_done[64] = {};
+    const int nev = nchunks < 64 ? nchunks : 64;  // events are reused round-robin past 64 chunks
+    auto fail = [&](int code) { rc = code; };
+    if (cudaStreamCreateWithFlags(&s_in, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&s_out, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ev_start, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ev_end, cudaEventDisableTiming) != cudaSuccess)
+        fail(B200LAB_ERR_CUDA);
+    for (int i = 0; rc == B200LAB_OK && i < nev; ++i)
+        if (cudaEventCreateWithFlags(&ev_in[i], cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&ev_done[i], cudaEventDisableTiming) != cudaSuccess)
+            fail(B200LAB_ERR_CUDA);
+    if (rc == B200LAB_OK) {
+        // the device buffers may still be in use by earlier work on `stream`
+        if (cudaEventRecord(ev_start, st) != cudaSuccess || cudaStreamWaitEvent(s_in, ev_start, 0) != cudaSuccess ||
+            cudaStreamWaitEvent(s_out, ev_start, 0) != cudaSuccess)
+            fail(B200LAB_ERR_CUDA);
+    }
+    const char* qh = static_cast<const char*>(Qh);
+    const char* kh = static_cast<const char*>(Kh);
+    const char* vh = static_cast<const char*>(Vh);
+    char* oh = static_cast<char*>(Oh);
+    char* qd = static_cast<char*>(Qd);
+    char* kd = static_cast<char*>(Kd);
+    char* vd = static_cast<char*>(Vd);
+    char* od = static_cast<char*>(Od);
+    for (int i = 0; rc == B200LAB_OK && i < nchunks; ++i) {
+        const size_t qo = (size_t)i * q_chunk, ko = (size_t)i * kv_chunk;
+        cudaEvent_t ein = ev_in[i % nev], edone = ev_done[i % nev];
+        if (cudaMemcpyAsync(qd + qo, qh + qo, q_chunk, cudaMemcpyHostToDevice, s_in) != cudaSuccess ||
+            cudaMemcpyAsync(kd + ko, kh + ko, kv_chunk, cudaMemcpyHostToDevice, s_in) != cudaSuccess ||
+            cudaMemcpyAsync(vd + ko, vh + ko, kv_chunk, cudaMemcpyHostToDevice, s_in) != cudaSuccess ||
+            cudaEventRecord(ein, s_in) != cudaSuccess || cudaStreamWaitEvent(st, ein, 0) != cudaSuccess) {
+            fail(B200LAB_ERR_CUDA);
+            break;
+        }
+        const int lrc = attn_fwd_sm100(qd + qo, kd + ko, vd + ko, od + qo, 1, hc * group, hc, Sq, Skv, D, scale,
+                                       causal, dtype, nullptr, 0, stream);
+        if (lrc != B200LAB_OK) {
+            fail(lrc);
+            break;
+        }
+        if (cudaEventRecord(edone, st) != cudaSuccess || cudaStreamWaitEvent(s_out, edone, 0) != cudaSuccess ||
+            cudaMemcpyAsync(oh + qo, od + qo, q_chunk, cudaMemcpyDeviceToHost, s_out) != cudaSuccess) {
+            fail(B200LAB_ERR_CUDA);
+            break;
+        }
+    }
+    // join: `stream` continues after every copy of this call, whatever happened above
+    if (s_in && ev_end && cudaEventRecord(ev_end, s_in) == cudaSuccess) cudaStreamWaitEvent(st, ev_end, 0);
+    if (s_out && ev_start && cudaEventRecord(ev_start, s_out) == cudaSuccess) cudaStreamWaitEvent(st, ev_start, 0);
+    for (int i = 0; i < nev; ++i) {
+        if (ev_in[i]) cudaEventDestroy(ev_in[i]);
+        if (ev_done[i]) cudaEventDestroy(ev_done[i]);
+    }
+    if (ev_start) cudaEventDestroy(ev_start);
+    if (ev_end) cudaEventDestroy(ev_end);
+    if (s_in) cudaStreamDestroy(s_in);
+    if (s_out) cudaStreamDestroy(s_out);
+    return rc;
 }
 
 extern "C" int attn_fwd_sm100_varlen(const void* Q, const void* K, const void* V, void* O, const int* cu_seqlens_q,
