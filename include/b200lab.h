@@ -240,6 +240,14 @@ const char* b200lab_strerror(int status);
  * B200LAB_OK.  The reference's equivalent is CUDA_CHECK -> exit(1)
  * (src/attn_sm75.cu:40-48); this library reports instead of exiting. */
 int b200lab_device_status(void* stream);
+/* Failure-path self-test (no counterpart in the reference): launches on
+ * `stream` a one-thread kernel whose bounded wait is on a barrier that nothing
+ * completes, so it gives up after the wait limit (1 s of GPU time) and records
+ * B200LAB_ERR_TIMEOUT, exactly as a kernel of this library does when a
+ * partner it waits for never arrives; the next b200lab_device_status() returns
+ * that status and the context stays usable.  Nothing faults or traps.  Returns
+ * the launch status. */
+int b200lab_watchdog_selftest(void* stream);
 /* Library version, major*10000 + minor*100 + patch. */
 int b200lab_version(void);
 /* Number of kernels this library has enqueued in this process (all devices,

@@ -39,6 +39,7 @@ EXPORTED = (
     "gdn_decode_sm100", "gdn_decode_sm100_state16", "gdn_decode_sm100_fused",
     "gdn_decode_sm100_slots",
     "b200lab_strerror", "b200lab_device_status", "b200lab_version", "b200lab_launch_count",
+    "b200lab_watchdog_selftest",
 )
 
 _LIB = None
@@ -96,6 +97,8 @@ def lib() -> ctypes.CDLL:
         L.b200lab_strerror.argtypes = [ci]
         L.b200lab_device_status.restype = ci
         L.b200lab_device_status.argtypes = [vp]
+        L.b200lab_watchdog_selftest.restype = ci
+        L.b200lab_watchdog_selftest.argtypes = [vp]
         L.b200lab_version.restype = ci
         L.b200lab_version.argtypes = []
         L.b200lab_launch_count.restype = ctypes.c_ulonglong
@@ -380,3 +383,9 @@ def launch_count() -> int:
 def device_status(stream=None) -> int:
     """Synchronise and return the library's device status (0 = no wait gave up)."""
     return int(lib().b200lab_device_status(_stream(stream)))
+
+
+def watchdog_selftest(stream=None) -> None:
+    """Enqueue the failure-path self-test: a kernel whose bounded wait never completes and
+    gives up after the wait limit; the next device_status() returns ERR_TIMEOUT."""
+    _check(lib().b200lab_watchdog_selftest(_stream(stream)), "b200lab_watchdog_selftest")

@@ -8,6 +8,7 @@ int take_err_attn();
 int take_err_attn_gated();
 int take_err_gdn_prefill();
 int take_err_gdn_decode();
+int take_err_watchdog();
 }  // namespace b200
 
 // Defines take_err_<name>() for the translation unit's error word `sym`.

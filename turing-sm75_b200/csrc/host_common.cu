@@ -34,6 +34,23 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 static std::atomic<unsigned long long> g_launches{0};
+
+__device__ int g_err_watchdog = 0;
+
+// One thread waits on a barrier that nothing arrives on: the bounded wait gives up after
+// kWaitLimitNs and records B200LAB_ERR_TIMEOUT, as any kernel here does when a partner
+// never arrives.
+__global__ void watchdog_selftest_kernel() {
+    __shared__ uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        abort_flag = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) mbar_wait(&bar, 0, &abort_flag, &g_err_watchdog);
+}
 void count_launch(int n) { g_launches.fetch_add((unsigned long long)n, std::memory_order_relaxed); }
 
 int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes,
@@ -71,6 +88,16 @@ int make_tmap_4d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
 
 }  // namespace b200
 
+B200_DEFINE_ERR_TAKER(watchdog, b200::g_err_watchdog)
+
+extern "C" int b200lab_watchdog_selftest(void* stream) {
+    int rc = b200::check_device_sm100();
+    if (rc != B200LAB_OK) return rc;
+    b200::watchdog_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>();
+    b200::count_launch(1);
+    return cudaGetLastError() == cudaSuccess ? B200LAB_OK : B200LAB_ERR_CUDA;
+}
+
 extern "C" const char* b200lab_strerror(int status) {
     switch (status) {
         case B200LAB_OK: return "ok";
@@ -95,7 +122,7 @@ extern "C" int b200lab_device_status(void* stream) {
         return B200LAB_ERR_CUDA;
     int worst = B200LAB_OK;
     const int words[] = {b200::take_err_attn(), b200::take_err_attn_gated(), b200::take_err_gdn_prefill(),
-                         b200::take_err_gdn_decode()};
+                         b200::take_err_gdn_decode(), b200::take_err_watchdog()};
     for (int w : words) {
         if (w == B200LAB_ERR_CUDA) return B200LAB_ERR_CUDA;
         if (w != B200LAB_OK) worst = w;
