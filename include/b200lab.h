@@ -136,6 +136,21 @@ int gdn_prefill_sm100(const void* q, const void* k, const void* v,
                       void* workspace, size_t ws_bytes, void* stream);
 size_t gdn_prefill_sm100_workspace(int B, int T, int Hqk, int Hv, int dk, int dv);
 
+/* Packed variable-length sequences (no counterpart in the reference, whose
+ * prefill runs one sequence, src/gdn_sm75.cu:1246-1412): q, k [total][Hqk][dk],
+ * v, o [total][Hv][dv], g_log, beta [total][Hv]; cu_seqlens device int32 [B+1]
+ * (sequence b is tokens [cu[b], cu[b+1]), total_tokens = cu[B]); state
+ * [B][Hv][dv][dk], one per sequence, updated in place (an empty sequence keeps
+ * its state).  Chunks start at each sequence's first token, so sequence b's
+ * outputs and state are those of a B = 1 call on it alone.  Workspace:
+ * gdn_prefill_sm100_workspace(B, max_seqlen, ...). */
+int gdn_prefill_sm100_varlen(const void* q, const void* k, const void* v,
+                             const float* g_log, const float* beta, float* state, void* o,
+                             const int* cu_seqlens, int max_seqlen, int total_tokens,
+                             int B, int Hqk, int Hv, int dk, int dv, int head_map,
+                             float scale, int in_dtype, int out_dtype,
+                             void* workspace, size_t ws_bytes, void* stream);
+
 /* ---- Gated DeltaNet chunked prefill without any allocation ----------------
  * No counterpart in the reference: it has no library, so nothing there
  * allocates on a caller's behalf.  This entry is for callers that cannot call

@@ -68,8 +68,22 @@ struct PrepParams {
     const float* A_log;    // fused: [Hv] or null
     const float* dt_bias;  // fused: [Hv] or null
     size_t ws_u, ws_aqk, ws_gcs, ws_rq, ws_rk;
-    int T, Hqk, Hv, nch, head_map;
+    const int* cu;  // packed sequences: [B+1] token offsets (device), or null: B x T dense
+    int T, Hqk, Hv, nch, head_map;  // with cu, T is the longest sequence; nch = ceil(T / 64)
 };
+
+// Tokens are addressed in one flattened sequence dimension ([B*T] dense, [total] packed), so
+// chunk c of sequence b starts at token seq_start + 64 c.  The last chunk of a sequence may
+// read the next sequence's rows (or zero fill past the end): those tokens get g = beta = 0,
+// which zeroes every product they could enter (their A, W and U rows, their columns of W and
+// U through beta, their Vn rows), and their outputs are not stored.
+struct SeqSpan {
+    int start, len;
+};
+__device__ __forceinline__ SeqSpan seq_span(const int* cu, int T, int b) {
+    if (cu) return SeqSpan{cu[b], cu[b + 1] - cu[b]};
+    return SeqSpan{b * T, T};
+}
 
 // Fused pre-processing (gdn_prefill_sm100_fused): q, k arrive raw and are L2-normalised,
 // x * rsqrt(sum x^2 + kNormEps) over dk; the gates come as logits,
@@ -269,11 +283,14 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
     float* Xs = reinterpret_cast<float*>(smem + kXs);
     volatile int* abort = &ms->abort;
 
-    const int c = blockIdx.x;   // chunk
+    const int c = blockIdx.x;   // chunk of the sequence
     const int h = blockIdx.y;   // v-head
-    const int b = blockIdx.z;
-    const int hq = qk_head(h, p.Hqk, p.Hv, p.head_map);
+    const int b = blockIdx.z;   // sequence
+    const SeqSpan seq = seq_span(p.cu, p.T, b);
     const int t0 = c * kC;
+    if (t0 >= seq.len) return;  // packed: a shorter sequence has fewer chunks
+    const int hq = qk_head(h, p.Hqk, p.Hv, p.head_map);
+    const int tok0 = seq.start + t0;  // first token of the chunk in the flattened dimension
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
     const size_t bhc = ((size_t)b * p.Hv + h) * p.nch + c;
@@ -285,13 +302,13 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
     // previous (always full) chunk's g_log, for M
     float g_in = 0.f, be_in = 0.f;
     if (tid < kC) {
-        if (t0 + tid < p.T) {
-            const size_t gi = ((size_t)b * p.T + t0 + tid) * p.Hv + h;
+        if (t0 + tid < seq.len) {
+            const size_t gi = ((size_t)tok0 + tid) * p.Hv + h;
             g_in = p.g_log[gi];
             be_in = p.beta[gi];
         }
     } else if (c > 0) {
-        g_in = p.g_log[((size_t)b * p.T + (t0 - kC + tid - kC)) * p.Hv + h];
+        g_in = p.g_log[((size_t)tok0 - kC + tid - kC) * p.Hv + h];
     }
 
     if (tid == 0) {
@@ -316,16 +333,16 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
 
     if (tid == 0) {
         mbar_arrive_expect_tx(&ms->bar_tma, 4 * 8192);
-        tma_load_4d(smem + kK0, &tmK, &ms->bar_tma, 0, hq, t0, b);
-        tma_load_4d(smem + kK1, &tmK, &ms->bar_tma, 64, hq, t0, b);
-        tma_load_4d(smem + kQ0, &tmQ, &ms->bar_tma, 0, hq, t0, b);
-        tma_load_4d(smem + kQ1, &tmQ, &ms->bar_tma, 64, hq, t0, b);
+        tma_load_4d(smem + kK0, &tmK, &ms->bar_tma, 0, hq, tok0, 0);
+        tma_load_4d(smem + kK1, &tmK, &ms->bar_tma, 64, hq, tok0, 0);
+        tma_load_4d(smem + kQ0, &tmQ, &ms->bar_tma, 0, hq, tok0, 0);
+        tma_load_4d(smem + kQ1, &tmQ, &ms->bar_tma, 64, hq, tok0, 0);
     }
     // gates: gcs = inclusive prefix sum of g_log over the chunk (padded tokens: g=0, beta=0)
     if (tid < kC) {
         float g = g_in, be = be_in;
         if constexpr (kFused) {
-            if (t0 + tid < p.T) {
+            if (t0 + tid < seq.len) {
                 g = fused_gate(g, p, h);
                 be = 1.f / (1.f + __expf(-be));
             }
@@ -392,8 +409,8 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
     if (tid == 0 && ok) {
         // Q has been read: V goes over it (needed only by MMA2, after the solve)
         mbar_arrive_expect_tx(&ms->bar_v, 2 * 8192);
-        tma_load_4d(smem + kV0, &tmV, &ms->bar_v, 0, h, t0, b);
-        tma_load_4d(smem + kV1, &tmV, &ms->bar_v, 64, h, t0, b);
+        tma_load_4d(smem + kV0, &tmV, &ms->bar_v, 0, h, tok0, 0);
+        tma_load_4d(smem + kV1, &tmV, &ms->bar_v, 64, h, tok0, 0);
     }
     tc_fence_after();
     const int row = (warp & 1) * 32 + lane;  // token within the chunk
@@ -504,8 +521,8 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
         if (c > 0) {
             // K of the previous chunk into the (now dead) A tile, for M below
             mbar_arrive_expect_tx(&ms->bar_kp, 2 * 8192);
-            tma_load_4d(smem + kAs, &tmK, &ms->bar_kp, 0, hq, t0 - kC, b);
-            tma_load_4d(smem + kAs + 8192, &tmK, &ms->bar_kp, 64, hq, t0 - kC, b);
+            tma_load_4d(smem + kAs, &tmK, &ms->bar_kp, 0, hq, tok0 - kC, 0);
+            tma_load_4d(smem + kAs + 8192, &tmK, &ms->bar_kp, 64, hq, tok0 - kC, 0);
         }
         tc_fence_after();
         const uint32_t bk = smem_u32(smem + kK0);
@@ -721,6 +738,7 @@ struct StateParams {
     float* state;
     void* o;
     size_t ws_gcs, ws_rq, ws_rk;
+    const int* cu;  // as PrepParams
     int T, Hqk, Hv, nch, head_map;
     float scale;
 };
@@ -761,11 +779,14 @@ __global__ void __launch_bounds__(st::kThreads, 1)
     const int slice = blockIdx.x;
     const int h = blockIdx.y;
     const int b = blockIdx.z;
+    const SeqSpan seq = seq_span(p.cu, p.T, b);
+    const int nch = (seq.len + kC - 1) / kC;  // this sequence's chunks (p.nch for the longest)
+    if (nch == 0) return;                     // an empty sequence: its state stays as it is
     const int c0 = slice * kSlice;
     const int hq = qk_head(h, p.Hqk, p.Hv, p.head_map);
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
-    const size_t bh = (size_t)b * p.Hv + h;
+    const size_t bh = (size_t)b * p.Hv + h;  // workspace slots: p.nch chunks a (sequence, head)
 
     if (tid == 0) {
         for (int i = 0; i < kStages; ++i) {
@@ -809,7 +830,7 @@ __global__ void __launch_bounds__(st::kThreads, 1)
             tma_load_3d(pro + 8192, &tmW, &ms->pro_full, 0, 0, bhc0);
             tma_load_3d(pro + 24576, &tmW, &ms->pro_full, 64, 0, bhc0);
             int issued = 0;
-            for (int c = 0; c < p.nch; ++c) {
+            for (int c = 0; c < nch; ++c) {
                 const int s = c % kStages;
                 if (!mbar_wait(&ms->empty[s], ((c / kStages) & 1) ^ 1, abort, &g_err_gdn_prefill)) break;
                 if (c == kStages - 1 && !mbar_wait(&ms->pro_done, 0, abort, &g_err_gdn_prefill)) break;
@@ -819,12 +840,12 @@ __global__ void __launch_bounds__(st::kThreads, 1)
                 // W_{c+1}, M_{c+1} of the last chunk read the next sequence's first chunk (or
                 // zero fill past the end): those rows of the products are not used
                 mbar_arrive_expect_tx(bar, kStageTx);
-                tma_load_4d(stg + kA1 + 0, &tmQ, bar, 0, hq, c * kC, b);
+                tma_load_4d(stg + kA1 + 0, &tmQ, bar, 0, hq, seq.start + c * kC, 0);
                 tma_load_3d(stg + kA1 + 8192, &tmW, bar, 0, 0, bhc + 1);
-                tma_load_4d(stg + kA1 + 16384, &tmQ, bar, 64, hq, c * kC, b);
+                tma_load_4d(stg + kA1 + 16384, &tmQ, bar, 64, hq, seq.start + c * kC, 0);
                 tma_load_3d(stg + kA1 + 24576, &tmW, bar, 64, 0, bhc + 1);
-                tma_load_4d(stg + kKt, &tmK, bar, 0, hq, c * kC, b);
-                tma_load_4d(stg + kKt + 8192, &tmK, bar, 64, hq, c * kC, b);
+                tma_load_4d(stg + kKt, &tmK, bar, 0, hq, seq.start + c * kC, 0);
+                tma_load_4d(stg + kKt + 8192, &tmK, bar, 64, hq, seq.start + c * kC, 0);
                 tma_load_3d(stg + kAM, &tmAqk, bar, 0, 0, bhc);
                 tma_load_3d(stg + kAM + 8192, &tmM, bar, 0, 0, bhc + 1);
                 tma_load_3d(stg + kU, &tmU, bar, c0, 0, bhc);
@@ -844,7 +865,7 @@ __global__ void __launch_bounds__(st::kThreads, 1)
             const uint64_t dK = smem_desc(smem_u32(smem + kKt), 8192, 1024, kLayoutSW128);
             const uint64_t dVn = smem_desc(smem_u32(smem + kVn), 4096, 512, kLayoutSW64);
             const uint64_t dVt = smem_desc(smem_u32(smem + kVt), 4096, 512, kLayoutSW64);
-            for (int c = 0; c < p.nch; ++c) {
+            for (int c = 0; c < nch; ++c) {
                 const int s = c % kStages;
                 const uint32_t so = (s * kStage) >> 4;
                 const uint32_t buf = (c & 1) * 32;
@@ -894,7 +915,7 @@ __global__ void __launch_bounds__(st::kThreads, 1)
                 mma_commit(&ms->rq_full[1]);
                 mma_commit(&ms->pro_done);
             }
-            for (int c = 0; ok && c < p.nch; ++c) {
+            for (int c = 0; ok && c < nch; ++c) {
                 const int s = c % kStages;
                 if (!mbar_wait(&ms->full[s], (c / kStages) & 1, abort, &g_err_gdn_prefill)) break;
                 if (c > 0 && !mbar_wait(&ms->s_ready[c & 1], (c >> 1) & 1, abort, &g_err_gdn_prefill)) break;
@@ -946,11 +967,11 @@ __global__ void __launch_bounds__(st::kThreads, 1)
                 if (lane == 0) mbar_arrive(&ms->s_ready[c & 1]);
             };
             bool ok = true;
-            if (p.nch > 0) publish_S(0);
-            float glast_nx = p.nch > 0 ? gcs_all[bhc0 * kC + kC - 1] : 0.f;
-            for (int c = 0; c < p.nch; ++c) {
+            publish_S(0);
+            float glast_nx = gcs_all[bhc0 * kC + kC - 1];
+            for (int c = 0; c < nch; ++c) {
                 const float gam = __expf(glast_nx);
-                if (c + 1 < p.nch) glast_nx = gcs_all[(bhc0 + c + 1) * kC + kC - 1];
+                if (c + 1 < nch) glast_nx = gcs_all[(bhc0 + c + 1) * kC + kC - 1];
                 if (!wait_all(&ms->ds_full[c & 1], (c >> 1) & 1)) { ok = false; break; }
                 tc_fence_after();
                 uint32_t ds[32];
@@ -958,7 +979,7 @@ __global__ void __launch_bounds__(st::kThreads, 1)
                 tmem_ld_wait();
 #pragma unroll
                 for (int cc = 0; cc < kSlice; ++cc) S[cc] = fmaf(gam, S[cc], __uint_as_float(ds[cc]));
-                if (c + 1 < p.nch) {
+                if (c + 1 < nch) {
                     // the S tile is rewritten only once the RQ product that reads S_c is done
                     if (!wait_all(&ms->rq_full[c & 1], st::rq_parity(c))) { ok = false; break; }
                     tc_fence_after();
@@ -973,12 +994,12 @@ __global__ void __launch_bounds__(st::kThreads, 1)
             // ---- outputs: o_c = scale (e^{gcs} Q_c S_c^T + Aqk_c Vn_c), token row ----
             const int row = tid - kWarpOut * 32;  // 0..63 = TMEM lane
             const float* rq_all = reinterpret_cast<const float*>(p.ws + p.ws_rq);
-            float gcs_nx = p.nch > 0 ? gcs_all[bhc0 * kC + row] : 0.f;
-            float rq_nx = (kFused && p.nch > 0) ? rq_all[bhc0 * kC + row] : 1.f;
-            for (int c = 0; c < p.nch; ++c) {
+            float gcs_nx = gcs_all[bhc0 * kC + row];
+            float rq_nx = kFused ? rq_all[bhc0 * kC + row] : 1.f;
+            for (int c = 0; c < nch; ++c) {
                 const float gcs_t = gcs_nx;
                 const float rq_t = rq_nx;  // 1/|q_t| (fused pre-processing)
-                if (c + 1 < p.nch) {
+                if (c + 1 < nch) {
                     gcs_nx = gcs_all[(bhc0 + c + 1) * kC + row];
                     if constexpr (kFused) rq_nx = rq_all[(bhc0 + c + 1) * kC + row];
                 }
@@ -993,13 +1014,13 @@ __global__ void __launch_bounds__(st::kThreads, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&ms->o_done[c & 1]);
                 const int tt = c * kC + row;
-                if (tt < p.T) {
+                if (tt < seq.len) {
                     const float eg = __expf(gcs_t) * rq_t;
                     float ov[kSlice];
 #pragma unroll
                     for (int cc = 0; cc < kSlice; ++cc)
                         ov[cc] = p.scale * fmaf(eg, __uint_as_float(pq[cc]), __uint_as_float(oi[cc]));
-                    store_row32(static_cast<TOut*>(p.o) + (((size_t)b * p.T + tt) * p.Hv + h) * kD + c0, ov);
+                    store_row32(static_cast<TOut*>(p.o) + (((size_t)seq.start + tt) * p.Hv + h) * kD + c0, ov);
                 }
             }
         } else {
@@ -1008,11 +1029,11 @@ __global__ void __launch_bounds__(st::kThreads, 1)
             uint8_t* sVn = smem + kVn;
             uint8_t* sVt = smem + kVt;
             const float* rk_all = reinterpret_cast<const float*>(p.ws + p.ws_rk);
-            float rk_nx = (kFused && p.nch > 0) ? rk_all[bhc0 * kC + row] : 1.f;
+            float rk_nx = kFused ? rk_all[bhc0 * kC + row] : 1.f;
             float gam_prev = 1.f;
-            for (int c = 0; c < p.nch; ++c) {
+            for (int c = 0; c < nch; ++c) {
                 const float rk_t = rk_nx;  // 1/|k_t|: K^T diag(1/|k|) Vt is the normalised keys' product
-                if (kFused && c + 1 < p.nch) rk_nx = rk_all[(bhc0 + c + 1) * kC + row];
+                if (kFused && c + 1 < nch) rk_nx = rk_all[(bhc0 + c + 1) * kC + row];
                 const int s = c % kStages;
                 // chunk c's U row and gates from its stage (released only after vt_ready(c))
                 if (!wait_all(&ms->full[s], (c / kStages) & 1)) break;
@@ -1079,10 +1100,12 @@ struct Fuse {
     const float* dt_bias;
 };
 
+// Packed sequences: cu is the device [B+1] token-offset array and ntok its last entry; dense
+// B x T: cu = null, ntok = B * T.  T is the (longest) sequence length.
 template <typename T16, typename TOut>
 int launch(const void* q, const void* k, const void* v, const float* g_log, const float* beta,
            float* state, void* o, int B, int T, int Hqk, int Hv, int head_map, float scale,
-           void* ws, cudaStream_t stream, Fuse fuse) {
+           void* ws, cudaStream_t stream, Fuse fuse, const int* cu, int ntok) {
     const int nch = (T + kC - 1) / kC;
     const size_t nbhc = (size_t)B * Hv * nch;
     const WsLayout L = ws_layout(nbhc);
@@ -1090,9 +1113,9 @@ int launch(const void* q, const void* k, const void* v, const float* g_log, cons
                                                         : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
     CUtensorMap tq, tk, tv, tw, ta;
     int rc;
-    if ((rc = make_tmap_4d(&tq, q, dt, 2, kD, Hqk, T, B, 64, 1, kC, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
-    if ((rc = make_tmap_4d(&tk, k, dt, 2, kD, Hqk, T, B, 64, 1, kC, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
-    if ((rc = make_tmap_4d(&tv, v, dt, 2, kD, Hv, T, B, 64, 1, kC, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
+    if ((rc = make_tmap_4d(&tq, q, dt, 2, kD, Hqk, ntok, 1, 64, 1, kC, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
+    if ((rc = make_tmap_4d(&tk, k, dt, 2, kD, Hqk, ntok, 1, 64, 1, kC, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
+    if ((rc = make_tmap_4d(&tv, v, dt, 2, kD, Hv, ntok, 1, 64, 1, kC, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
     uint8_t* wsb = static_cast<uint8_t*>(ws);
     if ((rc = make_tmap_3d(&tw, wsb + L.w, dt, 2, kD, kC, nbhc, 64, kC, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
     if ((rc = make_tmap_3d(&ta, wsb + L.aqk, dt, 2, kC, kC, nbhc, 64, kC, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
@@ -1113,6 +1136,7 @@ int launch(const void* q, const void* k, const void* v, const float* g_log, cons
     pp.ws_rk = L.rk;
     pp.A_log = fuse.A_log;
     pp.dt_bias = fuse.dt_bias;
+    pp.cu = cu;
     pp.T = T;
     pp.Hqk = Hqk;
     pp.Hv = Hv;
@@ -1130,6 +1154,7 @@ int launch(const void* q, const void* k, const void* v, const float* g_log, cons
     sp.ws_gcs = L.gcs;
     sp.ws_rq = L.rq;
     sp.ws_rk = L.rk;
+    sp.cu = cu;
     sp.T = T;
     sp.Hqk = Hqk;
     sp.Hv = Hv;
@@ -1158,14 +1183,15 @@ int launch(const void* q, const void* k, const void* v, const float* g_log, cons
 template <typename T16>
 int dispatch_out(int out_dtype, const void* q, const void* k, const void* v, const float* g,
                  const float* be, float* state, void* o, int B, int T, int Hqk, int Hv, int hm,
-                 float scale, void* ws, cudaStream_t s, Fuse f) {
+                 float scale, void* ws, cudaStream_t s, Fuse f, const int* cu, int ntok) {
     switch (out_dtype) {
         case B200LAB_F16:
-            return launch<T16, __half>(q, k, v, g, be, state, o, B, T, Hqk, Hv, hm, scale, ws, s, f);
+            return launch<T16, __half>(q, k, v, g, be, state, o, B, T, Hqk, Hv, hm, scale, ws, s, f, cu, ntok);
         case B200LAB_BF16:
-            return launch<T16, __nv_bfloat16>(q, k, v, g, be, state, o, B, T, Hqk, Hv, hm, scale, ws, s, f);
+            return launch<T16, __nv_bfloat16>(q, k, v, g, be, state, o, B, T, Hqk, Hv, hm, scale, ws, s, f, cu,
+                                              ntok);
         case B200LAB_F32:
-            return launch<T16, float>(q, k, v, g, be, state, o, B, T, Hqk, Hv, hm, scale, ws, s, f);
+            return launch<T16, float>(q, k, v, g, be, state, o, B, T, Hqk, Hv, hm, scale, ws, s, f, cu, ntok);
     }
     return B200LAB_ERR_UNSUPPORTED;
 }
@@ -1188,12 +1214,15 @@ extern "C" size_t gdn_prefill_sm100_workspace(int B, int T, int Hqk, int Hv, int
 
 namespace b200 {
 namespace {
+// cu / ntok: packed sequences (T = the longest), or null / unused for dense B x T
 int prefill_entry(const void* q, const void* k, const void* v, const float* g_log, const float* beta,
                   float* state, void* o, int B, int T, int Hqk, int Hv, int dk, int dv, int head_map,
                   float scale, int in_dtype, int out_dtype, void* workspace, size_t ws_bytes, void* stream,
-                  Fuse fuse) {
+                  Fuse fuse, const int* cu = nullptr, int ntok = 0) {
     if (!q || !k || !v || !g_log || !beta || !state || !o) return B200LAB_ERR_INVALID;
     if (B < 1 || T < 0 || Hqk < 1 || Hv < 1 || dk < 1 || dv < 1) return B200LAB_ERR_INVALID;
+    if (cu && ntok < 1) return B200LAB_ERR_INVALID;
+    if (!cu && (long long)B * T > 0x7fffffffLL) return B200LAB_ERR_UNSUPPORTED;
     if (head_map != 0 && head_map != 1) return B200LAB_ERR_INVALID;
     if (head_map == 1 && Hv % Hqk != 0) return B200LAB_ERR_INVALID;
     if (in_dtype < B200LAB_F16 || in_dtype > B200LAB_F32) return B200LAB_ERR_INVALID;
@@ -1210,11 +1239,12 @@ int prefill_entry(const void* q, const void* k, const void* v, const float* g_lo
     int rc = check_device_sm100();
     if (rc != B200LAB_OK) return rc;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (!cu) ntok = B * T;
     if (in_dtype == B200LAB_BF16)
         return dispatch_out<__nv_bfloat16>(out_dtype, q, k, v, g_log, beta, state, o, B, T, Hqk, Hv,
-                                           head_map, scale, workspace, s, fuse);
+                                           head_map, scale, workspace, s, fuse, cu, ntok);
     return dispatch_out<__half>(out_dtype, q, k, v, g_log, beta, state, o, B, T, Hqk, Hv, head_map,
-                                scale, workspace, s, fuse);
+                                scale, workspace, s, fuse, cu, ntok);
 }
 }  // namespace
 }  // namespace b200
@@ -1226,6 +1256,18 @@ extern "C" int gdn_prefill_sm100(const void* q, const void* k, const void* v, co
     return b200::prefill_entry(q, k, v, g_log, beta, state, o, B, T, Hqk, Hv, dk, dv, head_map, scale,
                                in_dtype, out_dtype, workspace, ws_bytes, stream,
                                b200::Fuse{false, nullptr, nullptr});
+}
+
+extern "C" int gdn_prefill_sm100_varlen(const void* q, const void* k, const void* v, const float* g_log,
+                                        const float* beta, float* state, void* o, const int* cu_seqlens,
+                                        int max_seqlen, int total_tokens, int B, int Hqk, int Hv, int dk,
+                                        int dv, int head_map, float scale, int in_dtype, int out_dtype,
+                                        void* workspace, size_t ws_bytes, void* stream) {
+    if (!cu_seqlens) return B200LAB_ERR_INVALID;
+    if (max_seqlen < 1 || total_tokens < 1) return B200LAB_ERR_INVALID;
+    return b200::prefill_entry(q, k, v, g_log, beta, state, o, B, max_seqlen, Hqk, Hv, dk, dv, head_map, scale,
+                               in_dtype, out_dtype, workspace, ws_bytes, stream,
+                               b200::Fuse{false, nullptr, nullptr}, cu_seqlens, total_tokens);
 }
 
 extern "C" int gdn_prefill_sm100_fused(const void* q, const void* k, const void* v, const float* a,
