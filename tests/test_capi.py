@@ -42,6 +42,12 @@ def test_null_pointers_rejected_before_launch():
         in (b200lab.ERR_INVALID, b200lab.ERR_UNSUPPORTED)
     assert L.attn_fwd_sm100_host(n, n, n, n, n, n, n, n, 1, 1, 1, 16, 16, 128, 0.1, 0, 1, n) \
         == b200lab.ERR_INVALID
+    p = ctypes.c_void_p(16)  # never dereferenced
+    # packed GDN prefill: no cu_seqlens, or no tokens
+    assert L.gdn_prefill_sm100_varlen(p, p, p, p, p, p, p, n, 64, 64, 1, 1, 1, 128, 128, 0, 0.1, 1, 1, p, 1 << 20, n) \
+        == b200lab.ERR_INVALID
+    assert L.gdn_prefill_sm100_varlen(p, p, p, p, p, p, p, p, 64, 0, 1, 1, 1, 128, 128, 0, 0.1, 1, 1, p, 1 << 20, n) \
+        == b200lab.ERR_INVALID
 
 
 def test_shape_rules_rejected_before_launch():
