@@ -191,6 +191,16 @@ int gdn_prefill_sm100_fused(const void* q, const void* k, const void* v,
                             int Hqk, int Hv, int dk, int dv, int head_map, float scale,
                             int in_dtype, int out_dtype, void* workspace, size_t ws_bytes,
                             void* stream);
+/* The same with packed sequences (cu_seqlens, as gdn_prefill_sm100_varlen):
+ * raw q, k [total][Hqk][dk], logits a, b [total][Hv]. */
+int gdn_prefill_sm100_fused_varlen(const void* q, const void* k, const void* v,
+                                   const float* a, const float* b,
+                                   const float* A_log, const float* dt_bias,
+                                   float* state, void* o, const int* cu_seqlens,
+                                   int max_seqlen, int total_tokens, int B, int Hqk, int Hv,
+                                   int dk, int dv, int head_map, float scale,
+                                   int in_dtype, int out_dtype,
+                                   void* workspace, size_t ws_bytes, void* stream);
 
 /* ---- Gated DeltaNet single-token decode ----------------------------------
  * Replaces the token-serial kernels with T = 1, e.g. gdn_occ8_kernel

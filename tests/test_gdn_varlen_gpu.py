@@ -52,3 +52,37 @@ def test_varlen_equals_per_sequence_calls(cuda, lens, Hqk, Hv, head_map, dtype, 
                                                 S0[i:i + 1].double().numpy(), scale, head_map)
             assert_close(to_np(o[lo:hi])[None], o_ref, f"sequence {i} vs oracle")
             assert_close(to_np(S[i])[None], S_ref, f"sequence {i} state vs oracle")
+
+
+def test_fused_varlen_equals_per_sequence_fused_calls(cuda):
+    """Raw q, k and gate / beta logits over packed sequences (gdn_prefill_sm100_fused_varlen)
+    give each sequence the bits of gdn_prefill_sm100_fused on it alone."""
+    dev = torch.device("cuda:0")
+    lens, Hqk, Hv = [70, 1, 128, 0, 33], 2, 4
+    total = sum(lens)
+    gen = torch.Generator().manual_seed(21)
+    q = (torch.randn((total, Hqk, 128), generator=gen) * 3).to(torch.bfloat16)
+    k = (torch.randn((total, Hqk, 128), generator=gen) * 3).to(torch.bfloat16)
+    v = torch.randn((total, Hv, 128), generator=gen).to(torch.bfloat16)
+    a = torch.randn((total, Hv), generator=gen)
+    bl = torch.randn((total, Hv), generator=gen)
+    A_log = torch.randn((Hv,), generator=gen) * 0.5
+    dt_bias = torch.randn((Hv,), generator=gen) * 0.5
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32)
+    S0 = workloads.gdn_state(len(lens), Hv, 128, std=0.02, seed=8)
+    S = S0.clone().to(dev)
+    d = lambda t: t.to(dev)  # noqa: E731
+    o = b200lab.gdn_prefill_fused_varlen(d(q), d(k), d(v), d(a), d(bl), S, d(cu), max(lens), A_log=d(A_log),
+                                         dt_bias=d(dt_bias), out_dtype=torch.float32)
+    assert b200lab.device_status() == b200lab.OK
+    for i, T in enumerate(lens):
+        lo, hi = int(cu[i]), int(cu[i + 1])
+        if T == 0:
+            assert torch.equal(S[i].cpu(), S0[i])
+            continue
+        Si = S0[i:i + 1].clone().to(dev)
+        oi = b200lab.gdn_prefill_fused(d(q[None, lo:hi]), d(k[None, lo:hi]), d(v[None, lo:hi]), d(a[None, lo:hi]),
+                                       d(bl[None, lo:hi]), Si, A_log=d(A_log), dt_bias=d(dt_bias),
+                                       out_dtype=torch.float32)
+        assert torch.equal(o[lo:hi].cpu(), oi[0].cpu()), f"sequence {i} outputs"
+        assert torch.equal(S[i].cpu(), Si[0].cpu()), f"sequence {i} state"

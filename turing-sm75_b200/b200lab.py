@@ -35,7 +35,7 @@ EXPORTED = (
     "attn_fwd_sm100", "attn_fwd_sm100_workspace", "attn_gated_fwd_sm100", "attn_fwd_sm100_varlen",
     "attn_fwd_sm100_host",
     "gdn_prefill_sm100", "gdn_prefill_sm100_workspace", "gdn_prefill_sm100_noalloc",
-    "gdn_prefill_sm100_fused", "gdn_prefill_sm100_varlen",
+    "gdn_prefill_sm100_fused", "gdn_prefill_sm100_varlen", "gdn_prefill_sm100_fused_varlen",
     "gdn_decode_sm100", "gdn_decode_sm100_state16", "gdn_decode_sm100_fused",
     "gdn_decode_sm100_slots",
     "b200lab_strerror", "b200lab_device_status", "b200lab_version", "b200lab_launch_count",
@@ -88,6 +88,8 @@ def lib() -> ctypes.CDLL:
         L.gdn_prefill_sm100_fused.restype = ci
         L.gdn_prefill_sm100_varlen.restype = ci
         L.gdn_prefill_sm100_varlen.argtypes = [vp] * 8 + [ci] * 8 + [cf, ci, ci, vp, sz, vp]
+        L.gdn_prefill_sm100_fused_varlen.restype = ci
+        L.gdn_prefill_sm100_fused_varlen.argtypes = [vp] * 10 + [ci] * 8 + [cf, ci, ci, vp, sz, vp]
         L.gdn_prefill_sm100_fused.argtypes = [vp] * 9 + [ci] * 7 + [cf, ci, ci, vp, sz, vp]
         L.gdn_decode_sm100_slots.restype = ci
         L.gdn_decode_sm100_slots.argtypes = [vp] * 8 + [ci] * 6 + [cf, ci, ci, vp]
@@ -304,6 +306,35 @@ def gdn_prefill_varlen(q, k, v, g_log, beta, state, cu_seqlens, max_seqlen: int,
                                         _dev(workspace, "workspace"),
                                         workspace.numel() * workspace.element_size(), _stream(stream))
     _check(st, "gdn_prefill_sm100_varlen")
+    return out
+
+
+def gdn_prefill_fused_varlen(q, k, v, a, b, state, cu_seqlens, max_seqlen: int, *, A_log=None, dt_bias=None,
+                             scale: float | None = None, head_map: int = 0, out=None, out_dtype=None,
+                             workspace=None, stream=None):
+    """gdn_prefill_fused over packed sequences: raw q,k [total,Hqk,dk]; v [total,Hv,dv]; logits
+    a,b [total,Hv] fp32; cu_seqlens [B+1] int32 on the device; state [B,Hv,dv,dk] (in place)."""
+    torch = _torch()
+    total, Hqk, dk = q.shape
+    Hv, dv = v.shape[1], v.shape[2]
+    B = cu_seqlens.numel() - 1
+    if cu_seqlens.dtype != torch.int32:
+        raise TypeError("cu_seqlens must be int32")
+    if scale is None:
+        scale = 1.0 / (dk ** 0.5)
+    if out is None:
+        out = torch.empty((total, Hv, dv), dtype=out_dtype or q.dtype, device=q.device)
+    need = gdn_prefill_workspace_bytes(B, max_seqlen, Hqk, Hv, dk, dv)
+    if workspace is None:
+        workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=q.device)
+    opt = lambda t, n: _dev(t, n) if t is not None else ctypes.c_void_p(0)  # noqa: E731
+    st = lib().gdn_prefill_sm100_fused_varlen(
+        _dev(q, "q"), _dev(k, "k"), _dev(v, "v"), _dev(a, "a"), _dev(b, "b"), opt(A_log, "A_log"),
+        opt(dt_bias, "dt_bias"), _dev(state, "state"), _dev(out, "out"), _dev(cu_seqlens, "cu_seqlens"),
+        int(max_seqlen), int(total), B, Hqk, Hv, dk, dv, int(head_map), float(scale), _dtype_code(q),
+        _dtype_code(out), _dev(workspace, "workspace"), workspace.numel() * workspace.element_size(),
+        _stream(stream))
+    _check(st, "gdn_prefill_sm100_fused_varlen")
     return out
 
 

@@ -1270,6 +1270,19 @@ extern "C" int gdn_prefill_sm100_varlen(const void* q, const void* k, const void
                                b200::Fuse{false, nullptr, nullptr}, cu_seqlens, total_tokens);
 }
 
+extern "C" int gdn_prefill_sm100_fused_varlen(const void* q, const void* k, const void* v, const float* a,
+                                              const float* b, const float* A_log, const float* dt_bias,
+                                              float* state, void* o, const int* cu_seqlens, int max_seqlen,
+                                              int total_tokens, int B, int Hqk, int Hv, int dk, int dv,
+                                              int head_map, float scale, int in_dtype, int out_dtype,
+                                              void* workspace, size_t ws_bytes, void* stream) {
+    if (!cu_seqlens) return B200LAB_ERR_INVALID;
+    if (max_seqlen < 1 || total_tokens < 1) return B200LAB_ERR_INVALID;
+    return b200::prefill_entry(q, k, v, a, b, state, o, B, max_seqlen, Hqk, Hv, dk, dv, head_map, scale, in_dtype,
+                               out_dtype, workspace, ws_bytes, stream, b200::Fuse{true, A_log, dt_bias},
+                               cu_seqlens, total_tokens);
+}
+
 extern "C" int gdn_prefill_sm100_fused(const void* q, const void* k, const void* v, const float* a,
                                        const float* b, const float* A_log, const float* dt_bias,
                                        float* state, void* o, int B, int T, int Hqk, int Hv, int dk,
