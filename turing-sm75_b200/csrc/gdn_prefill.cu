@@ -122,12 +122,6 @@ __device__ __forceinline__ int qk_head(int h, int Hqk, int Hv, int head_map) {
     return head_map == 0 ? h % Hqk : h / (Hv / Hqk);
 }
 
-// byte offset of element (row r, col j) in a K-major 128B-swizzled tile whose
-// rows are 128 bytes (64 16-bit elements) and whose 8-row groups are packed.
-__device__ __forceinline__ uint32_t sw128_off(int r, int j) {
-    return (uint32_t)(r * 128 + ((((j >> 3) ^ (r & 7)) & 7) << 4) + (j & 7) * 2);
-}
-
 // ===========================================================================
 // Kernel 1: per-chunk preparation
 // ===========================================================================
