@@ -143,7 +143,10 @@ size_t gdn_prefill_sm100_workspace(int B, int T, int Hqk, int Hv, int dk, int dv
  * [B][Hv][dv][dk], one per sequence, updated in place (an empty sequence keeps
  * its state).  Chunks start at each sequence's first token, so sequence b's
  * outputs and state are those of a B = 1 call on it alone.  Workspace:
- * gdn_prefill_sm100_workspace(B, max_seqlen, ...). */
+ * gdn_prefill_sm100_workspace(B, max_seqlen, ...).  The kernels check the
+ * offsets before using them: a sequence outside [0, total_tokens) or longer
+ * than max_seqlen is skipped and b200lab_device_status() then returns
+ * B200LAB_ERR_INVALID. */
 int gdn_prefill_sm100_varlen(const void* q, const void* k, const void* v,
                              const float* g_log, const float* beta, float* state, void* o,
                              const int* cu_seqlens, int max_seqlen, int total_tokens,

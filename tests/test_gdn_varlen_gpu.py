@@ -86,3 +86,20 @@ def test_fused_varlen_equals_per_sequence_fused_calls(cuda):
                                        out_dtype=torch.float32)
         assert torch.equal(o[lo:hi].cpu(), oi[0].cpu()), f"sequence {i} outputs"
         assert torch.equal(S[i].cpu(), Si[0].cpu()), f"sequence {i} state"
+
+
+@pytest.mark.parametrize("cu_list,max_seqlen,total", [([0, 100, 500], 400, 300),   # past total_tokens
+                                                      ([0, 100, 300], 150, 300)])  # longer than max_seqlen
+def test_inconsistent_offsets_are_reported_not_followed(cuda, cu_list, max_seqlen, total):
+    """Offsets that leave the buffers or exceed max_seqlen are checked on the device before any
+    access through them: the call reports ERR_INVALID and the context stays usable."""
+    dev = torch.device("cuda:0")
+    q, k, v, g, b = (t[0].to(dev) for t in workloads.gdn_inputs(1, total, 2, 4, 128, torch.bfloat16, seed=4))
+    S = torch.zeros((2, 4, 128, 128), device=dev)
+    cu = torch.tensor(cu_list, dtype=torch.int32, device=dev)
+    b200lab.gdn_prefill_varlen(q, k, v, g, b, S, cu, max_seqlen)
+    assert b200lab.device_status() == b200lab.ERR_INVALID
+    assert b200lab.device_status() == b200lab.OK
+    ok_cu = torch.tensor([0, 100, total], dtype=torch.int32, device=dev)
+    b200lab.gdn_prefill_varlen(q, k, v, g, b, torch.zeros_like(S), ok_cu, total - 100)
+    assert b200lab.device_status() == b200lab.OK

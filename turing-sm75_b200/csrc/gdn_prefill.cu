@@ -70,6 +70,7 @@ struct PrepParams {
     size_t ws_u, ws_aqk, ws_gcs, ws_rq, ws_rk;
     const int* cu;  // packed sequences: [B+1] token offsets (device), or null: B x T dense
     int T, Hqk, Hv, nch, head_map;  // with cu, T is the longest sequence; nch = ceil(T / 64)
+    int ntok;                       // tokens in the flattened dimension (B*T, or cu[B])
 };
 
 // Tokens are addressed in one flattened sequence dimension ([B*T] dense, [total] packed), so
@@ -83,6 +84,11 @@ struct SeqSpan {
 __device__ __forceinline__ SeqSpan seq_span(const int* cu, int T, int b) {
     if (cu) return SeqSpan{cu[b], cu[b + 1] - cu[b]};
     return SeqSpan{b * T, T};
+}
+// A packed sequence must lie inside [0, ntok) and be no longer than the T the grid and the
+// workspace were sized for; a caller's offsets that break this are reported, not followed.
+__device__ __forceinline__ bool seq_ok(SeqSpan s, int T, int ntok) {
+    return s.start >= 0 && s.len >= 0 && s.len <= T && s.start <= ntok - s.len;
 }
 
 // Fused pre-processing (gdn_prefill_sm100_fused): q, k arrive raw and are L2-normalised,
@@ -281,6 +287,10 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
     const int h = blockIdx.y;   // v-head
     const int b = blockIdx.z;   // sequence
     const SeqSpan seq = seq_span(p.cu, p.T, b);
+    if (!seq_ok(seq, p.T, p.ntok)) {
+        if (threadIdx.x == 0 && c == 0) atomicExch(&g_err_gdn_prefill, B200LAB_ERR_INVALID);
+        return;
+    }
     const int t0 = c * kC;
     if (t0 >= seq.len) return;  // packed: a shorter sequence has fewer chunks
     const int hq = qk_head(h, p.Hqk, p.Hv, p.head_map);
@@ -734,6 +744,7 @@ struct StateParams {
     size_t ws_gcs, ws_rq, ws_rk;
     const int* cu;  // as PrepParams
     int T, Hqk, Hv, nch, head_map;
+    int ntok;
     float scale;
 };
 
@@ -774,6 +785,7 @@ __global__ void __launch_bounds__(st::kThreads, 1)
     const int h = blockIdx.y;
     const int b = blockIdx.z;
     const SeqSpan seq = seq_span(p.cu, p.T, b);
+    if (!seq_ok(seq, p.T, p.ntok)) return;    // recorded by the prep grid; state left as it is
     const int nch = (seq.len + kC - 1) / kC;  // this sequence's chunks (p.nch for the longest)
     if (nch == 0) return;                     // an empty sequence: its state stays as it is
     const int c0 = slice * kSlice;
@@ -1131,6 +1143,7 @@ int launch(const void* q, const void* k, const void* v, const float* g_log, cons
     pp.A_log = fuse.A_log;
     pp.dt_bias = fuse.dt_bias;
     pp.cu = cu;
+    pp.ntok = ntok;
     pp.T = T;
     pp.Hqk = Hqk;
     pp.Hv = Hv;
@@ -1149,6 +1162,7 @@ int launch(const void* q, const void* k, const void* v, const float* g_log, cons
     sp.ws_rq = L.rq;
     sp.ws_rk = L.rk;
     sp.cu = cu;
+    sp.ntok = ntok;
     sp.T = T;
     sp.Hqk = Hqk;
     sp.Hv = Hv;
