@@ -93,7 +93,10 @@ int attn_fwd_sm100_host(const void* Qh, const void* Kh, const void* Vh, void* Oh
  *   cu_seqlens_q, cu_seqlens_k : [B+1] device int32 prefix sums; sequence b is
  *   tokens [cu[b], cu[b+1]) of each; max_seqlen_q bounds the grid.
  *   Causal is aligned per sequence: key j visible to query i iff
- *   j <= i + (Skv_b - Sq_b).  D = 64 or 128; no workspace (no key splits). */
+ *   j <= i + (Skv_b - Sq_b).  D = 64 or 128; no workspace (no key splits).
+ *   The kernel checks the offsets before using them: a sequence outside the
+ *   buffers or longer than max_seqlen_q is skipped and b200lab_device_status()
+ *   then returns B200LAB_ERR_INVALID. */
 int attn_fwd_sm100_varlen(const void* Q, const void* K, const void* V, void* O,
                           const int* cu_seqlens_q, const int* cu_seqlens_k,
                           int max_seqlen_q, int total_q, int total_k, int B, int Hq,

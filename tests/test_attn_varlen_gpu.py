@@ -62,3 +62,24 @@ def test_varlen_matches_dense_batch(cuda):
     Od = b200lab.attn_fwd(dense(Q), dense(K), dense(V), causal=True)
     torch.cuda.synchronize()
     assert torch.equal(Ov.view(B, S, Hq, D).permute(0, 2, 1, 3), Od)
+
+
+@pytest.mark.parametrize("cu_q,cu_k,max_q", [([0, 64, 400], [0, 64, 200], 336),   # queries past total_q
+                                             ([0, 64, 200], [0, 64, 300], 136),   # keys past total_k
+                                             ([0, 64, 200], [0, 64, 200], 100)])  # longer than max_seqlen_q
+def test_varlen_inconsistent_offsets_are_reported_not_followed(cuda, cu_q, cu_k, max_q):
+    """Offsets that leave the buffers or exceed max_seqlen_q are checked on the device before
+    any access through them: ERR_INVALID, and the context stays usable."""
+    dev = torch.device("cuda:0")
+    gen = torch.Generator().manual_seed(2)
+    Q = torch.randn((200, 4, 128), generator=gen).to(torch.bfloat16).to(dev)
+    K = torch.randn((200, 2, 128), generator=gen).to(torch.bfloat16).to(dev)
+    V = torch.randn((200, 2, 128), generator=gen).to(torch.bfloat16).to(dev)
+    cq = torch.tensor(cu_q, dtype=torch.int32, device=dev)
+    ck = torch.tensor(cu_k, dtype=torch.int32, device=dev)
+    b200lab.attn_fwd_varlen(Q, K, V, cq, ck, max_q, causal=True)
+    assert b200lab.device_status() == b200lab.ERR_INVALID
+    assert b200lab.device_status() == b200lab.OK
+    ok = torch.tensor([0, 64, 200], dtype=torch.int32, device=dev)
+    b200lab.attn_fwd_varlen(Q, K, V, ok, ok, 136, causal=True)
+    assert b200lab.device_status() == b200lab.OK

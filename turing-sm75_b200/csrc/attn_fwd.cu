@@ -93,6 +93,7 @@ struct Params {
     float* part_ml;  // [B*Hq*Sq][nsplit][2]: running max (log2 units), row sum
     int Hq, Sq, Skv, group, n_ctas, causal;
     int nsplit, tiles_per_split;
+    int total_q, total_k, max_sq;  // varlen: the buffers' token counts and the grid's sizing
     float scale_log2;
 };
 
@@ -165,6 +166,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         k_tok0 = p.cu_k[b];
         Sq = p.cu_q[b + 1] - q_tok0;
         Skv = p.cu_k[b + 1] - k_tok0;
+        // a caller's offsets are checked before anything is read or written through them
+        if (q_tok0 < 0 || Sq < 0 || Sq > p.max_sq || q_tok0 > p.total_q - Sq || k_tok0 < 0 || Skv < 0 ||
+            k_tok0 > p.total_k - Skv) {
+            if (threadIdx.x == 0 && cta_lin == 0 && hq == 0) atomicExch(&g_err_attn, B200LAB_ERR_INVALID);
+            return;
+        }
         n_ctas = (Sq + kQTiles * BM - 1) / (kQTiles * BM);
         if (cta_lin >= n_ctas) return;  // the grid covers the longest sequence
     }
@@ -563,7 +570,7 @@ int launch_varlen(const void* Q, const void* K, const void* V, void* O, const in
     if (rc) return rc;
     rc = make_tmap_4d(&tv, V, dt, 2, D, Hkv, total_k, 1, 64, 1, BN, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
-    Params p;
+    Params p{};
     p.O = O;
     p.cu_q = cu_q;
     p.cu_k = cu_k;
@@ -577,6 +584,9 @@ int launch_varlen(const void* Q, const void* K, const void* V, void* O, const in
     p.causal = causal;
     p.nsplit = 1;
     p.tiles_per_split = 1 << 30;
+    p.total_q = total_q;
+    p.total_k = total_k;
+    p.max_sq = max_sq;
     p.scale_log2 = scale * 1.4426950408889634f;
     auto kern = attn_fwd_kernel<D, T, false, true>;
     B200_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc));
@@ -634,7 +644,7 @@ int launch(const void* Q, const void* K, const void* V, void* O, int B, int Hq, 
     if (rc) return rc;
     rc = make_tmap_3d(&tv, V, dt, 2, D, Skv, (uint64_t)B * Hkv, 64, BN, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
-    Params p;
+    Params p{};
     p.O = O;
     p.Hq = Hq;
     p.Sq = Sq;
