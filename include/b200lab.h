@@ -237,14 +237,16 @@ int gdn_decode_sm100_fused(const void* q, const void* k, const void* v,
 
 /* The decode step for continuous batching (no C entry of the reference
  * corresponds; the paged batching serving callers need): the states live in a
- * pool [n_slots][Hv][dv][dk] fp32 and sequence b uses state_pool[slots[b]]
+ * pool [pool_size][Hv][dv][dk] fp32 and sequence b uses state_pool[slots[b]]
  * (slots: B device ints); slots[b] < 0 marks a padding entry, whose state and
- * output are not touched.  Otherwise as gdn_decode_sm100. */
+ * output are not touched; slots[b] >= pool_size is skipped the same way and
+ * b200lab_device_status() then returns B200LAB_ERR_INVALID.  Otherwise as
+ * gdn_decode_sm100. */
 int gdn_decode_sm100_slots(const void* q, const void* k, const void* v,
                            const float* g_log, const float* beta, float* state_pool,
-                           const int* slots, void* o, int B, int Hqk, int Hv, int dk,
-                           int dv, int head_map, float scale, int in_dtype, int out_dtype,
-                           void* stream);
+                           const int* slots, int pool_size, void* o, int B, int Hqk,
+                           int Hv, int dk, int dv, int head_map, float scale,
+                           int in_dtype, int out_dtype, void* stream);
 
 /* The same decode step with a 16-bit recurrent state in HBM (state_dtype
  * B200LAB_F16 or B200LAB_BF16; [B][Hv][dv][dk], updated in place; q, k and

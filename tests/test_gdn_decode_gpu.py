@@ -87,3 +87,29 @@ def test_slots_pool_matches_dense_and_skips_padding(cuda):
     assert_close(pool_out[slots[live].long().numpy()], S_ref, "slot states")
     untouched = [s for s in range(n_pool) if s not in set(slots.tolist())]
     assert np.array_equal(pool_out[untouched], to_np(pool)[untouched])
+
+
+def test_slots_past_the_pool_are_reported_not_followed(cuda):
+    """A slot id at or beyond the pool size is checked on the device before the pool is
+    touched: that entry is skipped, the call reports ERR_INVALID, the others are updated."""
+    dev = torch.device("cuda:0")
+    B, Hqk, Hv, n_pool = 3, 2, 4, 4
+    slots = torch.tensor([2, 4, 0], dtype=torch.int32)  # 4 is past a pool of 4
+    pool = workloads.gdn_state(n_pool, Hv, 128, std=0.02, seed=41)
+    pool_dev = pool.clone().to(dev)
+    q, k, v, g, b = workloads.gdn_decode_inputs(B, Hqk, Hv, 128, torch.bfloat16, seed=42)
+    out = torch.full((B, Hv, 128), 5.0, dtype=torch.float32, device=dev)
+    b200lab.gdn_decode_slots(q.to(dev), k.to(dev), v.to(dev), g.to(dev), b.to(dev), pool_dev,
+                             slots.to(dev), out=out)
+    assert b200lab.device_status() == b200lab.ERR_INVALID
+    assert b200lab.device_status() == b200lab.OK
+    o = to_np(out)
+    assert np.all(o[1] == 5.0)  # the bad entry wrote nothing
+    live = [0, 2]
+    o_ref, S_ref = oracle.gdn_recurrent(to_np(q)[live][:, None], to_np(k)[live][:, None], to_np(v)[live][:, None],
+                                        to_np(g)[live][:, None], to_np(b)[live][:, None],
+                                        pool[slots[live].long()].double().numpy(), 1.0 / np.sqrt(128))
+    assert_close(o[live], o_ref[:, 0], "valid slots")
+    pool_out = to_np(pool_dev)
+    assert_close(pool_out[[2, 0]], S_ref, "valid slot states")
+    assert np.array_equal(pool_out[[1, 3]], to_np(pool)[[1, 3]])

@@ -92,7 +92,7 @@ def lib() -> ctypes.CDLL:
         L.gdn_prefill_sm100_fused_varlen.argtypes = [vp] * 10 + [ci] * 8 + [cf, ci, ci, vp, sz, vp]
         L.gdn_prefill_sm100_fused.argtypes = [vp] * 9 + [ci] * 7 + [cf, ci, ci, vp, sz, vp]
         L.gdn_decode_sm100_slots.restype = ci
-        L.gdn_decode_sm100_slots.argtypes = [vp] * 8 + [ci] * 6 + [cf, ci, ci, vp]
+        L.gdn_decode_sm100_slots.argtypes = [vp] * 7 + [ci, vp] + [ci] * 6 + [cf, ci, ci, vp]
         L.gdn_decode_sm100_fused.restype = ci
         L.gdn_decode_sm100_fused.argtypes = [vp] * 9 + [ci] * 6 + [cf, ci, ci, vp]
         L.gdn_decode_sm100_state16.restype = ci
@@ -418,7 +418,8 @@ def gdn_decode_fused(q, k, v, a, b, state, *, A_log=None, dt_bias=None, scale: f
 def gdn_decode_slots(q, k, v, g_log, beta, state_pool, slots, *, scale: float | None = None,
                      head_map: int = 0, out=None, out_dtype=None, stream=None):
     """Decode step over a state pool: sequence b uses state_pool[slots[b]] (slots: int32 [B] on
-    the device; < 0 = padding, skipped).  state_pool [n,Hv,dv,dk] fp32 updated in place."""
+    the device; < 0 = padding, skipped; >= n is reported as ERR_INVALID by device_status).
+    state_pool [n,Hv,dv,dk] fp32 updated in place."""
     torch = _torch()
     B, Hqk, dk = q.shape
     Hv, dv = v.shape[1], v.shape[2]
@@ -430,8 +431,9 @@ def gdn_decode_slots(q, k, v, g_log, beta, state_pool, slots, *, scale: float | 
         out = torch.zeros((B, Hv, dv), dtype=out_dtype or q.dtype, device=q.device)
     st = lib().gdn_decode_sm100_slots(_dev(q, "q"), _dev(k, "k"), _dev(v, "v"), _dev(g_log, "g_log"),
                                       _dev(beta, "beta"), _dev(state_pool, "state_pool"), _dev(slots, "slots"),
-                                      _dev(out, "out"), B, Hqk, Hv, dk, dv, int(head_map), float(scale),
-                                      _dtype_code(q), _dtype_code(out), _stream(stream))
+                                      int(state_pool.shape[0]), _dev(out, "out"), B, Hqk, Hv, dk, dv,
+                                      int(head_map), float(scale), _dtype_code(q), _dtype_code(out),
+                                      _stream(stream))
     _check(st, "gdn_decode_sm100_slots")
     return out
 

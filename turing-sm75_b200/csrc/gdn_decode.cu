@@ -89,8 +89,10 @@ struct Pre {
     const float* dt_bias;  // [Hv] or null (0)
     int fused;
     // Continuous batching (gdn_decode_sm100_slots): sequence b's state is
-    // state[slots[b]] of a pool of [Hv][dv][dk] states; slots[b] < 0 is padding (skipped).
+    // state[slots[b]] of a pool of pool_size [Hv][dv][dk] states; slots[b] < 0 is padding
+    // (skipped); slots[b] >= pool_size is reported as ERR_INVALID and skipped.
     const int* slots = nullptr;
+    int pool_size = 0;
 };
 constexpr float kNormEps = 1e-6f;
 
@@ -115,6 +117,10 @@ __global__ void __launch_bounds__(kThreads, 4) gdn_decode_kernel(
     if (pre.slots) {
         const int slot = pre.slots[b];
         if (slot < 0) return;  // padding entry: no state, no output (uniform over the CTA)
+        if (slot >= pre.pool_size) {  // outside the pool: reported, never followed
+            if (threadIdx.x == 0) atomicExch(&g_err_gdn_decode, B200LAB_ERR_INVALID);
+            return;
+        }
         sh = (size_t)slot * Hv + h;
     }
     TS* S = state + sh * kD * kD + (size_t)row0 * kD + 4 * lane;
@@ -376,11 +382,11 @@ extern "C" int gdn_decode_sm100_fused(const void* q, const void* k, const void* 
 }
 
 extern "C" int gdn_decode_sm100_slots(const void* q, const void* k, const void* v, const float* g_log,
-                                      const float* beta, float* state_pool, const int* slots, void* o,
-                                      int B, int Hqk, int Hv, int dk, int dv, int head_map, float scale,
-                                      int in_dtype, int out_dtype, void* stream) {
+                                      const float* beta, float* state_pool, const int* slots, int pool_size,
+                                      void* o, int B, int Hqk, int Hv, int dk, int dv, int head_map,
+                                      float scale, int in_dtype, int out_dtype, void* stream) {
     using namespace b200;
-    if (!slots) return B200LAB_ERR_INVALID;
+    if (!slots || pool_size < 1) return B200LAB_ERR_INVALID;
     int rc = check_args(q, k, v, g_log, beta, state_pool, o, B, Hqk, Hv, dk, dv, head_map, in_dtype,
                         out_dtype);
     if (rc != B200LAB_OK) return rc;
@@ -391,6 +397,7 @@ extern "C" int gdn_decode_sm100_slots(const void* q, const void* k, const void* 
     if (rc != B200LAB_OK) return rc;
     Pre pre{nullptr, nullptr, 0};
     pre.slots = slots;
+    pre.pool_size = pool_size;
     return dispatch_in<float>(in_dtype, out_dtype, q, k, v, g_log, beta, state_pool, o, B, Hqk, Hv,
                               head_map, scale, static_cast<cudaStream_t>(stream), pre);
 }
