@@ -14,19 +14,20 @@
 //   Two query tiles would need 768 columns, so the overlap comes from S instead: the
 //   tensor core computes S(j+1) while the softmax works on S(j), and PV(j) runs as soon
 //   as P(j) is in TMEM.  Per 64-key tile the tensor work (QK^T and PV, 8.4 MFLOP) is
-//   ~1024 cycles against ~950 of softmax, so the two can keep each other busy.
+//   ~1320 cycles (the N = 64 QK^T instructions run at two thirds of the full rate)
+//   against ~1000 of softmax.
 //   warp 4: TMA producer (Q once; K(0), K(1); then per tile the stage {V(j), K(j+2)} into
 //           slot j & 1 of two rings of 128-byte-swizzled 64-column boxes).
 //   warp 5: TMEM owner and MMA issuer: QK(0), QK(1), then per tile PV(j), QK(j+2).
 //   warps 0-3: softmax, thread = query row = TMEM lane; P(j) packed to 16 bits over the
 //           first 32 columns of its S buffer; lazy O rescale (max grows by > 2^8) after
 //           waiting for PV(j-1); epilogue O / l * sigmoid(G).
-// The issuing thread keeps the tensor pipe busy only while it is issuing: its issue queue
-// is about one instruction deep, so every barrier wait or commit between two MMAs leaves
-// the pipe idle for ~50-150 cycles.  Per tile the MMA thread therefore waits once (P(j),
-// which the softmax warps publish only after they have seen stage j land) and commits once: done[j & 1] marks PV(j) and QK(j+2) complete, which is
-// at once "S(j+2) ready" for the softmax, "slots of V(j) and K(j+2) free" for the
-// producer, and "PV(j) done" for a rescale of O.
+// The issuing thread keeps the tensor pipe busy only while it is issuing: every barrier
+// wait or commit it makes between MMAs idles the pipe for ~50-150 cycles, wherever it is
+// placed.  Per tile the MMA thread therefore waits once (P(j), which the softmax warps
+// publish only after they have seen stage j land) and commits once: done[j & 1] marks
+// PV(j) and QK(j+2) complete, which is at once "S(j+2) ready" for the softmax, "slots of
+// V(j) and K(j+2) free" for the producer, and "PV(j) done" for a rescale of O.
 // Every mbarrier wait is bounded (common.cuh).
 #include "common.cuh"
 #include "errwords.h"
