@@ -51,8 +51,9 @@ constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P <= 2^8 between rescales
 
 // The MMA thread keeps the tensor pipe fed only while it issues: each barrier wait or commit
-// it makes between MMAs idles the pipe (~50-150 cycles, measured, wherever it is placed).  Per key tile it therefore waits three times (the stage, P_0, P_1) and commits
-// twice: s_full0 after QK_0(j+1), and done[j&1] after the whole step, which completes
+// it makes between MMAs idles the pipe (~50-150 cycles, measured, wherever it is placed).
+// Per key tile it therefore waits three times (the stage, P_0, P_1) and commits twice:
+// s_full0 after QK_0(j+1), and done[j&1] after the whole step, which completes
 // when PV(j) and QK(j+1) of both tiles have: "S_1(j+1) ready" for the second softmax
 // warpgroup and "V slot j&1 and K slot (j+1)&1 free" for the producer, which loads V(j)
 // and K(j+1) as one stage under one barrier.
