@@ -153,3 +153,22 @@ def test_host_buffer_pipeline_equals_device_path(cuda, B, Hq, Hkv, S, D, dtype):
     assert torch.equal(Oh, O_dev.cpu())
     ref = oracle.attn_fwd(to_np(Q), to_np(K), to_np(V), 1.0 / np.sqrt(D), True)
     assert_close(to_np(Oh), ref, "host pipeline")
+
+
+@pytest.mark.parametrize("name", ["d64", "d128"])
+@pytest.mark.parametrize("causal", [0, 1])
+def test_kernel_vs_reference_naive_golden(cuda, name, causal):
+    """The kernel on the inputs of the committed golden fixture (outputs of the reference's
+    own naive_attn_kernel, tests/golden/make_attn_golden.py): within the reference's PASS bar
+    of it (src/attn_sm75.cu:501) and within the parity bar of the fp64 oracle."""
+    import os
+    z = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "attn_ref_naive.npz"))
+    dev = torch.device("cuda:0")
+    q, k, v = (torch.from_numpy(z[f"{name}_{t}"])[None, None].to(dev) for t in "qkv")
+    scale = float(z[f"{name}_scale"])
+    O = to_np(b200lab.attn_fwd(q, k, v, scale=scale, causal=bool(causal)))[0, 0]
+    assert b200lab.device_status() == b200lab.OK
+    ref_naive = z[f"{name}_o_c{causal}"].astype(np.float64)
+    assert np.abs(O - ref_naive).max() < 2e-2
+    ref64 = oracle.attn_fwd(to_np(q), to_np(k), to_np(v), scale, bool(causal))[0, 0]
+    assert_close(O, ref64, f"golden {name} causal{causal}")
