@@ -134,10 +134,14 @@ def test_split_kv_without_workspace_runs_unsplit(cuda):
     assert_close(to_np(O2), to_np(O1), "unsplit vs split")
 
 
-@pytest.mark.parametrize("B,Hq,Hkv,S,D,dtype", [(2, 8, 4, 384, 128, torch.bfloat16),   # 8 chunks of 1 kv-head
-                                                (3, 6, 2, 200, 64, torch.float16),     # 3 batches x 2 chunks
+# chunks are runs of (batch, kv-head) units: about an eighth of them each, the last two such
+# chunks' worth split into halves and quarters
+@pytest.mark.parametrize("B,Hq,Hkv,S,D,dtype", [(2, 8, 4, 384, 128, torch.bfloat16),   # 8 chunks of 1 unit
+                                                (3, 6, 2, 200, 64, torch.float16),     # 6 chunks of 1 unit
                                                 (1, 4, 1, 300, 256, torch.bfloat16),   # one chunk, head dim 256
-                                                (9, 2, 2, 64, 128, torch.bfloat16)])   # more batches than 8
+                                                (9, 2, 2, 64, 128, torch.bfloat16),    # 2 x 7, 1, 1
+                                                (6, 6, 3, 160, 64, torch.float16),     # chunks across batches
+                                                (4, 8, 8, 128, 128, torch.bfloat16)])  # 4 x 6, 2, 2, 1 x 4
 def test_host_buffer_pipeline_equals_device_path(cuda, B, Hq, Hkv, S, D, dtype):
     """attn_fwd_sm100_host (host in/out, copies pipelined with the chunked launches) gives the
     device entry's bits, and matches the oracle."""

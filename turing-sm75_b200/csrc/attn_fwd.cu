@@ -35,6 +35,8 @@
 #include "common.cuh"
 #include "errwords.h"
 
+#include <vector>
+
 namespace b200 {
 namespace {
 
@@ -726,8 +728,10 @@ extern "C" int attn_fwd_sm100(const void* Q, const void* K, const void* V, void*
                     : launch<64, __half>(Q, K, V, O, B, Hq, Hkv, Sq, Skv, scale, causal, workspace, ws_bytes, st);
 }
 
-// Host-buffer pipeline over attn_fwd_sm100: chunks of whole (batch, kv-head) units, each a
-// contiguous slab of Q/O ([B][Hq][Sq][D], the q-heads of a kv group adjacent) and of K/V.
+// Host-buffer pipeline over attn_fwd_sm100: chunks of whole (batch, kv-head) units.  Units
+// are numbered b * Hkv + kv-head; any run of consecutive units is one contiguous slab of Q/O
+// ([B][Hq][Sq][D], the q-heads of a kv group adjacent) and of K/V, so a chunk is one call with
+// B = 1, Hq = n * group, Hkv = n over its slab, whatever batch boundaries it spans.
 extern "C" int attn_fwd_sm100_host(const void* Qh, const void* Kh, const void* Vh, void* Oh, void* Qd, void* Kd,
                                    void* Vd, void* Od, int B, int Hq, int Hkv, int Sq, int Skv, int D, float scale,
                                    int causal, int dtype, void* stream) {
@@ -742,17 +746,40 @@ extern "C" int attn_fwd_sm100_host(const void* Qh, const void* Kh, const void* V
     int rc = check_device_sm100();
     if (rc != B200LAB_OK) return rc;
     const int group = Hq / Hkv;
-    // kv-heads per chunk: split each batch's heads only as far as needed for ~8 chunks (16
-    // measured the same on C5: the copies in, not the pipeline's fill, bound the call)
-    constexpr int kTargetChunks = 8;
-    int m = 1;  // chunks per batch, a divisor of Hkv
-    for (int d = 1; d <= Hkv; ++d)
-        if (Hkv % d == 0 && (long long)B * d <= kTargetChunks) m = d;
-    const int hc = Hkv / m;
-    const int nchunks = B * m;
+    // Chunk schedule, in units: about an eighth of the units a chunk, and the last two such
+    // chunks' worth split into halves then quarters.  The copies in run back to back; what
+    // follows the last of them (that chunk's kernel and copy out) is the pipeline's tail,
+    // which the small final chunks shorten.  C5 (32 units): 4 x 6, 2, 2, 1 x 4 took 18.05 ms
+    // against 18.98 ms for eight chunks of 4 (the copies alone, pipelined: ~17 ms); chunks of
+    // 1 or 2 units throughout were slower (smaller copies move fewer bytes a second).
+    const long long units = (long long)B * Hkv;
+    if (units > (1LL << 30)) return B200LAB_ERR_UNSUPPORTED;
+    const int nunits = static_cast<int>(units);
+    std::vector<int> sched;
+    {
+        int c = nunits / 8 > 1 ? nunits / 8 : 1;
+        if (c > 65535 / Hq * Hkv) c = 65535 / Hq * Hkv;  // a chunk's q-heads stay a grid dimension
+        if (c < 1) c = 1;
+        const int tail = nunits < 2 * c ? nunits : 2 * c;
+        const int head = nunits - tail;
+        for (int u = 0; u < head; u += c) sched.push_back(c < head - u ? c : head - u);
+        const int half = c / 2 > 1 ? c / 2 : 1, quarter = c / 4 > 1 ? c / 4 : 1;
+        int rem = tail;
+        for (int k = 0; k < 2 && rem > 0; ++k) {
+            const int n = half < rem ? half : rem;
+            sched.push_back(n);
+            rem -= n;
+        }
+        while (rem > 0) {
+            const int n = quarter < rem ? quarter : rem;
+            sched.push_back(n);
+            rem -= n;
+        }
+    }
+    const int nchunks = static_cast<int>(sched.size());
     const size_t esz = 2;
-    const size_t q_chunk = (size_t)hc * group * Sq * D * esz;  // Q or O bytes of a chunk
-    const size_t kv_chunk = (size_t)hc * Skv * D * esz;
+    const size_t q_unit = (size_t)group * Sq * D * esz;  // Q or O bytes of a unit
+    const size_t kv_unit = (size_t)Skv * D * esz;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     cudaStream_t s_in = nullptr, s_out = nullptr;
     cudaEvent_t ev_start = nullptr, ev_end = nullptr;
@@ -782,8 +809,11 @@ extern "C" int attn_fwd_sm100_host(const void* Qh, const void* Kh, const void* V
     char* kd = static_cast<char*>(Kd);
     char* vd = static_cast<char*>(Vd);
     char* od = static_cast<char*>(Od);
-    for (int i = 0; rc == B200LAB_OK && i < nchunks; ++i) {
-        const size_t qo = (size_t)i * q_chunk, ko = (size_t)i * kv_chunk;
+    size_t u0 = 0;  // first unit of chunk i
+    for (int i = 0; rc == B200LAB_OK && i < nchunks; u0 += sched[i], ++i) {
+        const int hc = sched[i];  // units (kv-heads) of this chunk
+        const size_t qo = u0 * q_unit, ko = u0 * kv_unit;
+        const size_t q_chunk = (size_t)hc * q_unit, kv_chunk = (size_t)hc * kv_unit;
         cudaEvent_t ein = ev_in[i % nev], edone = ev_done[i % nev];
         if (cudaMemcpyAsync(qd + qo, qh + qo, q_chunk, cudaMemcpyHostToDevice, s_in) != cudaSuccess ||
             cudaMemcpyAsync(kd + ko, kh + ko, kv_chunk, cudaMemcpyHostToDevice, s_in) != cudaSuccess ||
