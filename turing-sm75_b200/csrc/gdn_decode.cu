@@ -112,6 +112,11 @@ __global__ void __launch_bounds__(kThreads, 4) gdn_decode_kernel(
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int row0 = (blockIdx.x % kCtasPerHead) * (kRowsPerWarp * 8) + warp * kRowsPerWarp;
+    // launched with programmatic stream serialisation (launch_step): nothing global is read or
+    // written before the previous grid in the stream has completed; the next one may then be
+    // scheduled onto the SMs this grid's last CTAs free
+    grid_dependency_wait();
+    allow_dependent_launch();
 
     size_t sh = (size_t)bh;  // state index of (b, h)
     if (pre.slots) {
@@ -213,6 +218,8 @@ __global__ void __launch_bounds__(kThreads, 4) gdn_decode16_kernel(
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int half = lane >> 4, l16 = lane & 15;
     const int row0 = warp * kRows;
+    grid_dependency_wait();  // as in gdn_decode_kernel
+    allow_dependent_launch();
     TS* S = state + (size_t)bh * kD * kD + (size_t)(row0 + half) * kD + 8 * l16;
     uint4 raw[kRows / 2];
 #pragma unroll
@@ -254,24 +261,39 @@ __global__ void __launch_bounds__(kThreads, 4) gdn_decode16_kernel(
     }
 }
 
+// One decode step as a programmatic dependent launch: consecutive steps on a stream (each
+// waits for the previous grid before touching memory) then start without the launch gap.
+template <typename Kern, typename... Args>
+int launch_step(Kern kern, int grid, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, args...) != cudaSuccess) return B200LAB_ERR_CUDA;
+    count_launch(1);
+    return cudaGetLastError() == cudaSuccess ? B200LAB_OK : B200LAB_ERR_CUDA;
+}
+
 template <typename TIn, typename TOut, typename TS>
 int launch(const void* q, const void* k, const void* v, const float* g_log, const float* beta,
            void* state, void* o, int B, int Hqk, int Hv, int head_map, float scale,
            cudaStream_t st, Pre pre) {
     if constexpr (sizeof(TS) == 2) {
-        gdn_decode16_kernel<TIn, TOut, TS><<<B * Hv, kThreads, 0, st>>>(
-            static_cast<const TIn*>(q), static_cast<const TIn*>(k), static_cast<const TIn*>(v), g_log, beta,
-            static_cast<TS*>(state), static_cast<TOut*>(o), Hqk, Hv, head_map, scale);
-        count_launch(1);
-        return cudaGetLastError() == cudaSuccess ? B200LAB_OK : B200LAB_ERR_CUDA;
+        return launch_step(gdn_decode16_kernel<TIn, TOut, TS>, B * Hv, st, static_cast<const TIn*>(q),
+                           static_cast<const TIn*>(k), static_cast<const TIn*>(v), g_log, beta,
+                           static_cast<TS*>(state), static_cast<TOut*>(o), Hqk, Hv, head_map, scale);
     }
     // the fused pre-processing is its own instantiation: the plain step keeps its registers
     auto kern = pre.fused ? gdn_decode_kernel<TIn, TOut, TS, true> : gdn_decode_kernel<TIn, TOut, TS, false>;
-    kern<<<B * Hv * Rows<TS>::kCtasPerHead, kThreads, 0, st>>>(
-        static_cast<const TIn*>(q), static_cast<const TIn*>(k), static_cast<const TIn*>(v),
-        g_log, beta, static_cast<TS*>(state), static_cast<TOut*>(o), Hqk, Hv, head_map, scale, pre);
-    count_launch(1);
-    return cudaGetLastError() == cudaSuccess ? B200LAB_OK : B200LAB_ERR_CUDA;
+    return launch_step(kern, B * Hv * Rows<TS>::kCtasPerHead, st, static_cast<const TIn*>(q),
+                       static_cast<const TIn*>(k), static_cast<const TIn*>(v), g_log, beta,
+                       static_cast<TS*>(state), static_cast<TOut*>(o), Hqk, Hv, head_map, scale, pre);
 }
 
 template <typename TIn, typename TS>
