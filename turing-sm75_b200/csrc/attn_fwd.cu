@@ -399,9 +399,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float neg_mb = (m == -INFINITY) ? 0.f : -m;
 
             // P = exp2(s*c - m), packed two per 32-bit column, over S's first 64 columns
-            float rs[8];
+            float2 rs[4];  // row-sum partials, pairs added with packed f32x2 adds
 #pragma unroll
-            for (int u = 0; u < 8; ++u) rs[u] = 0.f;
+            for (int u = 0; u < 4; ++u) rs[u] = make_float2(0.f, 0.f);
 #pragma unroll
             for (int half = 0; half < 2; ++half) {  // 64 keys -> 32 packed columns at a time
                 uint32_t pk[32];
@@ -417,13 +417,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                         e.x = ex2(x.x);
                         e.y = ex2(x.y);
                     }
-                    rs[c & 7] += e.x;
-                    rs[(c + 1) & 7] += e.y;
+                    rs[c2 & 3] = __fadd2_rn(rs[c2 & 3], e);
                     pk[c2] = Elem<T>::pack2(e.x, e.y);
                 }
                 tmem_st32(tS + half * 32, pk);
             }
-            const float rowsum = ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
+            const float rowsum =
+                ((rs[0].x + rs[0].y) + (rs[1].x + rs[1].y)) + ((rs[2].x + rs[2].y) + (rs[3].x + rs[3].y));
 
             // O_t is idle here: PV_t(j-1) finished before S_t(j) was signalled.
             if (j > 0 && __any_sync(0xffffffffu, rescale)) {
