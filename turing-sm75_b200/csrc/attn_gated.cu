@@ -291,14 +291,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 m = mt;
             }
             const float neg_mb = (m == -INFINITY) ? 0.f : -m;
-            float rs[4] = {0.f, 0.f, 0.f, 0.f};
+            float2 rs[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};  // packed f32x2 partials
             uint32_t pk[32];
 #pragma unroll
             for (int c2 = 0; c2 < BN / 2; ++c2) {
-                const float e0 = ex2(fmaf(__uint_as_float(sr[2 * c2]), sl2, neg_mb));
-                const float e1 = ex2(fmaf(__uint_as_float(sr[2 * c2 + 1]), sl2, neg_mb));
-                rs[c2 & 3] += e0 + e1;
-                pk[c2] = Elem<T>::pack2(e0, e1);
+                const float2 x = __ffma2_rn(make_float2(__uint_as_float(sr[2 * c2]), __uint_as_float(sr[2 * c2 + 1])),
+                                            make_float2(sl2, sl2), make_float2(neg_mb, neg_mb));
+                const float2 e = make_float2(ex2(x.x), ex2(x.y));
+                rs[c2 & 1] = __fadd2_rn(rs[c2 & 1], e);
+                pk[c2] = Elem<T>::pack2(e.x, e.y);
             }
             tmem_st32(tS, pk);
             // O may be rescaled only once PV(j-1) has finished (S(j) was computed earlier)
@@ -323,7 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             tmem_st_wait();
-            l = l * alpha + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
+            l = l * alpha + ((rs[0].x + rs[0].y) + (rs[1].x + rs[1].y));
             // P(j) is published only once stage j (V(j), K(j+2)) has landed, so the MMA thread
             // waits once a tile (each wait it makes idles the tensor pipe)
             if (!__all_sync(0xffffffffu, mbar_wait(&bars->kv_full[st], (j >> 1) & 1, abort, &g_err_attn_gated))) {
