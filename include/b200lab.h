@@ -21,7 +21,8 @@
  *     (except B200LAB_ERR_CUDA, which reports a failed launch).
  *   - Device-side bounded waits that run out set a device error word instead
  *     of hanging; b200lab_device_status() reads and clears it.
- *   - Entry points are stateless and re-entrant apart from that error word.
+ *   - Entry points are stateless and re-entrant apart from that error word
+ *     (and attn_fwd_sm100_host's per-thread copy streams, described there).
  */
 #ifndef B200LAB_H
 #define B200LAB_H
@@ -79,7 +80,10 @@ size_t attn_fwd_sm100_workspace(int B, int Hq, int Hkv, int Sq, int Skv, int D,
  * device buffers of the full sizes.  The (batch, kv-head) units are cut into
  * about eight contiguous chunks; chunk i+1 is copied in while chunk i is
  * computed and chunk i-1 copied out (two internal streams, joined back into
- * `stream` before return; no device memory is allocated).  Oh is complete once
+ * `stream` before return; no device memory is allocated).  The two streams and
+ * their events are created on a host thread's first call for a device and kept
+ * until that thread exits; calls from one thread on one device share them, so
+ * their copies run in call order.  Oh is complete once
  * `stream` reaches the point of the call.  Same arguments and status codes as
  * attn_fwd_sm100, no workspace (no key splits). */
 int attn_fwd_sm100_host(const void* Qh, const void* Kh, const void* Vh, void* Oh,

@@ -728,6 +728,53 @@ extern "C" int attn_fwd_sm100(const void* Q, const void* K, const void* V, void*
                     : launch<64, __half>(Q, K, V, O, B, Hq, Hkv, Sq, Skv, scale, causal, workspace, ws_bytes, st);
 }
 
+namespace {
+// Streams and events of the host-buffer pipeline.  A host thread creates them on its first
+// call for a device and keeps them until it exits: creating two streams and up to 130 events
+// on every call cost ~0.25 ms of a C5 call, all of it while the GPU waited at the call's first
+// event.  Kept per thread, so callers on different threads never share them; calls from one
+// thread on one device share the two copy streams, so their copies run in call order.
+struct HostPipe {
+    static constexpr int kEvents = 64;
+    cudaStream_t s_in = nullptr, s_out = nullptr;
+    cudaEvent_t ev_start = nullptr, ev_end = nullptr;
+    cudaEvent_t ev_in[kEvents] = {}, ev_done[kEvents] = {};
+    bool ready = false;
+    int create() {
+        bool ok = cudaStreamCreateWithFlags(&s_in, cudaStreamNonBlocking) == cudaSuccess &&
+                  cudaStreamCreateWithFlags(&s_out, cudaStreamNonBlocking) == cudaSuccess &&
+                  cudaEventCreateWithFlags(&ev_start, cudaEventDisableTiming) == cudaSuccess &&
+                  cudaEventCreateWithFlags(&ev_end, cudaEventDisableTiming) == cudaSuccess;
+        for (int i = 0; ok && i < kEvents; ++i)
+            ok = cudaEventCreateWithFlags(&ev_in[i], cudaEventDisableTiming) == cudaSuccess &&
+                 cudaEventCreateWithFlags(&ev_done[i], cudaEventDisableTiming) == cudaSuccess;
+        if (!ok) {
+            destroy();
+            return B200LAB_ERR_CUDA;
+        }
+        ready = true;
+        return B200LAB_OK;
+    }
+    void destroy() {
+        for (int i = 0; i < kEvents; ++i) {
+            if (ev_in[i]) cudaEventDestroy(ev_in[i]);
+            if (ev_done[i]) cudaEventDestroy(ev_done[i]);
+            ev_in[i] = ev_done[i] = nullptr;
+        }
+        if (ev_start) cudaEventDestroy(ev_start);
+        if (ev_end) cudaEventDestroy(ev_end);
+        if (s_in) cudaStreamDestroy(s_in);
+        if (s_out) cudaStreamDestroy(s_out);
+        ev_start = ev_end = nullptr;
+        s_in = s_out = nullptr;
+        ready = false;
+    }
+    ~HostPipe() { destroy(); }
+};
+constexpr int kPipeDevices = 16;
+thread_local HostPipe t_host_pipes[kPipeDevices];
+}  // namespace
+
 // Host-buffer pipeline over attn_fwd_sm100: chunks of whole (batch, kv-head) units.  Units
 // are numbered b * Hkv + kv-head; any run of consecutive units is one contiguous slab of Q/O
 // ([B][Hq][Sq][D], the q-heads of a kv group adjacent) and of K/V, so a chunk is one call with
@@ -781,20 +828,17 @@ extern "C" int attn_fwd_sm100_host(const void* Qh, const void* Kh, const void* V
     const size_t q_unit = (size_t)group * Sq * D * esz;  // Q or O bytes of a unit
     const size_t kv_unit = (size_t)Skv * D * esz;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    cudaStream_t s_in = nullptr, s_out = nullptr;
-    cudaEvent_t ev_start = nullptr, ev_end = nullptr;
-    cudaEvent_t ev_in[64] = {}, ev_done[64] = {};
-    const int nev = nchunks < 64 ? nchunks : 64;  // events are reused round-robin past 64 chunks
+    const int nev = nchunks < HostPipe::kEvents ? nchunks : HostPipe::kEvents;  // reused round-robin past that
     auto fail = [&](int code) { rc = code; };
-    if (cudaStreamCreateWithFlags(&s_in, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaStreamCreateWithFlags(&s_out, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaEventCreateWithFlags(&ev_start, cudaEventDisableTiming) != cudaSuccess ||
-        cudaEventCreateWithFlags(&ev_end, cudaEventDisableTiming) != cudaSuccess)
-        fail(B200LAB_ERR_CUDA);
-    for (int i = 0; rc == B200LAB_OK && i < nev; ++i)
-        if (cudaEventCreateWithFlags(&ev_in[i], cudaEventDisableTiming) != cudaSuccess ||
-            cudaEventCreateWithFlags(&ev_done[i], cudaEventDisableTiming) != cudaSuccess)
-            fail(B200LAB_ERR_CUDA);
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess) return B200LAB_ERR_CUDA;
+    HostPipe per_call;  // devices past the per-thread cache get their own, destroyed on return
+    HostPipe& pipe = (dev >= 0 && dev < kPipeDevices) ? t_host_pipes[dev] : per_call;
+    if (!pipe.ready && pipe.create() != B200LAB_OK) return B200LAB_ERR_CUDA;
+    cudaStream_t s_in = pipe.s_in, s_out = pipe.s_out;
+    cudaEvent_t ev_start = pipe.ev_start, ev_end = pipe.ev_end;
+    cudaEvent_t* ev_in = pipe.ev_in;
+    cudaEvent_t* ev_done = pipe.ev_done;
     if (rc == B200LAB_OK) {
         // the device buffers may still be in use by earlier work on `stream`
         if (cudaEventRecord(ev_start, st) != cudaSuccess || cudaStreamWaitEvent(s_in, ev_start, 0) != cudaSuccess ||
@@ -835,16 +879,8 @@ extern "C" int attn_fwd_sm100_host(const void* Qh, const void* Kh, const void* V
         }
     }
     // join: `stream` continues after every copy of this call, whatever happened above
-    if (s_in && ev_end && cudaEventRecord(ev_end, s_in) == cudaSuccess) cudaStreamWaitEvent(st, ev_end, 0);
-    if (s_out && ev_start && cudaEventRecord(ev_start, s_out) == cudaSuccess) cudaStreamWaitEvent(st, ev_start, 0);
-    for (int i = 0; i < nev; ++i) {
-        if (ev_in[i]) cudaEventDestroy(ev_in[i]);
-        if (ev_done[i]) cudaEventDestroy(ev_done[i]);
-    }
-    if (ev_start) cudaEventDestroy(ev_start);
-    if (ev_end) cudaEventDestroy(ev_end);
-    if (s_in) cudaStreamDestroy(s_in);
-    if (s_out) cudaStreamDestroy(s_out);
+    if (cudaEventRecord(ev_end, s_in) == cudaSuccess) cudaStreamWaitEvent(st, ev_end, 0);
+    if (cudaEventRecord(ev_start, s_out) == cudaSuccess) cudaStreamWaitEvent(st, ev_start, 0);
     return rc;
 }
 
