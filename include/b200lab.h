@@ -175,9 +175,9 @@ int gdn_prefill_sm100_varlen(const void* q, const void* k, const void* v,
  * rejected with B200LAB_ERR_WORKSPACE before anything is launched (about
  * 50 KB per (sequence, v-head, 64-token chunk): B*Hv*ceil(T/64) <= 1344,
  * e.g. Hv=48 up to T=1792, Hv=32 up to T=2688).
- * The first call on a device looks up the array's device address (with that
- * device current) and caches it; make that first call before any stream
- * capture.  All calls on a device share the one array, so calls that overlap
+ * Every call looks up the array's device address with the caller's device
+ * current; the first call on a device also loads the library's kernels there,
+ * so make that first call before any stream capture.  All calls on a device share the one array, so calls that overlap
  * on the GPU (other streams, other host threads) race and must be
  * serialised by the caller.  Nothing in the scratch needs to start at zero:
  * the preparation kernel writes every byte the state kernel reads. */

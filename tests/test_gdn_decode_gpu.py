@@ -6,7 +6,7 @@ import torch
 import b200lab
 import oracle
 import workloads
-from helpers import assert_close, to_np
+from helpers import assert_close, elementwise_rel, errors, to_np
 
 pytestmark = pytest.mark.gpu
 
@@ -40,6 +40,43 @@ def test_small(cuda, head_map, dtype, out_dtype):
 def test_c4_shape_two_steps(cuda):
     c = workloads.CONFIGS["gdn_decode_c4"]
     _steps(c["B"], c["Hqk"], c["Hv"], torch.bfloat16, torch.bfloat16, 0, steps=2, seed=5)
+
+
+def _c4_full_length(state_dtype, seed):
+    """The C4 workload as the bench runs it: B64 Hqk16 Hv32 d128, 256 consecutive in-place
+    steps on one state, fresh inputs each step.  Every step's output and the final state are
+    checked against the fp64 recurrence run over the same 256 tokens; returns the worst
+    normwise and elementwise errors (outputs) and the state's."""
+    c = workloads.CONFIGS["gdn_decode_c4"]
+    B, Hqk, Hv, T = c["B"], c["Hqk"], c["Hv"], c["steps"]
+    dev = torch.device("cuda:0")
+    S0 = workloads.gdn_state(B, Hv, 128, std=0.02, seed=seed).to(state_dtype)
+    steps = [workloads.gdn_decode_inputs(B, Hqk, Hv, 128, torch.bfloat16, seed=seed * 1000 + t)
+             for t in range(T)]
+    S_dev = S0.to(dev)
+    outs = torch.empty((T, B, Hv, 128), dtype=torch.bfloat16, device=dev)
+    for t, (q, k, v, g, b) in enumerate(steps):
+        b200lab.gdn_decode(q.to(dev), k.to(dev), v.to(dev), g.to(dev), b.to(dev), S_dev, out=outs[t])
+    torch.cuda.synchronize()
+    assert b200lab.device_status() == b200lab.OK
+    stack = [np.stack([to_np(s[i]) for s in steps], axis=1) for i in range(5)]  # [B, T, ...]
+    o_ref, S_ref = oracle.gdn_recurrent(*stack, S0.double().numpy(), 1.0 / np.sqrt(128))
+    o = to_np(outs)
+    worst = (0.0, 0.0)
+    for t in range(T):
+        assert_close(o[t], o_ref[:, t], f"out step {t}")
+        worst = (max(worst[0], errors(o[t], o_ref[:, t])[1]),
+                 max(worst[1], elementwise_rel(o[t], o_ref[:, t])))
+    assert_close(to_np(S_dev), S_ref, "state after 256 steps")
+    st = (errors(to_np(S_dev), S_ref)[1], elementwise_rel(to_np(S_dev), S_ref))
+    print(f"\nC4 x256 {state_dtype}: outputs normwise {worst[0]:.3e} elementwise {worst[1]:.3e}; "
+          f"state normwise {st[0]:.3e} elementwise {st[1]:.3e}")
+    return worst, st
+
+
+def test_c4_full_length_fp32_state(cuda):
+    """The timed C4 workload end to end: 256 in-place steps at the full shape."""
+    _c4_full_length(torch.float32, seed=17)
 
 
 def test_decode_equals_prefill_oracle_chain(cuda):

@@ -55,6 +55,13 @@ def test_c4_shape_fp16_state_two_steps(cuda):
     _steps(c["B"], c["Hqk"], c["Hv"], torch.float16, steps=2, seed=5, out_dtype=torch.bfloat16)
 
 
+def test_c4_full_length_fp16_state(cuda):
+    """The C4 workload with an fp16 state: B64 Hqk16 Hv32, 256 consecutive in-place steps,
+    every output and the final state against the fp64 recurrence."""
+    from test_gdn_decode_gpu import _c4_full_length
+    _c4_full_length(torch.float16, seed=19)
+
+
 def test_matches_fp32_state_entry_on_first_step(cuda):
     """One step from the same (16-bit-representable) state: the two entries agree up to the
     final rounding of the 16-bit state (their reductions sum in different orders)."""

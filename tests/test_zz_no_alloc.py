@@ -53,7 +53,9 @@ def _run_both(B, T, Hqk, Hv, seed):
 
 
 def test_noalloc_matches_workspace_entry_twice(cuda):
-    for call, (T, seed) in enumerate([(300, 21), (1000, 22)]):
+    # the larger problem first: the second call (a partial last chunk) then finds the first
+    # call's data in every scratch byte it reads, so nothing it needs may rely on zeros
+    for call, (T, seed) in enumerate([(1000, 22), (300, 21)]):
         o_ws, S_ws, o_na, S_na = _run_both(1, T, 16, 32, seed)
         assert_close(o_na, o_ws, f"call {call}: outputs")
         assert_close(S_na, S_ws, f"call {call}: state")

@@ -879,9 +879,13 @@ extern "C" int attn_fwd_sm100_host(const void* Qh, const void* Kh, const void* V
         }
     }
     // join: `stream` continues after every copy of this call, whatever happened above
-    if (cudaEventRecord(ev_end, s_in) == cudaSuccess) cudaStreamWaitEvent(st, ev_end, 0);
-    if (cudaEventRecord(ev_start, s_out) == cudaSuccess) cudaStreamWaitEvent(st, ev_start, 0);
-    return rc;
+    bool joined = cudaEventRecord(ev_end, s_in) == cudaSuccess && cudaStreamWaitEvent(st, ev_end, 0) == cudaSuccess;
+    joined = cudaEventRecord(ev_start, s_out) == cudaSuccess && cudaStreamWaitEvent(st, ev_start, 0) == cudaSuccess &&
+             joined;
+    // a CUDA failure on the cached streams or events (e.g. after cudaDeviceReset, which
+    // invalidates them) drops the cache, so the next call on this thread creates them anew
+    if ((rc == B200LAB_ERR_CUDA || !joined) && &pipe != &per_call) pipe.destroy();
+    return joined ? rc : B200LAB_ERR_CUDA;
 }
 
 extern "C" int attn_fwd_sm100_varlen(const void* Q, const void* K, const void* V, void* O, const int* cu_seqlens_q,

@@ -1304,45 +1304,24 @@ extern "C" int gdn_prefill_sm100_fused(const void* q, const void* k, const void*
 // Allocation-free entry (gdn_prefill_sm100_noalloc): scratch in a file-scope
 // device array instead of a caller workspace.  In host code the array's name
 // is only a host-side stand-in, so its device address is looked up with
-// cudaGetSymbolAddress once per device (with that device current) and cached.
+// cudaGetSymbolAddress on every call, with the caller's device current (the
+// first lookup on a device loads the module there; later ones are cheap, and
+// a module reloaded after cudaDeviceReset is found at its new address).
 // ===========================================================================
-#include <mutex>
-
 static __device__ __align__(256) unsigned char g_prefill_noalloc_scratch[B200LAB_NOALLOC_SCRATCH_BYTES];
-
-namespace {
-constexpr int kNoAllocMaxDevices = 64;
-std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
-
-// Device address of the scratch array on the current device (set-up on first use).
-int noalloc_scratch(void** out) {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return B200LAB_ERR_CUDA;
-    if (dev < 0 || dev >= kNoAllocMaxDevices) return B200LAB_ERR_UNSUPPORTED;
-    std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (!g_noalloc_ptr[dev]) {
-        void* p = nullptr;
-        if (cudaGetSymbolAddress(&p, g_prefill_noalloc_scratch) != cudaSuccess || !p)
-            return B200LAB_ERR_CUDA;
-        g_noalloc_ptr[dev] = p;
-    }
-    *out = g_noalloc_ptr[dev];
-    return B200LAB_OK;
-}
-}  // namespace
 
 extern "C" int gdn_prefill_sm100_noalloc(const void* q, const void* k, const void* v,
                                          const float* g_log, const float* beta, float* state,
                                          void* o, int B, int T, int Hqk, int Hv, int dk, int dv,
                                          int head_map, float scale, int in_dtype, int out_dtype,
                                          void* stream) {
-    if (gdn_prefill_sm100_workspace(B, T, Hqk, Hv, dk, dv) > (size_t)B200LAB_NOALLOC_SCRATCH_BYTES)
-        return B200LAB_ERR_WORKSPACE;
-    if (b200::check_device_sm100() != B200LAB_OK) return B200LAB_ERR_DEVICE;
-    void* scratch = nullptr;
-    const int rc = noalloc_scratch(&scratch);
+    int rc = b200::check_device_sm100();
     if (rc != B200LAB_OK) return rc;
+    void* scratch = nullptr;
+    if (cudaGetSymbolAddress(&scratch, g_prefill_noalloc_scratch) != cudaSuccess || !scratch)
+        return B200LAB_ERR_CUDA;
+    // the workspace entry checks the arguments first, then that the problem's workspace fits
+    // in the array (B200LAB_ERR_WORKSPACE otherwise)
     return gdn_prefill_sm100(q, k, v, g_log, beta, state, o, B, T, Hqk, Hv, dk, dv, head_map,
                              scale, in_dtype, out_dtype, scratch,
                              (size_t)B200LAB_NOALLOC_SCRATCH_BYTES, stream);
