@@ -6,8 +6,11 @@
 
 One JSON line on stdout (rank 0).  The headline workload is the long-context
 causal GQA attention config (B4 Hq32 Hkv8 S16384 D128 bf16), the config the
-reference's metric is sharded across 1/2/4/8 GPUs on; GDN decode (GB/s) and
-GDN prefill (tok/s) are reported in the same line under "secondary".
+reference's metric is sharded across 1/2/4/8 GPUs on; GDN decode (GB/s), GDN
+prefill (tok/s), gated attention and the other attention shapes (C1, C2, the
+C5 shape at S 4096 / 8192 with D 128 / 64, split-KV short queries) are
+reported in the same line under "secondary", each with its own roofline, and
+the line ends with a compact "summary" of every figure.
 
 Multi-GPU: one process per GPU (torchrun), units sharded across ranks with no
 data-path collective -- attention by (batch, kv-head) with its q-heads, GDN
@@ -50,6 +53,10 @@ def load_peaks():
         return {k: float(d[k]) for k in FALLBACK_PEAKS}, "measured"
     except Exception:
         return dict(FALLBACK_PEAKS), "fallback"
+
+
+def _scaled(x, f):
+    return None if x is None else x * f
 
 
 def profile_traffic(name):
@@ -264,24 +271,53 @@ def bench_attention(name, cfg, args, dist, peaks):
     torch.cuda.synchronize()
     e2e_ms = dist.max(e0.elapsed_time(e1) / e2e_steps)
 
-    # optional NCCL all-gather of the output shards (timed on its own)
+    # the same host<->device bytes with no kernel: all copies in and out at once, every rank
+    # at the same time (the floor the host-buffer call runs against)
+    s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+
+    def copies_only():
+        s_in.wait_stream(stream)
+        s_out.wait_stream(stream)
+        with torch.cuda.stream(s_in):
+            Q.copy_(Qh, non_blocking=True)
+            K.copy_(Kh, non_blocking=True)
+            V.copy_(Vh, non_blocking=True)
+        with torch.cuda.stream(s_out):
+            Oh.copy_(O, non_blocking=True)
+        stream.wait_stream(s_in)
+        stream.wait_stream(s_out)
+
+    copies_only()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        copies_only()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    floor_ms = dist.max(e0.elapsed_time(e1) / e2e_steps)
+
+    # optional NCCL all-gather of the output shards (sharding.allgather_attention), timed
+    # on its own
     allgather = None
     if dist.world > 1:
-        import torch.distributed as tdist
-        gathered = torch.empty((dist.world,) + tuple(O.shape), dtype=O.dtype, device=dev)
+        import sharding
         for _ in range(2):
-            tdist.all_gather_into_tensor(gathered, O)
+            full = sharding.allgather_attention(O, cfg["B"], cfg["Hq"])
         torch.cuda.synchronize()
         dist.barrier()
         e0.record(stream)
         for _ in range(3):
-            tdist.all_gather_into_tensor(gathered, O)
+            full = sharding.allgather_attention(O, cfg["B"], cfg["Hq"])
         e1.record(stream)
         torch.cuda.synchronize()
         ag_ms = dist.max(e0.elapsed_time(e1) / 3)
+        total_bytes = full.numel() * full.element_size()
         allgather = {"ms": ag_ms, "bytes_per_rank_out": O.numel() * O.element_size(),
+                     "bus_gbs": total_bytes * (dist.world - 1) / dist.world / (ag_ms * 1e-3) / 1e9,
                      "kernel_plus_allgather_ms": ms + ag_ms}
-        del gathered
+        del full
 
     tflops = flops_total / (ms * 1e-3) / 1e12
     achieved = flops_local / (ms_local * 1e-3) / 1e12
@@ -304,13 +340,126 @@ def bench_attention(name, cfg, args, dist, peaks):
                      # a shard moves its units' share
                      "traffic": None if traffic is None else traffic * flops_local / flops_total},
         "e2e": {"value": flops_total / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
-                "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": O.numel() * O.element_size()},
+                "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": O.numel() * O.element_size(),
+                "copy_floor_ms": floor_ms, "frac_of_copy_floor": floor_ms / e2e_ms,
+                "copy_floor_note": "the same copies in and out with no kernel, all ranks at once"},
         "gpu_launches": int(launches),
         "clocks": clk.summary(),
     }
     if allgather:
         res["allgather"] = allgather
-    del Q, K, V, O, Qh, Kh, Vh, Oh
+    del Q, K, V, O, Qh, Kh, Vh, Oh, s_in, s_out
+    torch.cuda.empty_cache()
+    return res
+
+
+# Secondary attention shapes: the BASELINE configs C1 and C2, the C5 shape at S 4096 / 8192
+# with head dim 128 and 64, and short queries against a long key range (split-KV).
+ATTN_CASES = {
+    "attn_c1": dict(B=1, Hq=4, Hkv=4, Sq=256, Skv=256, D=128, causal=False, dtype="f16"),
+    "attn_c2_d128_causal": dict(B=2, Hq=8, Hkv=8, Sq=512, Skv=512, D=128, causal=True, dtype="bf16"),
+    "attn_c2_d128": dict(B=2, Hq=8, Hkv=8, Sq=512, Skv=512, D=128, causal=False, dtype="bf16"),
+    "attn_c2_d64_causal": dict(B=2, Hq=8, Hkv=8, Sq=512, Skv=512, D=64, causal=True, dtype="bf16"),
+    "attn_c2_d64": dict(B=2, Hq=8, Hkv=8, Sq=512, Skv=512, D=64, causal=False, dtype="bf16"),
+    "attn_s4096_d128": dict(B=4, Hq=32, Hkv=8, Sq=4096, Skv=4096, D=128, causal=True, dtype="bf16"),
+    "attn_s8192_d128": dict(B=4, Hq=32, Hkv=8, Sq=8192, Skv=8192, D=128, causal=True, dtype="bf16"),
+    "attn_s4096_d64": dict(B=4, Hq=32, Hkv=8, Sq=4096, Skv=4096, D=64, causal=True, dtype="bf16"),
+    "attn_s8192_d64": dict(B=4, Hq=32, Hkv=8, Sq=8192, Skv=8192, D=64, causal=True, dtype="bf16"),
+    "attn_splitkv_q1": dict(B=1, Hq=32, Hkv=8, Sq=1, Skv=16384, D=128, causal=True, dtype="bf16"),
+    "attn_splitkv_q64": dict(B=1, Hq=32, Hkv=8, Sq=64, Skv=16384, D=128, causal=True, dtype="bf16"),
+}
+
+
+def attn_case_flops(B, Hq, Sq, Skv, D, causal):
+    """QK^T and PV FLOPs over the visible (query, key) pairs; causal masks are aligned at the
+    bottom right (query i sees keys j <= Skv - Sq + i), so Sq = Skv gives 2 B H S (S+1) D."""
+    if not causal:
+        return 4.0 * B * Hq * Sq * Skv * D
+    off = Skv - Sq
+    pairs = sum(min(Skv, max(0, off + i + 1)) for i in range(Sq))
+    return 4.0 * B * Hq * pairs * D
+
+
+def bench_attn_case(name, shp, args, dist, peaks):
+    """One attention shape through attn_fwd_sm100 (workspace preallocated), device-timed.
+    Inputs smaller than L2 are timed launch by launch with L2 flushed before each; larger ones
+    back to back.  Roofline: the slower of tensor peak and HBM bandwidth for the shape."""
+    import torch
+    import b200lab
+    import workloads
+
+    B, Hq, Hkv, Sq, Skv, D, causal = (shp[k] for k in ("B", "Hq", "Hkv", "Sq", "Skv", "D", "causal"))
+    dtype = torch.float16 if shp["dtype"] == "f16" else torch.bfloat16
+    units = B * Hkv
+    if units % dist.world == 0:
+        import sharding
+        b0, nb, h0, nh = sharding.attn_shard(B, Hq, Hkv, dist.world, dist.rank)
+        Bl, Hql, Hkvl, shard = nb, nh * (Hq // Hkv), nh, "(batch, kv-head) units"
+        total_flops = attn_case_flops(B, Hq, Sq, Skv, D, causal)
+    else:  # fewer units than GPUs: every GPU runs the whole shape
+        Bl, Hql, Hkvl, shard = B, Hq, Hkv, "replicas (fewer units than GPUs)"
+        total_flops = dist.world * attn_case_flops(B, Hq, Sq, Skv, D, causal)
+    dev = torch.device("cuda", dist.local)
+    Q, K, V = workloads.attn_inputs(Bl, Hql, Hkvl, Sq, D, dtype, seed=61 + dist.rank, device=dev, Skv=Skv)
+    O = torch.empty_like(Q)
+    need = int(b200lab.lib().attn_fwd_sm100_workspace(Bl, Hql, Hkvl, Sq, Skv, D, int(causal)))
+    ws = torch.empty(max(need, 1), dtype=torch.uint8, device=dev) if need else None
+    stream = torch.cuda.current_stream()
+    flops_local = attn_case_flops(Bl, Hql, Sq, Skv, D, causal)
+    bytes_local = (Q.numel() * 2 + K.numel() + V.numel()) * Q.element_size()
+    small = bytes_local < 126e6
+    steps = max(3, min(args.steps, 20))
+
+    def step():
+        b200lab.attn_fwd(Q, K, V, causal=causal, out=O, workspace=ws, stream=stream)
+
+    for _ in range(args.warmup):
+        step()
+    flush = L2Flush(dev) if small else None
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    n0 = b200lab.launch_count()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(steps if small else 1)]
+    with ClockSampler(dev) as clk:
+        if small:
+            for e0, e1 in evs:
+                flush()
+                e0.record(stream)
+                step()
+                e1.record(stream)
+        else:
+            evs[0][0].record(stream)
+            for _ in range(steps):
+                step()
+            evs[0][1].record(stream)
+        torch.cuda.synchronize()
+    launches = b200lab.launch_count() - n0
+    ms_local = sum(a.elapsed_time(b) for a, b in evs) / steps
+    ms = dist.max(ms_local)
+    status = b200lab.device_status()
+    if status != b200lab.OK:
+        raise RuntimeError(f"device status {status}: {b200lab.strerror(status)}")
+    t_tc = flops_local / (peaks["bf16_tflops"] * 1e12)
+    t_hbm = bytes_local / (peaks["hbm_gbs"] * 1e9)
+    if t_tc >= t_hbm:
+        roof = {"bound": "tensor", "achieved": flops_local / (ms_local * 1e-3) / 1e12,
+                "peak": peaks["bf16_tflops"], "unit": "TFLOP/s"}
+    else:
+        roof = {"bound": "hbm", "achieved": bytes_local / (ms_local * 1e-3) / 1e9,
+                "peak": peaks["hbm_gbs"], "unit": "GB/s"}
+    roof["frac"] = roof["achieved"] / roof["peak"]
+    roof["traffic"] = None
+    res = {"metric": f"attn fwd TFLOP/s ({name})", "value": total_flops / (ms * 1e-3) / 1e12,
+           "unit": "TFLOP/s", "us_per_step": ms * 1e3, "steps": steps,
+           "flop_convention": "visible (query, key) pairs x 4 D (causal: bottom-right aligned)",
+           "dtype": shp["dtype"],
+           "config": {"workload": name, "B": B, "Hq": Hq, "Hkv": Hkv, "Sq": Sq, "Skv": Skv, "D": D,
+                      "causal": causal, "split_kv": bool(need), "sharding": shard,
+                      "l2": "L2 flushed before every launch" if small else "inputs larger than L2"},
+           "roofline": roof, "gpu_launches": int(launches), "clocks": clk.summary()}
+    del Q, K, V, O, ws, flush
     torch.cuda.empty_cache()
     return res
 
@@ -358,21 +507,24 @@ def bench_gated_attention(cfg, args, dist, peaks):
                       "S": S, "D": D, "causal": causal, "gate": "sigmoid(G), G [B,Hq,S,D]",
                       "l2": "inputs larger than L2"},
            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
-                        "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"], "traffic": None},
+                        "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
+                        "traffic": _scaled(profile_traffic("attn_gated_d256"),
+                                           attn_flops(B, Hq, S, D, causal) / flops_total)},
            "gpu_launches": int(launches), "clocks": clk.summary()}
     del Q, K, V, G, O
     torch.cuda.empty_cache()
     return res
 
 
-def bench_gdn_decode(cfg, args, dist, peaks, state_dtype=None):
+def bench_gdn_decode(cfg, args, dist, peaks, state_dtype=None, weak=False):
     """GDN decode over the config's 256 steps; state_dtype fp16/bf16 runs the 16-bit-state
-    entry (gdn_decode_sm100_state16), default the fp32 state."""
+    entry (gdn_decode_sm100_state16), default the fp32 state.  weak: every GPU runs the
+    config's B sequences (B x N in all) instead of a 1/N share of them."""
     import torch
     import b200lab
     import workloads
 
-    u0, Bl = split_units(cfg["B"], dist.world, dist.rank)
+    Bl = cfg["B"] if weak else split_units(cfg["B"], dist.world, dist.rank)[1]
     Hqk, Hv, d, T = cfg["Hqk"], cfg["Hv"], cfg["d"], cfg["steps"]
     dtype = cfg["dtype"]
     dev = torch.device("cuda", dist.local)
@@ -427,13 +579,16 @@ def bench_gdn_decode(cfg, args, dist, peaks, state_dtype=None):
     ms = dist.max(ms_local)
     gbs = bytes_step_local * dist.world / (ms * 1e-3) / 1e9
     achieved = bytes_step_local / (ms_local * 1e-3) / 1e9
-    traffic = profile_traffic("gdn_decode_c4") if ssz == 4 else None
+    traffic = _scaled(profile_traffic("gdn_decode_c4" if ssz == 4 else "gdn_decode_state16_c4"),
+                      Bl / cfg["B"])
     sname = {4: "fp32", 2: str(sdt).replace("torch.", "")}[ssz]
     res = {"metric": "GDN decode GB/s", "value": gbs, "unit": "GB/s", "us_per_step": ms * 1e3,
            "steps": T, "bytes_per_step": bytes_step_local * dist.world,
-           "config": {"workload": "gdn_decode_c4" + ("" if ssz == 4 else f"_state_{sname}"),
-                      "B": cfg["B"], "Hqk": Hqk, "Hv": Hv, "d": d,
-                      "state": f"{sname} [B,Hv,128,128] in place", "sharding": "sequences",
+           "config": {"workload": "gdn_decode_c4" + ("" if ssz == 4 else f"_state_{sname}")
+                      + ("_weak" if weak else ""),
+                      "B": Bl * dist.world if weak else cfg["B"], "Hqk": Hqk, "Hv": Hv, "d": d,
+                      "state": f"{sname} [B,Hv,128,128] in place",
+                      "sharding": f"sequences, {Bl} per GPU (weak scaling)" if weak else "sequences",
                       "l2": "state larger than L2 (134 MB at N=1), 256 consecutive steps" if ssz == 4
                       else "L2 flushed before every step (16-bit state 67 MB at N=1)"},
            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -444,7 +599,10 @@ def bench_gdn_decode(cfg, args, dist, peaks, state_dtype=None):
     return res
 
 
-def bench_gdn_prefill(cfg, args, dist, peaks):
+def bench_gdn_prefill(cfg, args, dist, peaks, fused=False):
+    """GDN chunked prefill at C3, L2 flushed before every launch.  fused: the entry with the
+    pre-processing fused in (raw q, k L2-normalised in the kernels, gates and beta from
+    logits: gdn_prefill_sm100_fused)."""
     import torch
     import b200lab
     import workloads
@@ -454,6 +612,13 @@ def bench_gdn_prefill(cfg, args, dist, peaks):
     h0, Hv_l, hq0, Hqk_l = sharding.gdn_prefill_shard(Hqk, Hv, dist.world, dist.rank)
     dev = torch.device("cuda", dist.local)
     q, k, v, g, b = workloads.gdn_inputs(1, T, Hqk_l, Hv_l, d, dtype, seed=7 + dist.rank, device=dev)
+    if fused:  # raw q, k (unnormalised) and the gate / beta logits with per-head parameters
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(17 + dist.rank)
+        q, k = (torch.randn(t.shape, generator=gen, device=dev).to(dtype) for t in (q, k))
+        g, b = (torch.randn(t.shape, generator=gen, device=dev) for t in (g, b))
+        A_log = torch.randn((Hv_l,), generator=gen, device=dev) * 0.5
+        dt_bias = torch.randn((Hv_l,), generator=gen, device=dev) * 0.5
     state = torch.zeros((1, Hv_l, d, d), dtype=torch.float32, device=dev)
     out = torch.empty((1, T, Hv_l, d), dtype=dtype, device=dev)
     stream = torch.cuda.current_stream()
@@ -462,7 +627,11 @@ def bench_gdn_prefill(cfg, args, dist, peaks):
     flush = L2Flush(dev)
 
     def step():
-        b200lab.gdn_prefill(q, k, v, g, b, state, out=out, workspace=ws, stream=stream)
+        if fused:
+            b200lab.gdn_prefill_fused(q, k, v, g, b, state, A_log=A_log, dt_bias=dt_bias, out=out,
+                                      workspace=ws, stream=stream)
+        else:
+            b200lab.gdn_prefill(q, k, v, g, b, state, out=out, workspace=ws, stream=stream)
 
     try:
         step()
@@ -491,14 +660,35 @@ def bench_gdn_prefill(cfg, args, dist, peaks):
                    + (g.numel() + b.numel()) * 4 + state.numel() * 4 * 2)
     flops_local = Hv_l * T * (6 * 64 * d + 6 * d * d) + Hqk_l * T * 4 * 64 * d
     achieved = bytes_local / (ms_local * 1e-3) / 1e9
+    allgather = None
+    if dist.world > 1:  # o [1][T][Hv][d] on every rank: all-gather + on-device permute
+        for _ in range(2):
+            full = sharding.allgather_gdn_prefill(out, Hv)
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = evs[0]
+        e0.record(stream)
+        for _ in range(3):
+            full = sharding.allgather_gdn_prefill(out, Hv)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ag_ms = dist.max(e0.elapsed_time(e1) / 3)
+        nbytes = full.numel() * full.element_size()
+        allgather = {"ms": ag_ms, "bus_gbs": nbytes * (dist.world - 1) / dist.world / (ag_ms * 1e-3) / 1e9,
+                     "includes": "all_gather_into_tensor + head permute"}
+        del full
+    wl = "gdn_prefill_c3" + ("_fused" if fused else "")
     res = {"metric": "GDN prefill tok/s", "value": T / (ms * 1e-3), "unit": "tok/s",
            "us_per_step": ms * 1e3,
-           "config": {"workload": "gdn_prefill_c3", "B": 1, "T": T, "Hqk": Hqk, "Hv": Hv, "d": d,
+           "config": {"workload": wl, "B": 1, "T": T, "Hqk": Hqk, "Hv": Hv, "d": d,
                       "chunk": 64, "sharding": "v-heads", "l2": "L2 flushed between launches"},
            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                        "frac": achieved / peaks["hbm_gbs"], "traffic": profile_traffic("gdn_prefill_c3"),
+                        "frac": achieved / peaks["hbm_gbs"],
+                        "traffic": _scaled(profile_traffic(wl), Hv_l / Hv),
                         "tensor_tflops": flops_local / (ms_local * 1e-3) / 1e12},
            "gpu_launches": int(launches), "clocks": clk.summary()}
+    if allgather:
+        res["allgather"] = allgather
     del q, k, v, g, b, state, out, ws, flush
     torch.cuda.empty_cache()
     return res
@@ -652,10 +842,18 @@ def run_ours(args):
     if args.secondary and name == "attn_c5" and not args.attn_shape:
         import torch
         state16 = lambda c, a, d_, p: bench_gdn_decode(c, a, d_, p, state_dtype=torch.float16)  # noqa: E731
-        for key, fn, c in (("gdn_decode", bench_gdn_decode, workloads.CONFIGS["gdn_decode_c4"]),
-                           ("gdn_decode_state16", state16, workloads.CONFIGS["gdn_decode_c4"]),
-                           ("attn_gated_d256", bench_gated_attention, workloads.CONFIGS["attn_gated_d256"]),
-                           ("gdn_prefill", bench_gdn_prefill, workloads.CONFIGS["gdn_prefill_c3"])):
+        weak = lambda c, a, d_, p: bench_gdn_decode(c, a, d_, p, weak=True)  # noqa: E731
+        fused = lambda c, a, d_, p: bench_gdn_prefill(c, a, d_, p, fused=True)  # noqa: E731
+        todo = [("gdn_decode", bench_gdn_decode, workloads.CONFIGS["gdn_decode_c4"]),
+                ("gdn_decode_state16", state16, workloads.CONFIGS["gdn_decode_c4"]),
+                ("attn_gated_d256", bench_gated_attention, workloads.CONFIGS["attn_gated_d256"]),
+                ("gdn_prefill", bench_gdn_prefill, workloads.CONFIGS["gdn_prefill_c3"]),
+                ("gdn_prefill_fused", fused, workloads.CONFIGS["gdn_prefill_c3"])]
+        if dist.world > 1:  # at N = 1 the weak-scaling decode is the gdn_decode line itself
+            todo.insert(1, ("gdn_decode_weak", weak, workloads.CONFIGS["gdn_decode_c4"]))
+        for key, shp in ATTN_CASES.items():
+            todo.append((key, lambda c, a, d_, p, key=key: bench_attn_case(key, c, a, d_, p), shp))
+        for key, fn, c in todo:
             try:
                 secondary[key] = fn(c, args, dist, peaks)
             except Exception as e:  # report, keep the headline line
@@ -690,8 +888,35 @@ def run_ours(args):
                     except Exception as e:
                         secondary["gdn_prefill"]["cpu_baseline_reference"] = {"status": repr(e)}
             line["secondary"] = secondary
+        # last key of the line: a compact digest of every figure above, so that a reader who
+        # keeps only the end of the output still sees them all
+        line["summary"] = summary_of(line)
     dist.close()
     return line
+
+
+def summary_of(line):
+    """{name: [value, roofline frac]} for the headline and every secondary line, plus the
+    end-to-end, copy-floor and all-gather figures, rounded to 4 significant digits."""
+    def r(x):
+        return None if x is None else float(f"{x:.4g}")
+
+    out = {"n": line["n_gpus"], line["config"]["workload"]: [r(line["value"]), r(line["roofline"]["frac"])]}
+    e2e = line.get("e2e", {})
+    if "value" in e2e:
+        out["e2e"] = [r(e2e["value"]), r(e2e.get("ms_per_step")), r(e2e.get("copy_floor_ms"))]
+    if "allgather" in line:
+        out["allgather"] = [r(line["allgather"]["ms"]), r(line["allgather"].get("bus_gbs"))]
+    for key, sec in line.get("secondary", {}).items():
+        if "value" not in sec:
+            out[key] = sec.get("status", "no value")[:60]
+            continue
+        out[key] = [r(sec["value"]), r(sec.get("roofline", {}).get("frac"))]
+        if "allgather" in sec:
+            out[key + "_allgather"] = [r(sec["allgather"]["ms"]), r(sec["allgather"].get("bus_gbs"))]
+    out["units"] = "[value in the line's unit, roofline frac]; e2e [TFLOP/s, ms, copy-floor ms]; " \
+                   "allgather [ms, bus GB/s]"
+    return out
 
 
 def main():

@@ -1,7 +1,8 @@
 """(batch, head) partition of the hot path over the GPUs of one node.
 
 Every unit is independent, so a shard needs no data-path collective; outputs
-can be re-assembled with one all-gather (bench.py times NCCL's).  Units:
+are re-assembled with one all-gather (allgather_* below; NCCL on the GPUs).
+Units:
 
 * attention: (batch, kv-head), each with its Hq/Hkv q-heads, so K/V are never
   duplicated and a shard of Q/O [B][Hq][S][D] is one contiguous slab;
@@ -49,3 +50,42 @@ def gdn_prefill_shard(Hqk: int, Hv: int, world: int, rank: int):
 
 def gdn_decode_shard(B: int, world: int, rank: int):
     return split_units(B, world, rank)
+
+
+# ----------------------------------------------------------------------------
+# Re-assembly of the sharded outputs: one all-gather over the process group
+# (NCCL over NVLink on the GPUs, gloo on the CPU), every rank gets the whole output.
+# ----------------------------------------------------------------------------
+def _gather_flat(local, group):
+    import torch
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    flat = local.contiguous().view(-1)
+    out = torch.empty((world * flat.numel(),), dtype=local.dtype, device=local.device)
+    dist.all_gather_into_tensor(out, flat, group=group)
+    return out, world
+
+
+def allgather_attention(o_local, B: int, Hq: int, group=None):
+    """O [B][Hq][Sq][D] on every rank from the (batch, kv-head) shards of attn_shard.  Units
+    are numbered b * Hkv + kv-head and a rank holds a contiguous run of them, i.e. one slab of
+    O, so the rank-ordered concatenation is the output itself (no permute)."""
+    out, _ = _gather_flat(o_local, group)
+    return out.view(B, Hq, o_local.shape[-2], o_local.shape[-1])
+
+
+def allgather_gdn_prefill(o_local, Hv: int, group=None):
+    """o [B][T][Hv][d] on every rank from the v-head shards of gdn_prefill_shard.  Rank r
+    holds v-heads [r n, (r+1) n) of every token, so the gathered [world][B][T][n][d] is
+    permuted on the device to [B][T][world][n][d] = [B][T][Hv][d] (one copy kernel)."""
+    B, T, n, d = o_local.shape
+    out, world = _gather_flat(o_local, group)
+    if world * n != Hv:
+        raise ValueError(f"{world} shards of {n} v-heads do not make {Hv}")
+    return out.view(world, B, T, n, d).permute(1, 2, 0, 3, 4).reshape(B, T, Hv, d)
+
+
+def allgather_gdn_decode(o_local, group=None):
+    """o [B][Hv][d] on every rank from the sequence shards of gdn_decode_shard."""
+    out, world = _gather_flat(o_local, group)
+    return out.view((world * o_local.shape[0],) + tuple(o_local.shape[1:]))
