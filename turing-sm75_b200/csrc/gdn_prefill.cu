@@ -41,10 +41,11 @@ __device__ int g_err_gdn_prefill = 0;
 
 constexpr int kC = 64;    // chunk length
 constexpr int kD = 128;   // dk = dv
+constexpr int kSlice = 32;  // state columns (v dim) per kernel-2 CTA
 
 // ---- workspace layout ------------------------------------------------------
 struct WsLayout {
-    size_t w, u, aqk, m, qt, gcs, vdec, total;
+    size_t w, u, aqk, m, gcs, rq, rk, total;
 };
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 __host__ __device__ inline WsLayout ws_layout(size_t nbhc) {
@@ -53,10 +54,10 @@ __host__ __device__ inline WsLayout ws_layout(size_t nbhc) {
     L.u = align_up(L.w + nbhc * kC * kD * 2, 1024);
     L.aqk = align_up(L.u + nbhc * kC * kD * 2, 1024);
     L.m = align_up(L.aqk + nbhc * kC * kC * 2, 1024);
-    L.qt = align_up(L.m + nbhc * kC * kC * 2, 1024);
-    L.gcs = align_up(L.qt + nbhc * kC * kD * 2, 1024);
-    L.vdec = align_up(L.gcs + nbhc * kC * 4, 1024);  // e^{gcs_last - gcs_t} (/ |k_t| fused)
-    L.total = align_up(L.vdec + nbhc * kC * 4, 1024);
+    L.gcs = align_up(L.m + nbhc * kC * kC * 2, 1024);
+    L.rq = align_up(L.gcs + nbhc * kC * 4, 1024);   // 1/|q_t|, 1/|k_t| (fused entry only)
+    L.rk = align_up(L.rq + nbhc * kC * 4, 1024);
+    L.total = align_up(L.rk + nbhc * kC * 4, 1024);
     return L;
 }
 
@@ -66,7 +67,7 @@ struct PrepParams {
     const float* beta;     // fused: the beta logits b
     const float* A_log;    // fused: [Hv] or null
     const float* dt_bias;  // fused: [Hv] or null
-    size_t ws_u, ws_aqk, ws_gcs, ws_vdec;
+    size_t ws_u, ws_aqk, ws_gcs, ws_rq, ws_rk;
     const int* cu;  // packed sequences: [B+1] token offsets (device), or null: B x T dense
     int T, Hqk, Hv, nch, head_map;  // with cu, T is the longest sequence; nch = ceil(T / 64)
     int ntok;                       // tokens in the flattened dimension (B*T, or cu[B])
@@ -271,8 +272,7 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
     gdn_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmW,
                     const __grid_constant__ CUtensorMap tmU, const __grid_constant__ CUtensorMap tmAqk,
-                    const __grid_constant__ CUtensorMap tmM, const __grid_constant__ CUtensorMap tmQt,
-                    const PrepParams p) {
+                    const __grid_constant__ CUtensorMap tmM, const PrepParams p) {
     using namespace prep;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -407,37 +407,11 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
         ok = __all_sync(0xffffffffu, mbar_wait(&ms->bar_tma, 0, abort, &g_err_gdn_prefill)) && ok;
         if (tid < kC) ms->rk[tid] = row_rnorm<T16>(smem + kK0, smem + kK1, tid);
         else ms->rq[tid - kC] = row_rnorm<T16>(smem + kQ0, smem + kQ1, tid - kC);
+        fence_proxy_async_smem();  // these reads of Q come before the V load's writes
         __syncthreads();
     }
-    // Qt = diag(e^{gcs_t} / |q_t|) Q, scaled in place over the Q tile (MMA1 has read it) and
-    // stored to the workspace: the state pass's output product takes it as is.  Thread =
-    // (row, 64-column box); scaling whole rows commutes with the 128-byte swizzle.
-    ok = __all_sync(0xffffffffu, mbar_wait(&ms->bar_tma, 0, abort, &g_err_gdn_prefill)) && ok;
-    tc_fence_after();
-    {
-        const int r = tid & (kC - 1);
-        uint8_t* qrow = smem + (tid < kC ? kQ0 : kQ1) + r * 128;
-        float f = ex2f(ms->g2[r]);
-        if constexpr (kFused) f *= ms->rq[r];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            uint4 raw = *reinterpret_cast<const uint4*>(qrow + q * 16);
-            uint32_t* w = &raw.x;
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const T16* e = reinterpret_cast<const T16*>(&w[u]);
-                w[u] = Elem<T16>::pack2(Elem<T16>::to_f(e[0]) * f, Elem<T16>::to_f(e[1]) * f);
-            }
-            *reinterpret_cast<uint4*>(qrow + q * 16) = raw;
-        }
-        fence_proxy_async_smem();
-    }
-    __syncthreads();
     if (tid == 0 && ok) {
-        tma_store_3d(&tmQt, smem + kQ0, 0, 0, (int)bhc);
-        tma_store_3d(&tmQt, smem + kQ1, 64, 0, (int)bhc);
-        bulk_commit();
-        bulk_wait_read();  // Qt has left shared memory: V goes over it (needed only by MMA2)
+        // Q has been read: V goes over it (needed only by MMA2, after the solve)
         mbar_arrive_expect_tx(&ms->bar_v, 2 * 8192);
         tma_load_4d(smem + kV0, &tmV, &ms->bar_v, 0, h, tok0, 0);
         tma_load_4d(smem + kV1, &tmV, &ms->bar_v, 64, h, tok0, 0);
@@ -590,9 +564,10 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
     if (ok && warp < 2) {
         stage_rows(smem + kK0);  // W -> [K0 | . | K1 | .]
         reinterpret_cast<float*>(p.ws + p.ws_gcs)[bhc * kC + row] = gcs_r;
-        float vdec = __expf(ms->gcs[kC - 1] - gcs_r);  // the state update's row decay
-        if constexpr (kFused) vdec *= ms->rk[row];     // K^T diag(1/|k|): normalised keys
-        reinterpret_cast<float*>(p.ws + p.ws_vdec)[bhc * kC + row] = vdec;
+        if constexpr (kFused) {
+            reinterpret_cast<float*>(p.ws + p.ws_rk)[bhc * kC + row] = ms->rk[row];
+            reinterpret_cast<float*>(p.ws + p.ws_rq)[bhc * kC + row] = ms->rq[row];
+        }
     }
     tc_fence_before();
     __syncthreads();  // W is out of TMEM
@@ -611,6 +586,8 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
     tc_fence_before();
     __syncthreads();
     if (tid == 0 && ok) {
+        tma_store_3d(&tmW, smem + kK0, 0, 0, (int)bhc);
+        tma_store_3d(&tmW, smem + kK1, 64, 0, (int)bhc);
         tma_store_3d(&tmU, smem + kV0, 0, 0, (int)bhc);
         tma_store_3d(&tmU, smem + kV1, 64, 0, (int)bhc);
         bulk_commit();
@@ -677,32 +654,11 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
         }
         fence_proxy_async_smem();
     }
-    // The state pass uses W only as e^{gcs_last of the previous chunk} W: the staged W (read
-    // unscaled by the M product above) is rescaled in place before it is stored.  Thread =
-    // (row, 64-column box), as for Qt.
-    if (c > 0 && ok) {
-        const float gam = __expf(ms->gprev[kC - 1]);
-        uint8_t* wrow = smem + (tid < kC ? kK0 : kK1) + (tid & (kC - 1)) * 128;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            uint4 raw = *reinterpret_cast<const uint4*>(wrow + q * 16);
-            uint32_t* w = &raw.x;
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const T16* e = reinterpret_cast<const T16*>(&w[u]);
-                w[u] = Elem<T16>::pack2(Elem<T16>::to_f(e[0]) * gam, Elem<T16>::to_f(e[1]) * gam);
-            }
-            *reinterpret_cast<uint4*>(wrow + q * 16) = raw;
-        }
-        fence_proxy_async_smem();
-    }
     __syncthreads();
     if (tid == 0 && ok) {
-        tma_store_3d(&tmW, smem + kK0, 0, 0, (int)bhc);
-        tma_store_3d(&tmW, smem + kK1, 64, 0, (int)bhc);
         tma_store_3d(&tmM, smem + kAT, 0, 0, (int)bhc);
         bulk_commit();
-        bulk_wait_all();   // the next kernel reads Qt, W, U, Aqk, M
+        bulk_wait_all();   // the next kernel reads W, U, Aqk, M
     }
     if (tid == 0) {
         mma_commit(&ms->drain);
@@ -717,122 +673,149 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
 }
 
 // ===========================================================================
-// Kernel 2: sequential state pass, one CTA per (sequence, v-head)
+// Kernel 2: sequential state pass
 // ===========================================================================
-// Transposed form: the v column j of the state is the MMA's M dimension (TMEM lane j), so
-// every product has N = 128 (the full tensor rate) and the state itself never leaves TMEM.
-// With S_c the state at the start of chunk c ([dv][dk], fp32), Vn_c = U_c - W_c S_c^T and
-// gam_c = e^{gcs_last,c}, per chunk:
-//   Y_c   = S_c [Qt_c; Wp_{c+1}]^T + Vn_c^T [Aqk_c; M_{c+1}]^T       (lane j, 128 columns)
-//           columns 0-63:   o_c^T / scale     (Qt_c = diag(e^{gcs}) Q_c from the prep pass)
-//           columns 64-127: U_{c+1} - Vn_{c+1}  (Wp_{c+1} = gam_c W_{c+1}, M_{c+1} as below)
-//   S_{c+1} = gam_c S_c + Vt_c^T K_c,   Vt_c = diag(e^{gcs_last - gcs}) Vn_c
-// where M_{c+1} = W_{c+1} K_c^T diag(e^{gcs_last,c - gcs_c}) (prep pass) carries the chain
-// through Vn: Vn_{c+1} = U_{c+1} - gam_c W_{c+1} S_c^T - M_{c+1} Vn_c.  The A operands (S_c,
-// Vn_c, Vt_c as 16-bit) are written to TMEM by the threads; the B operands come by TMA.
-namespace ch {
-// warps 0-3: the state (thread = v column j = TMEM lane): S16_c and gam_c S_c into TMEM;
-// warps 4-7: Vn_{c+1}, Vt_{c+1} from Y_c and U_{c+1}, then the outputs o_c;
-// warp 8: TMA producer; warp 9: TMEM owner and MMA issuer.
-constexpr int kThreads = 320;
-constexpr int kWarpVn = 4, kWarpProducer = 8, kWarpMma = 9;
-// one stage (the inputs of chunk c's products), 81 KiB:
-//   B1 [Qt_c b0 | Wp_{c+1} b0 | Qt_c b1 | Wp_{c+1} b1]  32 KiB  B of Y p1 (K-major, 128 rows)
-//   B2 [Aqk_c | M_{c+1}]                                16 KiB  B of Y p2 (K-major)
-//   Kt [K_c b0 | K_c b1]                                16 KiB  B of the state update (MN-major)
-//   U  [U_{c+1} b0 | U_{c+1} b1]                        16 KiB  read by the Vn warps
-//   G  gcs_c | gcs_{c+1} | 1/|k| of chunk c+1 (fp32 x 64 each)
-// (b0/b1: 64-column boxes, 128-byte swizzle).  The prologue stage carries Wp_0, U_0, gcs_0.
-constexpr int kB1 = 0, kB2 = 32768, kKt = 49152, kU = 65536, kG = 81920;
-constexpr int kStage = 82944;
-constexpr int kStages = 2;
-constexpr int kMisc = kStages * kStage;
-constexpr int kBytes = kMisc + 512;
+// The chain runs on Vn, not on S.  With R_{c+1} = W_{c+1} S_c^T and
+// M_{c+1} = W_{c+1} K_c^T diag(e^{gcs_last,c - gcs_c}) (from kernel 1),
+//   Vn_{c+1} = U_{c+1} - W_{c+1} S_{c+1}^T = U_{c+1} - e^{gcs_last,c} R_{c+1} - M_{c+1} Vn_c,
+// so the only MMA between Vn_c and Vn_{c+1} is the 64-deep M_{c+1} Vn_c; the 128-deep
+// products with S (R_{c+1} and Q_c S_c^T) run a chunk ahead, off the chain.
+namespace st {
+// warps 0-3 state (thread = key row of the slice), 4-5 outputs (TMEM lanes 0-63),
+// 6-7 Vn (lanes 64-127), 8 TMA producer, 9 chain MMAs, 10 state MMAs
+constexpr int kThreads = 352;
+constexpr int kWarpOut = 4, kWarpVn = 6, kWarpProducer = 8, kWarpMmaA = 9, kWarpMmaB = 10;
+// one stage of chunk c (69 KiB):
+//   A1  [Q_c b0 | W_{c+1} b0 | Q_c b1 | W_{c+1} b1]  32 KiB: A of [Q_c; W_{c+1}] S_c^T
+//   Kt  [K_c b0 | K_c b1]                              16 KiB: A of K_c^T Vt_c (MN-major)
+//   AM  [Aqk_c | M_{c+1}]                              16 KiB: A of [Aqk_c; M_{c+1}] Vn_c
+//   U   this CTA's 32 columns of U_c (64-byte swizzle)  4 KiB;  G  gcs_c  256 B
+// (b0/b1: 64-column boxes).  Three stages; the prologue's W_0 borrows stage 2's A1.
+constexpr int kStage = 70656;
+constexpr int kA1 = 0, kKt = 32768, kAM = 49152, kU = 65536, kG = 69632;
+constexpr int kStageTx = 8 * 8192 + 4096 + kC * 4;
+constexpr int kStages = 3;
+// B operands, MN-major with 64-byte swizzle: one 64-byte row (32 state columns,
+// 16-bit) per K index, so each thread writes its row as four 16-byte chunks
+constexpr int kSt = kStages * kStage;    // S^T tile: 128 keys x 32 v, 8 KiB
+constexpr int kVn = kSt + 8192;          // Vn tile: 64 tokens x 32 v, 4 KiB
+constexpr int kVt = kVn + 4096;          // decayed Vn tile, 4 KiB
+constexpr int kMisc = kVt + 4096;
+constexpr int kBytes = kMisc + 256;
 constexpr int kAlloc = kBytes + 1024;
-static_assert(kAlloc <= 232448, "chain kernel shared memory above the 227 KiB per-CTA limit");
-// TMEM columns: S fp32 [0,128); Y buffers [128,256), [256,384); A operands S16 (64 cols),
-// Vn16 (32), Vt16 (32)
-constexpr uint32_t kColS = 0, kColY = 128, kColS16 = 384, kColVn = 448, kColVt = 480;
-constexpr uint32_t kTmemCols = 512;
+static_assert(kAlloc <= 232448, "state kernel shared memory above the 227 KiB per-CTA limit");
+constexpr uint32_t kTmemCols = 256;
+// TMEM, two buffers each by chunk parity (32 columns a buffer):
+//   X1 = [Aqk_c; M_{c+1}] Vn_c   lanes 0-63 intra-chunk output, 64-127 chain term
+//   DS = K_c^T Vt_c              lane = key: the state increment
+//   RQ = [Q_c; W_{c+1}] S_c^T    lanes 0-63 Q S^T, 64-127 R_{c+1}
+constexpr uint32_t kColX1 = 0, kColDS = 64, kColRQ = 128;
 
 struct Misc {
     uint64_t full[kStages], empty[kStages];
-    uint64_t s_ready;      // S16_c and gam_c S_c are in TMEM (4 state-warp arrivals)
-    uint64_t vn_ready;     // Vn_c, Vt_c are in TMEM (4 Vn-warp arrivals)
-    uint64_t ds_done;      // the state update of chunk c has completed (MMA commit)
-    uint64_t y_full[2];    // Y buffer complete (MMA commit)
-    uint64_t y_empty[2];   // Y buffer read out (4 Vn-warp arrivals)
-    uint64_t drain;
+    uint64_t pro_full, pro_done;
+    uint64_t s_ready[2];
+    uint64_t vn_ready;  // Vn_c written: the chain product X1(c) may run
+    uint64_t vt_ready;  // decayed Vn_c written: the state increment DS(c) may run
+    uint64_t x1_full[2], ds_full[2], rq_full[2];
+    uint64_t o_done[2];  // the output warps have read X1 / RQ buffer (c & 1) of chunk c
+    uint64_t drain_a, drain_b;
     uint32_t tmem_base;
     int abort;
 };
-static_assert(sizeof(Misc) <= kBytes - kMisc, "chain Misc overflows its slot");
-// arrivals on a stage's `empty` barrier: the MMA thread's commit, 4 Vn warps, 4 state warps
-constexpr uint32_t kEmptyCount = 9;
-}  // namespace ch
+static_assert(sizeof(Misc) <= kBytes - kMisc, "state Misc overflows its slot");
 
-struct ChainParams {
+// rq_full[c & 1] completes for the prologue product (counted as c = -1, buffer 1)
+// and then for c = 0, 1, 2, ...: the parity of the completion that belongs to c
+__device__ __forceinline__ uint32_t rq_parity(int c) {
+    return c < 0 ? 0u : (uint32_t)(((c & 1) ? (c + 1) >> 1 : c >> 1) & 1);
+}
+}  // namespace st
+
+// byte offset of 16-byte chunk q (columns 8q..8q+7) of row r in a 64-byte-swizzled tile
+__device__ __forceinline__ uint32_t sw64_chunk(int r, int q) {
+    return (uint32_t)(r * 64 + ((q ^ ((r >> 1) & 3)) << 4));
+}
+
+struct StateParams {
     const uint8_t* ws;
     float* state;
     void* o;
-    size_t ws_gcs, ws_vdec;
+    size_t ws_gcs, ws_rq, ws_rk;
     const int* cu;  // as PrepParams
     int T, Hqk, Hv, nch, head_map;
     int ntok;
     float scale;
 };
 
-// Stage of chunk c: slot c & 1; slot 1 holds the prologue first, so both slots' use counts
-// are (c + 1) >> 1 and the barrier parities follow from it.
-__device__ __forceinline__ uint32_t ch_use(int c) { return (uint32_t)((c + 1) >> 1); }
-
-// 16-bit element (t, j) of a 64-token x 128-column tile held as two 128B-swizzled boxes
-template <typename T16>
-__device__ __forceinline__ float tile_elem(const uint8_t* tile, int t, int j) {
-    const int off = (j >> 6) * 8192 + t * 128 + ((((j & 63) >> 3) ^ (t & 7)) << 4) + (j & 7) * 2;
-    return Elem<T16>::to_f(*reinterpret_cast<const T16*>(tile + off));
+// 32 consecutive outputs of one thread as 16-byte vector stores
+template <typename TOut>
+__device__ __forceinline__ void store_row32(TOut* dst, const float (&v)[32]) {
+    if constexpr (sizeof(TOut) == 4) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+            reinterpret_cast<float4*>(dst)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            uint4 pk;
+            pk.x = Elem<TOut>::pack2(v[8 * q + 0], v[8 * q + 1]);
+            pk.y = Elem<TOut>::pack2(v[8 * q + 2], v[8 * q + 3]);
+            pk.z = Elem<TOut>::pack2(v[8 * q + 4], v[8 * q + 5]);
+            pk.w = Elem<TOut>::pack2(v[8 * q + 6], v[8 * q + 7]);
+            reinterpret_cast<uint4*>(dst)[q] = pk;
+        }
+    }
 }
 
-template <typename T16, typename TOut>
-__global__ void __launch_bounds__(ch::kThreads, 1)
-    gdn_chain_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQt,
+template <typename T16, typename TOut, bool kFused>
+__global__ void __launch_bounds__(st::kThreads, 1)
+    gdn_state_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmAqk,
                      const __grid_constant__ CUtensorMap tmM, const __grid_constant__ CUtensorMap tmU,
-                     const ChainParams p) {
-    using namespace ch;
+                     const StateParams p) {
+    using namespace st;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     Misc* ms = reinterpret_cast<Misc*>(smem + kMisc);
     volatile int* abort = &ms->abort;
 
-    const int h = blockIdx.x;
-    const int b = blockIdx.y;
+    const int slice = blockIdx.x;
+    const int h = blockIdx.y;
+    const int b = blockIdx.z;
     const SeqSpan seq = seq_span(p.cu, p.T, b);
     if (!seq_ok(seq, p.T, p.ntok)) return;    // recorded by the prep grid; state left as it is
     const int nch = (seq.len + kC - 1) / kC;  // this sequence's chunks (p.nch for the longest)
     if (nch == 0) return;                     // an empty sequence: its state stays as it is
+    const int c0 = slice * kSlice;
     const int hq = qk_head(h, p.Hqk, p.Hv, p.head_map);
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
-    const size_t bh = (size_t)b * p.Hv + h;
-    const int bhc0 = (int)(bh * p.nch);  // workspace slots: p.nch chunks a (sequence, head)
+    const size_t bh = (size_t)b * p.Hv + h;  // workspace slots: p.nch chunks a (sequence, head)
 
     if (tid == 0) {
         for (int i = 0; i < kStages; ++i) {
             mbar_init(&ms->full[i], 1);
-            mbar_init(&ms->empty[i], kEmptyCount);
-            mbar_init(&ms->y_full[i], 1);
-            mbar_init(&ms->y_empty[i], 4);
+            mbar_init(&ms->empty[i], 2);  // one commit from each MMA thread
         }
-        mbar_init(&ms->s_ready, 4);
-        mbar_init(&ms->vn_ready, 4);
-        mbar_init(&ms->ds_done, 1);
-        mbar_init(&ms->drain, 1);
+        mbar_init(&ms->pro_full, 1);
+        mbar_init(&ms->pro_done, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&ms->s_ready[i], 4);  // one arrival per state warp
+            mbar_init(&ms->x1_full[i], 1);
+            mbar_init(&ms->ds_full[i], 1);
+            mbar_init(&ms->rq_full[i], 1);
+            mbar_init(&ms->o_done[i], 2);   // one per output warp
+        }
+        mbar_init(&ms->vn_ready, 2);        // one per Vn warp
+        mbar_init(&ms->vt_ready, 2);
+        mbar_init(&ms->drain_a, 1);
+        mbar_init(&ms->drain_b, 1);
         ms->abort = 0;
         fence_barrier_init();
     }
-    if (warp == kWarpMma) {
+    if (warp == kWarpMmaA) {
         tmem_alloc(&ms->tmem_base, kTmemCols);
         tmem_relinquish();
     }
@@ -841,259 +824,273 @@ __global__ void __launch_bounds__(ch::kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = ms->tmem_base;
     constexpr uint32_t kFmt = Elem<T16>::kFmt;
-    volatile int no_abort = 0;  // drain waits ignore the abort flag: copies in flight land first
 
     if (warp == kWarpProducer) {
         if (lane == 0) {
             const float* gcs_all = reinterpret_cast<const float*>(p.ws + p.ws_gcs);
-            const float* vdec_all = reinterpret_cast<const float*>(p.ws + p.ws_vdec);
-            int last_use[kStages] = {-1, 0};  // slot 1 carries the prologue (use 0)
-            grid_dependency_wait();  // Qt, W, U, Aqk, M, gcs come from the prep grid
-            {   // prologue stage (slot 1): Wp_0 in the W rows of B1, U_0, gcs_0 and decays
-                uint8_t* stg = smem + kStage;
-                uint64_t* bar = &ms->full[1];
-                mbar_arrive_expect_tx(bar, 4 * 8192 + 2 * 256);
-                tma_load_3d(stg + kB1 + 8192, &tmW, bar, 0, 0, bhc0);
-                tma_load_3d(stg + kB1 + 24576, &tmW, bar, 64, 0, bhc0);
-                tma_load_3d(stg + kU, &tmU, bar, 0, 0, bhc0);
-                tma_load_3d(stg + kU + 8192, &tmU, bar, 64, 0, bhc0);
-                bulk_load_1d(stg + kG + 256, gcs_all + (size_t)bhc0 * kC, kC * 4, bar);
-                bulk_load_1d(stg + kG + 512, vdec_all + (size_t)bhc0 * kC, kC * 4, bar);
-            }
+            const int bhc0 = (int)(bh * p.nch);
+            grid_dependency_wait();  // W, U, Aqk, M, gcs come from the prep grid
+            // prologue: W_0 into the W rows of stage 2's A1 tile
+            uint8_t* pro = smem + (kStages - 1) * kStage + kA1;
+            mbar_arrive_expect_tx(&ms->pro_full, 2 * 8192);
+            tma_load_3d(pro + 8192, &tmW, &ms->pro_full, 0, 0, bhc0);
+            tma_load_3d(pro + 24576, &tmW, &ms->pro_full, 64, 0, bhc0);
+            int issued = 0;
             for (int c = 0; c < nch; ++c) {
-                const int s = c & 1;
-                const uint32_t u = ch_use(c);
-                if (u >= 1 && !mbar_wait(&ms->empty[s], (u - 1) & 1, abort, &g_err_gdn_prefill)) break;
+                const int s = c % kStages;
+                if (!mbar_wait(&ms->empty[s], ((c / kStages) & 1) ^ 1, abort, &g_err_gdn_prefill)) break;
+                if (c == kStages - 1 && !mbar_wait(&ms->pro_done, 0, abort, &g_err_gdn_prefill)) break;
                 uint8_t* stg = smem + s * kStage;
                 uint64_t* bar = &ms->full[s];
                 const int bhc = bhc0 + c;
-                const int tok = seq.start + c * kC;
-                const bool next = c + 1 < nch;  // the last chunk has no successor to prepare
-                mbar_arrive_expect_tx(bar, 5 * 8192 + 256 + (next ? 5 * 8192 + 2 * 256 : 0));
-                tma_load_3d(stg + kB1, &tmQt, bar, 0, 0, bhc);
-                tma_load_3d(stg + kB1 + 16384, &tmQt, bar, 64, 0, bhc);
-                tma_load_3d(stg + kB2, &tmAqk, bar, 0, 0, bhc);
-                tma_load_4d(stg + kKt, &tmK, bar, 0, hq, tok, 0);
-                tma_load_4d(stg + kKt + 8192, &tmK, bar, 64, hq, tok, 0);
+                // W_{c+1}, M_{c+1} of the last chunk read the next sequence's first chunk (or
+                // zero fill past the end): those rows of the products are not used
+                mbar_arrive_expect_tx(bar, kStageTx);
+                tma_load_4d(stg + kA1 + 0, &tmQ, bar, 0, hq, seq.start + c * kC, 0);
+                tma_load_3d(stg + kA1 + 8192, &tmW, bar, 0, 0, bhc + 1);
+                tma_load_4d(stg + kA1 + 16384, &tmQ, bar, 64, hq, seq.start + c * kC, 0);
+                tma_load_3d(stg + kA1 + 24576, &tmW, bar, 64, 0, bhc + 1);
+                tma_load_4d(stg + kKt, &tmK, bar, 0, hq, seq.start + c * kC, 0);
+                tma_load_4d(stg + kKt + 8192, &tmK, bar, 64, hq, seq.start + c * kC, 0);
+                tma_load_3d(stg + kAM, &tmAqk, bar, 0, 0, bhc);
+                tma_load_3d(stg + kAM + 8192, &tmM, bar, 0, 0, bhc + 1);
+                tma_load_3d(stg + kU, &tmU, bar, c0, 0, bhc);
                 bulk_load_1d(stg + kG, gcs_all + (size_t)bhc * kC, kC * 4, bar);
-                if (next) {
-                    tma_load_3d(stg + kB1 + 8192, &tmW, bar, 0, 0, bhc + 1);
-                    tma_load_3d(stg + kB1 + 24576, &tmW, bar, 64, 0, bhc + 1);
-                    tma_load_3d(stg + kB2 + 8192, &tmM, bar, 0, 0, bhc + 1);
-                    tma_load_3d(stg + kU, &tmU, bar, 0, 0, bhc + 1);
-                    tma_load_3d(stg + kU + 8192, &tmU, bar, 64, 0, bhc + 1);
-                    bulk_load_1d(stg + kG + 256, gcs_all + (size_t)(bhc + 1) * kC, kC * 4, bar);
-                    bulk_load_1d(stg + kG + 512, vdec_all + (size_t)(bhc + 1) * kC, kC * 4, bar);
-                }
-                last_use[s] = (int)u;
+                issued = c + 1;
             }
-            // every copy issued has landed before the CTA exits
-            for (int s = 0; s < kStages; ++s)
-                if (last_use[s] >= 0) mbar_wait(&ms->full[s], last_use[s] & 1, &no_abort, &g_err_gdn_prefill);
+            mbar_wait(&ms->pro_full, 0, abort, &g_err_gdn_prefill);
+            for (int c = max(0, issued - kStages); c < issued; ++c)
+                mbar_wait(&ms->full[c % kStages], (c / kStages) & 1, abort, &g_err_gdn_prefill);
         }
-    } else if (warp == kWarpMma) {
+    } else if (warp == kWarpMmaA) {
+        // chain MMAs: X1 = [Aqk_c; M_{c+1}] Vn_c, then DS = K_c^T Vt_c
         if (lane == 0) {
-            constexpr uint32_t id_y = make_idesc(kFmt, 128, 128, false, false);   // B K-major
-            constexpr uint32_t id_ds = make_idesc(kFmt, 128, 128, false, true);   // B MN-major
-            const uint64_t dB1 = smem_desc(smem_u32(smem + kB1), 16, 1024, kLayoutSW128);
-            const uint64_t dB2 = smem_desc(smem_u32(smem + kB2), 16, 1024, kLayoutSW128);
-            const uint64_t dKt = smem_desc(smem_u32(smem + kKt), 8192, 1024, kLayoutSW128);
-            // Y p1 = S_c [Qt_c; Wp_{c+1}]^T  (A = S16 from TMEM, K = dk = 128)
-            auto p1 = [&](uint32_t so, uint32_t ycol) {
-#pragma unroll
-                for (int kk = 0; kk < kD / 16; ++kk) {
-                    const uint32_t off = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
-                    mma_f16_ts(tmem + ycol, tmem + kColS16 + kk * 8, dB1 + so + off, id_y, kk > 0 ? 1u : 0u);
-                }
-            };
-            bool ok = mbar_wait(&ms->full[1], 0, abort, &g_err_gdn_prefill) &&
-                      mbar_wait(&ms->s_ready, 0, abort, &g_err_gdn_prefill);
-            if (ok) {  // prologue: W_0 S_0^T into Y buffer 1 (its Qt half reads nothing loaded)
-                tc_fence_after();
-                p1(kStage >> 4, kColY + 128);
-                mma_commit(&ms->y_full[1]);
-                mma_commit(&ms->empty[1]);
-            }
-            for (int c = 0; ok && c < nch; ++c) {
-                const int s = c & 1;
-                const uint32_t so = (uint32_t)(s * kStage) >> 4;
-                const uint32_t ycol = kColY + (c & 1) * 128;
-                if (!mbar_wait(&ms->full[s], ch_use(c) & 1, abort, &g_err_gdn_prefill)) break;
-                if (!mbar_wait(&ms->s_ready, c & 1, abort, &g_err_gdn_prefill)) break;
-                if (c >= 1 && !mbar_wait(&ms->y_empty[c & 1], ((c - 1) >> 1) & 1, abort, &g_err_gdn_prefill))
-                    break;
-                tc_fence_after();
-                p1(so, ycol);
-                // Vn_c is the chain dependency: waited for last
+            constexpr uint32_t id_kb = make_idesc(kFmt, 128, kSlice, false, true);  // A K-major, B MN
+            constexpr uint32_t id_mn = make_idesc(kFmt, 128, kSlice, true, true);   // both MN-major
+            const uint64_t dAM = smem_desc(smem_u32(smem + kAM), 16, 1024, kLayoutSW128);
+            const uint64_t dK = smem_desc(smem_u32(smem + kKt), 8192, 1024, kLayoutSW128);
+            const uint64_t dVn = smem_desc(smem_u32(smem + kVn), 4096, 512, kLayoutSW64);
+            const uint64_t dVt = smem_desc(smem_u32(smem + kVt), 4096, 512, kLayoutSW64);
+            for (int c = 0; c < nch; ++c) {
+                const int s = c % kStages;
+                const uint32_t so = (s * kStage) >> 4;
+                const uint32_t buf = (c & 1) * 32;
+                // Vn_c is the chain dependency, so it is waited for last: every wait between
+                // it and the MMAs would lengthen the chain
+                if (!mbar_wait(&ms->full[s], (c / kStages) & 1, abort, &g_err_gdn_prefill)) break;
+                if (c >= 2 && !mbar_wait(&ms->o_done[c & 1], ((c - 2) >> 1) & 1, abort, &g_err_gdn_prefill)) break;
                 if (!mbar_wait(&ms->vn_ready, c & 1, abort, &g_err_gdn_prefill)) break;
                 tc_fence_after();
-                // S += Vt_c^T K_c  (A = Vt16 from TMEM, K = 64 tokens; the threads put gam_c S_c there)
 #pragma unroll
                 for (int kk = 0; kk < kC / 16; ++kk)
-                    mma_f16_ts(tmem + kColS, tmem + kColVt + kk * 8, dKt + so + ((kk * 2048) >> 4), id_ds, 1u);
-                mma_commit(&ms->ds_done);
-                // Y p2 += Vn_c^T [Aqk_c; M_{c+1}]^T  (A = Vn16 from TMEM, K = 64 tokens)
+                    mma_f16_ss(tmem + kColX1 + buf, dAM + so + ((kk * 32) >> 4), dVn + ((kk * 1024) >> 4), id_kb,
+                               kk > 0 ? 1u : 0u);
+                mma_commit(&ms->x1_full[c & 1]);
+                if (!mbar_wait(&ms->vt_ready, c & 1, abort, &g_err_gdn_prefill)) break;
+                tc_fence_after();
 #pragma unroll
                 for (int kk = 0; kk < kC / 16; ++kk)
-                    mma_f16_ts(tmem + ycol, tmem + kColVn + kk * 8, dB2 + so + ((kk * 32) >> 4), id_y, 1u);
-                mma_commit(&ms->y_full[c & 1]);
+                    mma_f16_ss(tmem + kColDS + buf, dK + so + ((kk * 2048) >> 4), dVt + ((kk * 1024) >> 4), id_mn,
+                               kk > 0 ? 1u : 0u);
+                mma_commit(&ms->ds_full[c & 1]);
                 mma_commit(&ms->empty[s]);
             }
-            mma_commit(&ms->drain);
-            mbar_wait(&ms->drain, 0, &no_abort, &g_err_gdn_prefill);
+            mma_commit(&ms->drain_a);
+            mbar_wait(&ms->drain_a, 0, abort, &g_err_gdn_prefill);
         }
-    } else if (warp < kWarpVn) {
-        // ---- state warps: thread j = v column j = TMEM lane j ----
-        const int j = tid;
-        const uint32_t lb = static_cast<uint32_t>(warp * 32) << 16;
-        float* Srow = p.state + (bh * kD + j) * kD;  // S[j][0..127], 512 contiguous bytes
-        auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
-            return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, &g_err_gdn_prefill));
-        };
-        // the prologue stage is not read here: its arrivals are made at once
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&ms->empty[1]);
-        bool ok = true;
-        for (int c = 0; c < nch; ++c) {
-            const int s = c & 1;
-            if (!wait_all(&ms->full[s], ch_use(c) & 1)) { ok = false; break; }
-            const float gam = __expf(reinterpret_cast<const float*>(smem + s * kStage + kG)[kC - 1]);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&ms->empty[s]);
-            if (c > 0) {
-                if (!wait_all(&ms->ds_done, (c - 1) & 1)) { ok = false; break; }
-                tc_fence_after();
-            }
-            // S_c -> S16_c (A operand of Y p1) and gam_c S_c (the update accumulates onto it)
+    } else if (warp == kWarpMmaB) {
+        // state MMAs: RQ = [Q_c; W_{c+1}] S_c^T, one chunk ahead of the chain
+        if (lane == 0) {
+            constexpr uint32_t id_kb = make_idesc(kFmt, 128, kSlice, false, true);
+            const uint64_t dA1 = smem_desc(smem_u32(smem + kA1), 16, 1024, kLayoutSW128);
+            const uint64_t dS = smem_desc(smem_u32(smem + kSt), 8192, 512, kLayoutSW64);
+            auto rq = [&](uint32_t so, uint32_t buf) {
 #pragma unroll
-            for (int cc = 0; cc < kD / 32; ++cc) {
-                uint32_t r[32];
-                if (c == 0) {
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) {
-                        const float4 x = reinterpret_cast<const float4*>(Srow + cc * 32)[q];
-                        r[4 * q] = __float_as_uint(x.x);
-                        r[4 * q + 1] = __float_as_uint(x.y);
-                        r[4 * q + 2] = __float_as_uint(x.z);
-                        r[4 * q + 3] = __float_as_uint(x.w);
-                    }
-                } else {
-                    tmem_ld32(tmem + lb + kColS + cc * 32, r);
-                    tmem_ld_wait();
+                for (int kk = 0; kk < kD / 16; ++kk) {
+                    const uint32_t ao = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
+                    mma_f16_ss(tmem + kColRQ + buf, dA1 + so + ao, dS + ((kk * 1024) >> 4), id_kb,
+                               kk > 0 ? 1u : 0u);
                 }
-                uint32_t h16[16];
-#pragma unroll
-                for (int u = 0; u < 16; ++u)
-                    h16[u] = Elem<T16>::pack2(__uint_as_float(r[2 * u]), __uint_as_float(r[2 * u + 1]));
-                tmem_st16(tmem + lb + kColS16 + cc * 16, h16);
-#pragma unroll
-                for (int u = 0; u < 32; ++u) r[u] = __float_as_uint(__uint_as_float(r[u]) * gam);
-                tmem_st32(tmem + lb + kColS + cc * 32, r);
+            };
+            // prologue: R_0 = W_0 S_0^T (rows 64-127; rows 0-63 read stage 2's unused Q slot)
+            bool ok = mbar_wait(&ms->pro_full, 0, abort, &g_err_gdn_prefill) &&
+                      mbar_wait(&ms->s_ready[0], 0, abort, &g_err_gdn_prefill);
+            if (ok) {
+                tc_fence_after();
+                rq(((kStages - 1) * kStage) >> 4, 32);
+                mma_commit(&ms->rq_full[1]);
+                mma_commit(&ms->pro_done);
             }
-            tmem_st_wait();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&ms->s_ready);
-        }
-        if (ok && wait_all(&ms->ds_done, (nch - 1) & 1)) {
-            tc_fence_after();
-#pragma unroll
-            for (int cc = 0; cc < kD / 32; ++cc) {
-                uint32_t r[32];
-                tmem_ld32(tmem + lb + kColS + cc * 32, r);
-                tmem_ld_wait();
-#pragma unroll
-                for (int q = 0; q < 8; ++q)
-                    reinterpret_cast<float4*>(Srow + cc * 32)[q] =
-                        make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
-                                    __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
+            for (int c = 0; ok && c < nch; ++c) {
+                const int s = c % kStages;
+                if (!mbar_wait(&ms->full[s], (c / kStages) & 1, abort, &g_err_gdn_prefill)) break;
+                if (c > 0 && !mbar_wait(&ms->s_ready[c & 1], (c >> 1) & 1, abort, &g_err_gdn_prefill)) break;
+                if (c >= 2 && !mbar_wait(&ms->o_done[c & 1], ((c - 2) >> 1) & 1, abort, &g_err_gdn_prefill)) break;
+                tc_fence_after();
+                rq((s * kStage) >> 4, (c & 1) * 32);
+                mma_commit(&ms->rq_full[c & 1]);
+                mma_commit(&ms->empty[s]);
             }
+            mma_commit(&ms->drain_b);
+            mbar_wait(&ms->drain_b, 0, abort, &g_err_gdn_prefill);
         }
     } else {
-        // ---- Vn / output warps: thread j = v column j = TMEM lane j ----
-        const int j = tid - kWarpVn * 32;
-        const uint32_t lb = static_cast<uint32_t>((warp & 3) * 32) << 16;
+        // ---------------- compute warps: three roles, each on its own chain -------
+        const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+        const float* gcs_all = reinterpret_cast<const float*>(p.ws + p.ws_gcs);
+        const size_t bhc0 = bh * p.nch;
+        if (warp >= kWarpOut) grid_dependency_wait();  // gcs comes from the prep grid
         auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
             return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, &g_err_gdn_prefill));
         };
-        // offsets of column j of a 128B-swizzled 64-row tile, by row mod 8 (row t adds 128 t)
-        uint32_t uoff[8];
+        // 32 values -> one 64-byte row of an MN-major B tile (16-bit)
+        auto put_row = [&](uint8_t* tile, int r, const float* x) {
 #pragma unroll
-        for (int r = 0; r < 8; ++r)
-            uoff[r] = (uint32_t)((j >> 6) * 8192 + ((((j & 63) >> 3) ^ r) << 4) + (j & 7) * 2);
-        // Vn = U - y (y = the chain half of Y) and Vt = Vn * vdec into TMEM, then announced.
-        // vdec_t = e^{gcs_last - gcs_t} (/ |k_t| with the fused pre-processing), from the prep pass.
-        auto make_vn = [&](const uint8_t* stg, const uint32_t (&y)[64]) {
-            const float* vdec = reinterpret_cast<const float*>(stg + kG + 512);
-            uint32_t pv[32], pt[32];
-#pragma unroll
-            for (int t2 = 0; t2 < kC / 2; ++t2) {
-                const int t = 2 * t2;
-                const float u0 = Elem<T16>::to_f(*reinterpret_cast<const T16*>(stg + kU + uoff[t & 7] + t * 128));
-                const float u1 =
-                    Elem<T16>::to_f(*reinterpret_cast<const T16*>(stg + kU + uoff[(t + 1) & 7] + (t + 1) * 128));
-                const float v0 = u0 - __uint_as_float(y[t]);
-                const float v1 = u1 - __uint_as_float(y[t + 1]);
-                pv[t2] = Elem<T16>::pack2(v0, v1);
-                pt[t2] = Elem<T16>::pack2(v0 * vdec[t], v1 * vdec[t + 1]);
+            for (int q = 0; q < kSlice / 8; ++q) {
+                uint4 pk;
+                pk.x = Elem<T16>::pack2(x[8 * q + 0], x[8 * q + 1]);
+                pk.y = Elem<T16>::pack2(x[8 * q + 2], x[8 * q + 3]);
+                pk.z = Elem<T16>::pack2(x[8 * q + 4], x[8 * q + 5]);
+                pk.w = Elem<T16>::pack2(x[8 * q + 6], x[8 * q + 7]);
+                *reinterpret_cast<uint4*>(tile + sw64_chunk(r, q)) = pk;
             }
-            tmem_st32(tmem + lb + kColVn, pv);
-            tmem_st32(tmem + lb + kColVt, pt);
-            tmem_st_wait();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&ms->vn_ready);
         };
-        auto load_y = [&](uint32_t col, uint32_t (&y)[64]) {
-            tmem_ld32(tmem + lb + col, *reinterpret_cast<uint32_t(*)[32]>(&y[0]));
-            tmem_ld32(tmem + lb + col + 32, *reinterpret_cast<uint32_t(*)[32]>(&y[32]));
-            tmem_ld_wait();
-        };
-        bool ok = wait_all(&ms->full[1], 0) && wait_all(&ms->y_full[1], 0);
-        if (ok) {  // prologue: Vn_0 = U_0 - W_0 S_0^T
-            tc_fence_after();
-            uint32_t y[64];
-            load_y(kColY + 128 + 64, y);
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&ms->y_empty[1]);
-            make_vn(smem + kStage, y);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&ms->empty[1]);
-        }
-        TOut* obase = static_cast<TOut*>(p.o) + ((size_t)seq.start * p.Hv + h) * kD + j;
-        const size_t tstride = (size_t)p.Hv * kD;
-        for (int c = 0; ok && c < nch; ++c) {
-            const int s = c & 1;
-            const uint32_t ycol = kColY + (c & 1) * 128;
-            if (!wait_all(&ms->y_full[c & 1], ((c + 1) >> 1) & 1)) break;
-            if (!wait_all(&ms->full[s], ch_use(c) & 1)) break;  // U_{c+1} and the decays
-            tc_fence_after();
-            const uint8_t* stg = smem + s * kStage;
-            if (c + 1 < nch) {  // Vn_{c+1} = U_{c+1} - (Y_c columns 64-127)
-                uint32_t y[64];
-                load_y(ycol + 64, y);
-                make_vn(stg, y);
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&ms->empty[s]);
-            uint32_t o[64];
-            load_y(ycol, o);
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&ms->y_empty[c & 1]);
-            // o_c[t][j] = scale * Y_c[j][t] for the chunk's tokens of this sequence
-            const int nt = min(kC, seq.len - c * kC);
-            TOut* op = obase + (size_t)c * kC * tstride;
+        if (warp < kWarpOut) {
+            // ---- state: S_{c+1} = e^{gcs_last} S_c + K_c^T Vt_c, thread i = key i ----
+            const int i = tid;
+            float S[kSlice];
+            float* Sg = p.state + (bh * kD + c0) * kD + i;
 #pragma unroll
-            for (int t = 0; t < kC; ++t)
-                if (t < nt) op[(size_t)t * tstride] = Elem<TOut>::from_f(p.scale * __uint_as_float(o[t]));
+            for (int cc = 0; cc < kSlice; ++cc) S[cc] = Sg[(size_t)cc * kD];
+            grid_dependency_wait();  // (the state itself is an input, not a prep result)
+            uint8_t* sS = smem + kSt;
+            // S (16-bit) -> shared (B operand of the RQ product), then S_c is announced
+            auto publish_S = [&](int c) {
+                put_row(sS, i, S);
+                fence_proxy_async_smem();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ms->s_ready[c & 1]);
+            };
+            bool ok = true;
+            publish_S(0);
+            float glast_nx = gcs_all[bhc0 * kC + kC - 1];
+            for (int c = 0; c < nch; ++c) {
+                const float gam = __expf(glast_nx);
+                if (c + 1 < nch) glast_nx = gcs_all[(bhc0 + c + 1) * kC + kC - 1];
+                if (!wait_all(&ms->ds_full[c & 1], (c >> 1) & 1)) { ok = false; break; }
+                tc_fence_after();
+                uint32_t ds[32];
+                tmem_ld32(tmem + lane_base + kColDS + (c & 1) * 32, ds);
+                tmem_ld_wait();
+#pragma unroll
+                for (int cc = 0; cc < kSlice; ++cc) S[cc] = fmaf(gam, S[cc], __uint_as_float(ds[cc]));
+                if (c + 1 < nch) {
+                    // the S tile is rewritten only once the RQ product that reads S_c is done
+                    if (!wait_all(&ms->rq_full[c & 1], st::rq_parity(c))) { ok = false; break; }
+                    tc_fence_after();
+                    publish_S(c + 1);
+                }
+            }
+            if (ok) {
+#pragma unroll
+                for (int cc = 0; cc < kSlice; ++cc) Sg[(size_t)cc * kD] = S[cc];
+            }
+        } else if (warp < kWarpVn) {
+            // ---- outputs: o_c = scale (e^{gcs} Q_c S_c^T + Aqk_c Vn_c), token row ----
+            const int row = tid - kWarpOut * 32;  // 0..63 = TMEM lane
+            const float* rq_all = reinterpret_cast<const float*>(p.ws + p.ws_rq);
+            float gcs_nx = gcs_all[bhc0 * kC + row];
+            float rq_nx = kFused ? rq_all[bhc0 * kC + row] : 1.f;
+            for (int c = 0; c < nch; ++c) {
+                const float gcs_t = gcs_nx;
+                const float rq_t = rq_nx;  // 1/|q_t| (fused pre-processing)
+                if (c + 1 < nch) {
+                    gcs_nx = gcs_all[(bhc0 + c + 1) * kC + row];
+                    if constexpr (kFused) rq_nx = rq_all[(bhc0 + c + 1) * kC + row];
+                }
+                if (!wait_all(&ms->rq_full[c & 1], st::rq_parity(c))) break;
+                if (!wait_all(&ms->x1_full[c & 1], (c >> 1) & 1)) break;
+                tc_fence_after();
+                uint32_t pq[32], oi[32];
+                tmem_ld32(tmem + lane_base + kColRQ + (c & 1) * 32, pq);
+                tmem_ld32(tmem + lane_base + kColX1 + (c & 1) * 32, oi);
+                tmem_ld_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ms->o_done[c & 1]);
+                const int tt = c * kC + row;
+                if (tt < seq.len) {
+                    const float eg = __expf(gcs_t) * rq_t;
+                    float ov[kSlice];
+#pragma unroll
+                    for (int cc = 0; cc < kSlice; ++cc)
+                        ov[cc] = p.scale * fmaf(eg, __uint_as_float(pq[cc]), __uint_as_float(oi[cc]));
+                    store_row32(static_cast<TOut*>(p.o) + (((size_t)seq.start + tt) * p.Hv + h) * kD + c0, ov);
+                }
+            }
+        } else {
+            // ---- Vn_c = U_c - e^{gcs_last,c-1} R_c - M_c Vn_{c-1}   (c = 0: U_0 - W_0 S_0^T)
+            const int row = tid - kWarpVn * 32;  // token; TMEM lane 64 + row
+            uint8_t* sVn = smem + kVn;
+            uint8_t* sVt = smem + kVt;
+            const float* rk_all = reinterpret_cast<const float*>(p.ws + p.ws_rk);
+            float rk_nx = kFused ? rk_all[bhc0 * kC + row] : 1.f;
+            float gam_prev = 1.f;
+            for (int c = 0; c < nch; ++c) {
+                const float rk_t = rk_nx;  // 1/|k_t|: K^T diag(1/|k|) Vt is the normalised keys' product
+                if (kFused && c + 1 < nch) rk_nx = rk_all[(bhc0 + c + 1) * kC + row];
+                const int s = c % kStages;
+                // chunk c's U row and gates from its stage (released only after vt_ready(c))
+                if (!wait_all(&ms->full[s], (c / kStages) & 1)) break;
+                const uint8_t* stg = smem + s * kStage;
+                const float gcs_t = reinterpret_cast<const float*>(stg + kG)[row];
+                const float g_last = reinterpret_cast<const float*>(stg + kG)[kC - 1];
+                float u[kSlice];
+#pragma unroll
+                for (int q8 = 0; q8 < kSlice / 8; ++q8) {
+                    const uint4 raw = *reinterpret_cast<const uint4*>(stg + kU + sw64_chunk(row, q8));
+                    const T16* e = reinterpret_cast<const T16*>(&raw);
+#pragma unroll
+                    for (int u8 = 0; u8 < 8; ++u8) u[q8 * 8 + u8] = Elem<T16>::to_f(e[u8]);
+                }
+                if (!wait_all(&ms->rq_full[(c - 1) & 1], st::rq_parity(c - 1))) break;
+                if (c > 0 && !wait_all(&ms->x1_full[(c - 1) & 1], ((c - 1) >> 1) & 1)) break;
+                tc_fence_after();
+                uint32_t rr[32], xx[32];
+                tmem_ld32(tmem + lane_base + kColRQ + ((c - 1) & 1) * 32, rr);
+                if (c > 0) tmem_ld32(tmem + lane_base + kColX1 + ((c - 1) & 1) * 32, xx);
+                tmem_ld_wait();
+                const float dec = __expf(g_last - gcs_t) * rk_t;
+                float vt[kSlice];
+#pragma unroll
+                for (int cc = 0; cc < kSlice; ++cc) {
+                    float vn = fmaf(-gam_prev, __uint_as_float(rr[cc]), u[cc]);
+                    if (c > 0) vn -= __uint_as_float(xx[cc]);
+                    u[cc] = vn;
+                    vt[cc] = vn * dec;
+                }
+                // Vn_c first (its tile was read by X1(c-1), whose result is in hand), so the
+                // chain product X1(c) can start; then decayed Vn_c, once K^T Vt of chunk c-1
+                // has read the Vt tile
+                put_row(sVn, row, u);
+                fence_proxy_async_smem();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ms->vn_ready);
+                if (c > 0 && !wait_all(&ms->ds_full[(c - 1) & 1], ((c - 1) >> 1) & 1)) break;
+                put_row(sVt, row, vt);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ms->vt_ready);
+                gam_prev = __expf(g_last);
+            }
         }
     }
 
     tc_fence_before();
     __syncthreads();
-    if (warp == kWarpMma) {
+    if (warp == kWarpMmaA) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }
@@ -1128,10 +1125,11 @@ int launch(const void* q, const void* k, const void* v, const float* g_log, cons
     uint8_t* wsb = static_cast<uint8_t*>(ws);
     if ((rc = make_tmap_3d(&tw, wsb + L.w, dt, 2, kD, kC, nbhc, 64, kC, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
     if ((rc = make_tmap_3d(&ta, wsb + L.aqk, dt, 2, kC, kC, nbhc, 64, kC, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
-    CUtensorMap tu, tm, tqt;
+    CUtensorMap tu, tus, tm;
     if ((rc = make_tmap_3d(&tm, wsb + L.m, dt, 2, kC, kC, nbhc, 64, kC, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
     if ((rc = make_tmap_3d(&tu, wsb + L.u, dt, 2, kD, kC, nbhc, 64, kC, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
-    if ((rc = make_tmap_3d(&tqt, wsb + L.qt, dt, 2, kD, kC, nbhc, 64, kC, CU_TENSOR_MAP_SWIZZLE_128B))) return rc;
+    if ((rc = make_tmap_3d(&tus, wsb + L.u, dt, 2, kD, kC, nbhc, kSlice, kC, CU_TENSOR_MAP_SWIZZLE_64B)))
+        return rc;
 
     PrepParams pp;
     pp.ws = wsb;
@@ -1140,7 +1138,8 @@ int launch(const void* q, const void* k, const void* v, const float* g_log, cons
     pp.ws_u = L.u;
     pp.ws_aqk = L.aqk;
     pp.ws_gcs = L.gcs;
-    pp.ws_vdec = L.vdec;
+    pp.ws_rq = L.rq;
+    pp.ws_rk = L.rk;
     pp.A_log = fuse.A_log;
     pp.dt_bias = fuse.dt_bias;
     pp.cu = cu;
@@ -1152,38 +1151,39 @@ int launch(const void* q, const void* k, const void* v, const float* g_log, cons
     pp.head_map = head_map;
     auto k1 = fuse.on ? gdn_prep_kernel<T16, true> : gdn_prep_kernel<T16, false>;
     B200_TRY_CUDA(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, prep::kAlloc));
-    k1<<<dim3(nch, Hv, B), prep::kThreads, prep::kAlloc, stream>>>(tq, tk, tv, tw, tu, ta, tm, tqt, pp);
+    k1<<<dim3(nch, Hv, B), prep::kThreads, prep::kAlloc, stream>>>(tq, tk, tv, tw, tu, ta, tm, pp);
     B200_TRY_CUDA(cudaGetLastError());
 
-    ChainParams cp;
-    cp.ws = wsb;
-    cp.state = state;
-    cp.o = o;
-    cp.ws_gcs = L.gcs;
-    cp.ws_vdec = L.vdec;
-    cp.cu = cu;
-    cp.ntok = ntok;
-    cp.T = T;
-    cp.Hqk = Hqk;
-    cp.Hv = Hv;
-    cp.nch = nch;
-    cp.head_map = head_map;
-    cp.scale = scale;
-    auto k2 = gdn_chain_kernel<T16, TOut>;
-    B200_TRY_CUDA(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, ch::kAlloc));
-    // launched with programmatic stream serialisation: its prologue (barriers, TMEM) overlaps
-    // the prep grid's last CTAs; its producer waits for the prep grid's results
+    StateParams sp;
+    sp.ws = wsb;
+    sp.state = state;
+    sp.o = o;
+    sp.ws_gcs = L.gcs;
+    sp.ws_rq = L.rq;
+    sp.ws_rk = L.rk;
+    sp.cu = cu;
+    sp.ntok = ntok;
+    sp.T = T;
+    sp.Hqk = Hqk;
+    sp.Hv = Hv;
+    sp.nch = nch;
+    sp.head_map = head_map;
+    sp.scale = scale;
+    auto k2 = fuse.on ? gdn_state_kernel<T16, TOut, true> : gdn_state_kernel<T16, TOut, false>;
+    B200_TRY_CUDA(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, st::kAlloc));
+    // launched with programmatic stream serialisation: its prologue (barriers, TMEM, the
+    // initial state) overlaps the prep grid's last CTAs
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(Hv, B);
-    cfg.blockDim = dim3(ch::kThreads);
-    cfg.dynamicSmemBytes = ch::kAlloc;
+    cfg.gridDim = dim3(kD / kSlice, Hv, B);
+    cfg.blockDim = dim3(st::kThreads);
+    cfg.dynamicSmemBytes = st::kAlloc;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    B200_TRY_CUDA(cudaLaunchKernelEx(&cfg, k2, tk, tqt, tw, ta, tm, tu, cp));
+    B200_TRY_CUDA(cudaLaunchKernelEx(&cfg, k2, tq, tk, tw, ta, tm, tus, sp));
     count_launch(2);
     return cudaGetLastError() == cudaSuccess ? B200LAB_OK : B200LAB_ERR_CUDA;
 }
