@@ -135,13 +135,20 @@ int attn_gated_fwd_sm100(const void* Q, const void* K, const void* V, const void
  *   o     : [B][T][Hv][dv]  out_dtype (F16, BF16 or F32)
  *   head_map: 0 -> v-head h reads q/k head h % Hqk (the reference,
  *             src/gdn_sm75.cu:1083); 1 -> h / (Hv/Hqk).
- *   dk = dv = 128.  workspace: gdn_prefill_sm100_workspace() bytes. */
+ *   dk = dv = 128.  workspace: gdn_prefill_sm100_workspace_ex(..., in_dtype)
+ *   bytes (gdn_prefill_sm100_workspace() for 16-bit inputs).  fp32 q, k, v
+ *   (the reference kernels' const float*) are converted once to bf16 copies in
+ *   the workspace; the tensor-core operands are 16-bit for every in_dtype. */
 int gdn_prefill_sm100(const void* q, const void* k, const void* v,
                       const float* g_log, const float* beta, float* state, void* o,
                       int B, int T, int Hqk, int Hv, int dk, int dv, int head_map,
                       float scale, int in_dtype, int out_dtype,
                       void* workspace, size_t ws_bytes, void* stream);
 size_t gdn_prefill_sm100_workspace(int B, int T, int Hqk, int Hv, int dk, int dv);
+/* Workspace for a given in_dtype: the 16-bit size plus, for B200LAB_F32, the
+ * bf16 copies of q, k, v (B*T*(2*Hqk + Hv)*dk*2 bytes, rounded up).  Packed
+ * sequences (the varlen entries) use B and max_seqlen, as for the 16-bit size. */
+size_t gdn_prefill_sm100_workspace_ex(int B, int T, int Hqk, int Hv, int dk, int dv, int in_dtype);
 
 /* Packed variable-length sequences (no counterpart in the reference, whose
  * prefill runs one sequence, src/gdn_sm75.cu:1246-1412): q, k [total][Hqk][dk],
@@ -171,7 +178,7 @@ int gdn_prefill_sm100_varlen(const void* q, const void* k, const void* v,
  * Same arguments and results as gdn_prefill_sm100, minus the workspace: the
  * scratch is a file-scope device array of B200LAB_NOALLOC_SCRATCH_BYTES
  * (64 MiB) that every GPU loading the prefill kernels holds until the process
- * exits.  A problem whose gdn_prefill_sm100_workspace() exceeds that size is
+ * exits.  A problem whose gdn_prefill_sm100_workspace_ex() exceeds that size is
  * rejected with B200LAB_ERR_WORKSPACE before anything is launched (about
  * 50 KB per (sequence, v-head, 64-token chunk): B*Hv*ceil(T/64) <= 1344,
  * e.g. Hv=48 up to T=1792, Hv=32 up to T=2688).

@@ -109,13 +109,25 @@ def test_oracle_and_kernel_vs_reference_naive(cuda, B, H, S, D):
 
 
 @pytest.mark.parametrize("B,Hq,Hkv,Sq,Skv,D", [(1, 8, 2, 1, 4096, 128), (2, 4, 4, 64, 3000, 64),
-                                               (1, 4, 1, 300, 5000, 128), (1, 2, 2, 17, 1025, 128)])
+                                               (1, 4, 1, 300, 5000, 128), (1, 2, 2, 17, 1025, 128),
+                                               # GQA-packed rows: 256 rows = one tile pair,
+                                               # 300 rows over two CTAs, group 8
+                                               (1, 32, 8, 64, 2048, 128), (2, 6, 2, 100, 1500, 64),
+                                               (1, 8, 1, 33, 777, 128)])
 @pytest.mark.parametrize("causal", [False, True])
 def test_split_kv_short_queries(cuda, B, Hq, Hkv, Sq, Skv, D, causal):
     """Short queries over long keys take the split-KV path (partials + combine)."""
     assert b200lab.lib().attn_fwd_sm100_workspace(B, Hq, Hkv, Sq, Skv, D, int(causal)) > 0
     O, ref = _run(B, Hq, Hkv, Sq, Skv, D, causal, torch.bfloat16, seed=Sq * 7 + Skv)
     assert_close(O, ref, f"split-KV Sq{Sq} Skv{Skv}")
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_gqa_packed_rows_without_split(cuda, causal):
+    """Short GQA queries on a grid large enough not to split: the q-heads of each kv group
+    share one tile pair (rows r -> query r % Sq), causal mask per query index."""
+    O, ref = _run(16, 32, 8, 40, 300, 128, causal, torch.bfloat16, seed=5)
+    assert_close(O, ref, "packed unsplit")
 
 
 def test_split_kv_without_workspace_runs_unsplit(cuda):

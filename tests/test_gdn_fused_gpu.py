@@ -68,6 +68,24 @@ def test_prefill_fused(cuda, T, with_params):
     assert_close(to_np(S), S_ref, f"state T{T}")
 
 
+def test_prefill_fused_fp32_inputs(cuda):
+    """Raw fp32 q, k, v through the fused entry: converted once to bf16, then normalised."""
+    dev = torch.device("cuda:0")
+    B, T, Hqk, Hv = 2, 150, 2, 4
+    q, k, v, a, b, A_log, dt_bias = _raw_inputs(B, T, Hqk, Hv, seed=9, dtype=torch.float32)
+    S0 = workloads.gdn_state(B, Hv, 128, std=0.05, seed=9)
+    S = S0.clone().to(dev)
+    scale = 1.0 / np.sqrt(128)
+    o = b200lab.gdn_prefill_fused(q.to(dev), k.to(dev), v.to(dev), a.to(dev), b.to(dev), S,
+                                  A_log=A_log.to(dev), dt_bias=dt_bias.to(dev), scale=scale,
+                                  out_dtype=torch.float32)
+    assert b200lab.device_status() == b200lab.OK
+    qn, kn, gl, be = _pre(to_np(q), to_np(k), to_np(a), to_np(b), to_np(A_log), to_np(dt_bias))
+    o_ref, S_ref = oracle.gdn_recurrent(qn, kn, to_np(v), gl, be, S0.double().numpy(), scale)
+    assert_close(to_np(o), o_ref, "fp32-in fused out")
+    assert_close(to_np(S), S_ref, "fp32-in fused state")
+
+
 def test_prefill_fused_c3_shape(cuda):
     dev = torch.device("cuda:0")
     c = workloads.CONFIGS["gdn_prefill_c3"]

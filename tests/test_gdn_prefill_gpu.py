@@ -45,6 +45,38 @@ def test_dtypes(cuda, dtype, out_dtype):
     assert_close(S, S_ref, "state")
 
 
+@pytest.mark.parametrize("T", [17, 64, 200])
+@pytest.mark.parametrize("head_map", [0, 1])
+def test_fp32_inputs_ragged(cuda, T, head_map):
+    """fp32 q, k, v (the reference kernels' const float*): converted once to bf16 in the
+    workspace; the oracle runs on the unrounded fp32 values."""
+    o, S, o_ref, S_ref = _case(2, T, 2, 4, dtype=torch.float32, out_dtype=torch.float32,
+                               head_map=head_map, state_std=0.05, seed=40 + T)
+    assert_close(o, o_ref, f"fp32-in out T{T}")
+    assert_close(S, S_ref, f"fp32-in state T{T}")
+
+
+def test_fp32_inputs_c3_config(cuda):
+    c = workloads.CONFIGS["gdn_prefill_c3"]
+    o, S, o_ref, S_ref = _case(c["B"], c["T"], c["Hqk"], c["Hv"], dtype=torch.float32,
+                               out_dtype=torch.bfloat16, seed=8)
+    assert_close(o, o_ref, "C3 fp32-in out")
+    assert_close(S, S_ref, "C3 fp32-in state")
+
+
+def test_fp32_workspace_query(cuda):
+    """The fp32 workspace adds the bf16 copies of q, k, v; too small a workspace is refused."""
+    B, T, Hqk, Hv = 1, 130, 2, 4
+    base = b200lab.gdn_prefill_workspace_bytes(B, T, Hqk, Hv, in_dtype=b200lab.BF16)
+    f32 = b200lab.gdn_prefill_workspace_bytes(B, T, Hqk, Hv, in_dtype=b200lab.F32)
+    assert f32 >= base + B * T * (2 * Hqk + Hv) * 128 * 2
+    dev = torch.device("cuda:0")
+    q, k, v, g, b = (t.to(dev) for t in workloads.gdn_inputs(B, T, Hqk, Hv, 128, torch.float32, seed=3))
+    S = torch.zeros((B, Hv, 128, 128), device=dev)
+    with pytest.raises(b200lab.B200LabError):
+        b200lab.gdn_prefill(q, k, v, g, b, S, workspace=torch.empty(base, dtype=torch.uint8, device=dev))
+
+
 def test_c3_config(cuda):
     """B=1, T=4096, 16 q/k heads, 32 v heads, d=128, zero initial state."""
     c = workloads.CONFIGS["gdn_prefill_c3"]
@@ -98,6 +130,7 @@ def test_workspace_and_dtype_rules(cuda):
     st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     assert L.gdn_prefill_sm100(*args, 1, 1, p(ws), need - 1, st) == b200lab.ERR_WORKSPACE
     assert L.gdn_prefill_sm100(*args, 1, 1, ctypes.c_void_p(0), need, st) == b200lab.ERR_WORKSPACE
-    assert L.gdn_prefill_sm100(*args, 2, 1, p(ws), need, st) == b200lab.ERR_UNSUPPORTED  # fp32 in
+    # fp32 inputs need the larger workspace (their bf16 copies): the 16-bit size is refused
+    assert L.gdn_prefill_sm100(*args, 2, 1, p(ws), need, st) == b200lab.ERR_WORKSPACE
     assert L.gdn_prefill_sm100(*args, 1, 1, p(ws), need, st) == b200lab.OK
     assert b200lab.device_status() == b200lab.OK

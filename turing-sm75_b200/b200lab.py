@@ -34,7 +34,8 @@ F16, BF16, F32 = 0, 1, 2
 EXPORTED = (
     "attn_fwd_sm100", "attn_fwd_sm100_workspace", "attn_gated_fwd_sm100", "attn_fwd_sm100_varlen",
     "attn_fwd_sm100_host",
-    "gdn_prefill_sm100", "gdn_prefill_sm100_workspace", "gdn_prefill_sm100_noalloc",
+    "gdn_prefill_sm100", "gdn_prefill_sm100_workspace", "gdn_prefill_sm100_workspace_ex",
+    "gdn_prefill_sm100_noalloc",
     "gdn_prefill_sm100_fused", "gdn_prefill_sm100_varlen", "gdn_prefill_sm100_fused_varlen",
     "gdn_decode_sm100", "gdn_decode_sm100_state16", "gdn_decode_sm100_fused",
     "gdn_decode_sm100_slots",
@@ -81,6 +82,8 @@ def lib() -> ctypes.CDLL:
         L.gdn_prefill_sm100.argtypes = [vp] * 7 + [ci] * 7 + [cf, ci, ci, vp, sz, vp]
         L.gdn_prefill_sm100_workspace.restype = sz
         L.gdn_prefill_sm100_workspace.argtypes = [ci] * 6
+        L.gdn_prefill_sm100_workspace_ex.restype = sz
+        L.gdn_prefill_sm100_workspace_ex.argtypes = [ci] * 7
         L.gdn_prefill_sm100_noalloc.restype = ci
         L.gdn_prefill_sm100_noalloc.argtypes = [vp] * 7 + [ci] * 7 + [cf, ci, ci, vp]
         L.gdn_decode_sm100.restype = ci
@@ -251,8 +254,9 @@ def attn_fwd_varlen(Q, K, V, cu_seqlens_q, cu_seqlens_k, max_seqlen_q: int, *, s
     return out
 
 
-def gdn_prefill_workspace_bytes(B, T, Hqk, Hv, dk=128, dv=128) -> int:
-    return int(lib().gdn_prefill_sm100_workspace(B, T, Hqk, Hv, dk, dv))
+def gdn_prefill_workspace_bytes(B, T, Hqk, Hv, dk=128, dv=128, in_dtype=BF16) -> int:
+    """Workspace bytes of the prefill entries for inputs of type in_dtype (F16 / BF16 / F32)."""
+    return int(lib().gdn_prefill_sm100_workspace_ex(B, T, Hqk, Hv, dk, dv, int(in_dtype)))
 
 
 def gdn_prefill(q, k, v, g_log, beta, state, *, scale: float | None = None, head_map: int = 0,
@@ -266,7 +270,7 @@ def gdn_prefill(q, k, v, g_log, beta, state, *, scale: float | None = None, head
         scale = 1.0 / (dk ** 0.5)
     if out is None:
         out = torch.empty((B, T, Hv, dv), dtype=out_dtype or q.dtype, device=q.device)
-    need = gdn_prefill_workspace_bytes(B, T, Hqk, Hv, dk, dv)
+    need = gdn_prefill_workspace_bytes(B, T, Hqk, Hv, dk, dv, _dtype_code(q))
     ws_ptr, ws_bytes = ctypes.c_void_p(0), 0
     if need:
         if workspace is None:
@@ -296,7 +300,7 @@ def gdn_prefill_varlen(q, k, v, g_log, beta, state, cu_seqlens, max_seqlen: int,
         scale = 1.0 / (dk ** 0.5)
     if out is None:
         out = torch.empty((total, Hv, dv), dtype=out_dtype or q.dtype, device=q.device)
-    need = gdn_prefill_workspace_bytes(B, max_seqlen, Hqk, Hv, dk, dv)
+    need = gdn_prefill_workspace_bytes(B, max_seqlen, Hqk, Hv, dk, dv, _dtype_code(q))
     if workspace is None:
         workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=q.device)
     st = lib().gdn_prefill_sm100_varlen(_dev(q, "q"), _dev(k, "k"), _dev(v, "v"), _dev(g_log, "g_log"),
@@ -324,7 +328,7 @@ def gdn_prefill_fused_varlen(q, k, v, a, b, state, cu_seqlens, max_seqlen: int, 
         scale = 1.0 / (dk ** 0.5)
     if out is None:
         out = torch.empty((total, Hv, dv), dtype=out_dtype or q.dtype, device=q.device)
-    need = gdn_prefill_workspace_bytes(B, max_seqlen, Hqk, Hv, dk, dv)
+    need = gdn_prefill_workspace_bytes(B, max_seqlen, Hqk, Hv, dk, dv, _dtype_code(q))
     if workspace is None:
         workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=q.device)
     opt = lambda t, n: _dev(t, n) if t is not None else ctypes.c_void_p(0)  # noqa: E731
@@ -350,7 +354,7 @@ def gdn_prefill_fused(q, k, v, a, b, state, *, A_log=None, dt_bias=None, scale: 
         scale = 1.0 / (dk ** 0.5)
     if out is None:
         out = torch.empty((B, T, Hv, dv), dtype=out_dtype or q.dtype, device=q.device)
-    need = gdn_prefill_workspace_bytes(B, T, Hqk, Hv, dk, dv)
+    need = gdn_prefill_workspace_bytes(B, T, Hqk, Hv, dk, dv, _dtype_code(q))
     ws_ptr, ws_bytes = ctypes.c_void_p(0), 0
     if need:
         if workspace is None:

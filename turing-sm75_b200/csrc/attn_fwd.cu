@@ -96,6 +96,7 @@ struct Params {
     int Hq, Sq, Skv, group, n_ctas, causal;
     int nsplit, tiles_per_split;
     int total_q, total_k, max_sq;  // varlen: the buffers' token counts and the grid's sizing
+    int pack_sq;  // > 0: GQA-packed rows (row r is query r % pack_sq); 0: row = query
     float scale_log2;
 };
 
@@ -179,14 +180,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     const int cta = p.causal ? (n_ctas - 1 - cta_lin) : cta_lin;
     const int q0 = cta * (kQTiles * BM);
-    const int off = Skv - Sq;
+    // the causal mask: row r is query r (or r % pack_sq when a GQA group's q-heads are packed
+    // into the rows), aligned at the bottom right of the key range
+    const int sq_mask = p.pack_sq ? p.pack_sq : Sq;
+    const int off = Skv - sq_mask;
 
     // key tiles this CTA needs: enough for its last valid query row, then the
     // part [j0, j0 + nkv) of them that belongs to this CTA's key split
     const int nkv_all = (Skv + BN - 1) / BN;
     int nkv_need = nkv_all;
     if (p.causal) {
-        const long long last_row = min(q0 + kQTiles * BM, Sq) - 1;
+        const long long last_row = p.pack_sq ? p.pack_sq - 1 : min(q0 + kQTiles * BM, Sq) - 1;
         const long long lim = last_row + off;  // last visible key of that row
         nkv_need = lim < 0 ? 0 : min(nkv_all, (int)(lim / BN) + 1);
     }
@@ -348,7 +352,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t tS = tmem + lane_base + t * BN;
         const uint32_t tO = tmem + lane_base + L::kTmemO + t * D;
         const int qrow = q0 + t * BM + r;
-        const int key_lim = p.causal ? min(Skv - 1, qrow + off) : (Skv - 1);
+        const int key_lim = p.causal ? min(Skv - 1, (p.pack_sq ? qrow % p.pack_sq : qrow) + off) : (Skv - 1);
         const float sl2 = p.scale_log2;
         float m = -INFINITY;  // running max of scaled scores, log2 units
         float l = 0.f;
@@ -626,6 +630,20 @@ SplitPlan plan_splits(int B, int Hq, int Sq, int Skv) {
     return sp;
 }
 
+// Short queries of a GQA group are packed into the rows of one query tile pair: the q-heads
+// of a kv group are adjacent, so [B][Hq][Sq][D] is [B*Hkv][group*Sq][D], and row r of kv-head
+// h is query r % Sq of q-head h*group + r / Sq.  The kernel then runs with Hkv "heads" of
+// group*Sq rows: K/V are read once per group, the 128-row tiles are filled, and the causal
+// mask takes the query index r % Sq.  Partial and output rows keep their addresses.
+struct RowShape {
+    int Hq, Sq, pack_sq;
+};
+RowShape row_shape(int Hq, int Hkv, int Sq) {
+    const int group = Hq / Hkv;
+    if (group > 1 && Sq < kQTiles * BM) return RowShape{Hkv, group * Sq, Sq};
+    return RowShape{Hq, Sq, 0};
+}
+
 size_t split_workspace_bytes(int B, int Hq, int Sq, int Skv, int D) {
     const SplitPlan sp = plan_splits(B, Hq, Sq, Skv);
     if (sp.nsplit <= 1) return 0;
@@ -639,6 +657,10 @@ int launch(const void* Q, const void* K, const void* V, void* O, int B, int Hq, 
     using L = Layout<D>;
     const CUtensorMapDataType dt = Elem<T>::kFmt == 0 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                       : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    const int group = Hq / Hkv;
+    const RowShape rs = row_shape(Hq, Hkv, Sq);
+    Hq = rs.Hq;
+    Sq = rs.Sq;
     CUtensorMap tq, tk, tv;
     int rc = make_tmap_3d(&tq, Q, dt, 2, D, Sq, (uint64_t)B * Hq, 64, BM, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
@@ -651,7 +673,8 @@ int launch(const void* Q, const void* K, const void* V, void* O, int B, int Hq, 
     p.Hq = Hq;
     p.Sq = Sq;
     p.Skv = Skv;
-    p.group = Hq / Hkv;
+    p.group = rs.pack_sq ? 1 : group;
+    p.pack_sq = rs.pack_sq;
     p.n_ctas = (Sq + kQTiles * BM - 1) / (kQTiles * BM);
     p.causal = causal;
     p.scale_log2 = scale * 1.4426950408889634f;
@@ -697,10 +720,10 @@ int attn_d256_launch(const void* Q, const void* K, const void* V, const void* G,
 
 extern "C" size_t attn_fwd_sm100_workspace(int B, int Hq, int Hkv, int Sq, int Skv, int D,
                                            int causal) {
-    (void)Hkv;
     (void)causal;
-    if (B < 1 || Hq < 1 || Sq < 1 || Skv < 1 || (D != 64 && D != 128)) return 0;
-    return b200::split_workspace_bytes(B, Hq, Sq, Skv, D);
+    if (B < 1 || Hq < 1 || Hkv < 1 || Hq % Hkv || Sq < 1 || Skv < 1 || (D != 64 && D != 128)) return 0;
+    const b200::RowShape rs = b200::row_shape(Hq, Hkv, Sq);
+    return b200::split_workspace_bytes(B, rs.Hq, rs.Sq, Skv, D);
 }
 
 extern "C" int attn_fwd_sm100(const void* Q, const void* K, const void* V, void* O, int B, int Hq,

@@ -31,6 +31,8 @@
 //   and the state update S_{c+1} = e^{gcs_last} S_c + K_c^T diag(..) Vn_c run beside it
 //   on their own warps and MMA thread.
 // Every wait is bounded (common.cuh).
+#include <algorithm>
+
 #include "common.cuh"
 #include "errwords.h"
 
@@ -658,7 +660,9 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
     if (tid == 0 && ok) {
         tma_store_3d(&tmM, smem + kAT, 0, 0, (int)bhc);
         bulk_commit();
-        bulk_wait_all();   // the next kernel reads W, U, Aqk, M
+        // shared memory must outlive only the stores' reads of it: their writes are complete
+        // when the grid is, which the state pass waits for (griddepcontrol.wait)
+        bulk_wait_read();
     }
     if (tid == 0) {
         mma_commit(&ms->drain);
@@ -1188,6 +1192,35 @@ int launch(const void* q, const void* k, const void* v, const float* g_log, cons
     return cudaGetLastError() == cudaSuccess ? B200LAB_OK : B200LAB_ERR_CUDA;
 }
 
+// fp32 q / k / v: one pass converts them to bf16 copies in the workspace, which the chunked
+// kernels then read like 16-bit inputs (the tensor-core operands are 16-bit either way).
+// blockIdx.y picks the tensor; 8 elements a thread per step (two 16-byte loads, one store).
+struct F32Copies {
+    const float* src[3];
+    __nv_bfloat16* dst[3];
+    size_t n8[3];  // elements / 8
+};
+__global__ void __launch_bounds__(256) f32_to_bf16_kernel(const F32Copies a) {
+    const int t = blockIdx.y;
+    const float4* src = reinterpret_cast<const float4*>(a.src[t]);
+    uint4* dst = reinterpret_cast<uint4*>(a.dst[t]);
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < a.n8[t];
+         i += (size_t)gridDim.x * blockDim.x) {
+        const float4 x = src[2 * i], y = src[2 * i + 1];
+        uint4 o;
+        o.x = Elem<__nv_bfloat16>::pack2(x.x, x.y);
+        o.y = Elem<__nv_bfloat16>::pack2(x.z, x.w);
+        o.z = Elem<__nv_bfloat16>::pack2(y.x, y.y);
+        o.w = Elem<__nv_bfloat16>::pack2(y.z, y.w);
+        dst[i] = o;
+    }
+}
+
+// bytes of the bf16 copies of fp32 q, k, v for ntok tokens (each 1 KiB-aligned)
+size_t f32_copy_bytes(size_t ntok, int Hqk, int Hv) {
+    return 2 * align_up(ntok * Hqk * kD * 2, 1024) + align_up(ntok * Hv * kD * 2, 1024);
+}
+
 template <typename T16>
 int dispatch_out(int out_dtype, const void* q, const void* k, const void* v, const float* g,
                  const float* be, float* state, void* o, int B, int T, int Hqk, int Hv, int hm,
@@ -1220,6 +1253,12 @@ extern "C" size_t gdn_prefill_sm100_workspace(int B, int T, int Hqk, int Hv, int
     return b200::ws_layout((size_t)B * Hv * nch).total;
 }
 
+extern "C" size_t gdn_prefill_sm100_workspace_ex(int B, int T, int Hqk, int Hv, int dk, int dv, int in_dtype) {
+    const size_t base = gdn_prefill_sm100_workspace(B, T, Hqk, Hv, dk, dv);
+    if (base == 0 || in_dtype != B200LAB_F32 || Hqk < 1) return base;
+    return base + b200::f32_copy_bytes((size_t)B * T, Hqk, Hv);
+}
+
 namespace b200 {
 namespace {
 // cu / ntok: packed sequences (T = the longest), or null / unused for dense B x T
@@ -1236,18 +1275,40 @@ int prefill_entry(const void* q, const void* k, const void* v, const float* g_lo
     if (in_dtype < B200LAB_F16 || in_dtype > B200LAB_F32) return B200LAB_ERR_INVALID;
     if (out_dtype < B200LAB_F16 || out_dtype > B200LAB_F32) return B200LAB_ERR_INVALID;
     if (dk != 128 || dv != 128) return B200LAB_ERR_UNSUPPORTED;
-    if (in_dtype == B200LAB_F32) return B200LAB_ERR_UNSUPPORTED;  // 16-bit operands only
     if (B > 65535 || Hv > 65535) return B200LAB_ERR_UNSUPPORTED;
     if (T == 0) return B200LAB_OK;
     if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(state, 16) ||
         !aligned(o, 16))
         return B200LAB_ERR_INVALID;
-    const size_t need = gdn_prefill_sm100_workspace(B, T, Hqk, Hv, dk, dv);
+    // fp32 inputs: the bf16 copies are sized by B * max_seqlen tokens, which bounds total_tokens
+    if (in_dtype == B200LAB_F32 && cu && (long long)ntok > (long long)B * T) return B200LAB_ERR_INVALID;
+    const size_t need = gdn_prefill_sm100_workspace_ex(B, T, Hqk, Hv, dk, dv, in_dtype);
     if (!workspace || ws_bytes < need || !aligned(workspace, 256)) return B200LAB_ERR_WORKSPACE;
     int rc = check_device_sm100();
     if (rc != B200LAB_OK) return rc;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (!cu) ntok = B * T;
+    if (in_dtype == B200LAB_F32) {
+        // bf16 copies after the chunk items, then the 16-bit path on them
+        uint8_t* conv = static_cast<uint8_t*>(workspace) + gdn_prefill_sm100_workspace(B, T, Hqk, Hv, dk, dv);
+        const size_t nqk = (size_t)ntok * Hqk * kD, nv = (size_t)ntok * Hv * kD;
+        F32Copies cp;
+        cp.src[0] = static_cast<const float*>(q);
+        cp.src[1] = static_cast<const float*>(k);
+        cp.src[2] = static_cast<const float*>(v);
+        cp.dst[0] = reinterpret_cast<__nv_bfloat16*>(conv);
+        cp.dst[1] = reinterpret_cast<__nv_bfloat16*>(conv + align_up(nqk * 2, 1024));
+        cp.dst[2] = reinterpret_cast<__nv_bfloat16*>(conv + 2 * align_up(nqk * 2, 1024));
+        cp.n8[0] = cp.n8[1] = nqk / 8;
+        cp.n8[2] = nv / 8;
+        const size_t most = nqk > nv ? nqk : nv;
+        const unsigned gx = (unsigned)std::min<size_t>((most / 8 + 255) / 256, 148 * 16);
+        f32_to_bf16_kernel<<<dim3(gx, 3), 256, 0, s>>>(cp);
+        B200_TRY_CUDA(cudaGetLastError());
+        count_launch(1);
+        return dispatch_out<__nv_bfloat16>(out_dtype, cp.dst[0], cp.dst[1], cp.dst[2], g_log, beta, state, o, B,
+                                           T, Hqk, Hv, head_map, scale, workspace, s, fuse, cu, ntok);
+    }
     if (in_dtype == B200LAB_BF16)
         return dispatch_out<__nv_bfloat16>(out_dtype, q, k, v, g_log, beta, state, o, B, T, Hqk, Hv,
                                            head_map, scale, workspace, s, fuse, cu, ntok);

@@ -7,13 +7,13 @@
 // Hq=16, Hv=48, v-head h reads q/k head h % Hq), input generator (the LCG of
 // src/gdn_sm75.cu:1270-1279, drawn in the order q, k, v, g, beta), scale
 // 1/sqrt(128), report lines and exit codes (0 = all variants within 2e-2 of
-// the CPU recurrence, 1 = a variant failed, 2 = usage).  The kernels take
-// 16-bit q/k/v, so the LCG values are rounded to bf16 once and the CPU check
-// runs on the rounded values.  Variants:
+// the CPU recurrence, 1 = a variant failed, 2 = usage).  q/k/v go to the
+// library as fp32, the reference kernels' const float* (the prefill rounds
+// them to bf16 copies in its workspace), and the CPU check runs on the same
+// unrounded values.  Variants:
 //   prefill  gdn_prefill_sm100 (chunked, tcgen05)
 //   decode   gdn_decode_sm100 called once per token (token-serial)
 // Unlike the reference, the final state is checked too.
-#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -104,55 +104,51 @@ int main(int argc, char** argv) {
     for (auto& x : v) x = rnd() * 0.2f;
     for (auto& x : g) x = -0.2f + rnd() * 0.05f;
     for (auto& x : bt) x = 0.4f + (rnd() + 0.5f) * 0.4f;
-    std::vector<__nv_bfloat16> qh(nq), kh(nq), vh(nv);
-    for (size_t i = 0; i < nq; ++i) { qh[i] = __float2bfloat16(q[i]); q[i] = __bfloat162float(qh[i]); }
-    for (size_t i = 0; i < nq; ++i) { kh[i] = __float2bfloat16(k[i]); k[i] = __bfloat162float(kh[i]); }
-    for (size_t i = 0; i < nv; ++i) { vh[i] = __float2bfloat16(v[i]); v[i] = __bfloat162float(vh[i]); }
 
     std::vector<double> S_ref(ns, 0.0), o_ref(nv);
     cpu_recurrence(q, k, v, g, bt, S_ref, o_ref, B, T, Hq, Hv, scale);
 
-    __nv_bfloat16 *dq, *dk, *dv;
+    float *dq, *dk, *dv;
     float *dg, *db, *dS, *dO;
-    CHECK_CUDA(cudaMalloc(&dq, nq * 2));
-    CHECK_CUDA(cudaMalloc(&dk, nq * 2));
-    CHECK_CUDA(cudaMalloc(&dv, nv * 2));
+    CHECK_CUDA(cudaMalloc(&dq, nq * 4));
+    CHECK_CUDA(cudaMalloc(&dk, nq * 4));
+    CHECK_CUDA(cudaMalloc(&dv, nv * 4));
     CHECK_CUDA(cudaMalloc(&dg, ng * 4));
     CHECK_CUDA(cudaMalloc(&db, ng * 4));
     CHECK_CUDA(cudaMalloc(&dS, ns * 4));
     CHECK_CUDA(cudaMalloc(&dO, nv * 4));
-    CHECK_CUDA(cudaMemcpy(dq, qh.data(), nq * 2, cudaMemcpyHostToDevice));
-    CHECK_CUDA(cudaMemcpy(dk, kh.data(), nq * 2, cudaMemcpyHostToDevice));
-    CHECK_CUDA(cudaMemcpy(dv, vh.data(), nv * 2, cudaMemcpyHostToDevice));
+    CHECK_CUDA(cudaMemcpy(dq, q.data(), nq * 4, cudaMemcpyHostToDevice));
+    CHECK_CUDA(cudaMemcpy(dk, k.data(), nq * 4, cudaMemcpyHostToDevice));
+    CHECK_CUDA(cudaMemcpy(dv, v.data(), nv * 4, cudaMemcpyHostToDevice));
     CHECK_CUDA(cudaMemcpy(dg, g.data(), ng * 4, cudaMemcpyHostToDevice));
     CHECK_CUDA(cudaMemcpy(db, bt.data(), ng * 4, cudaMemcpyHostToDevice));
-    const size_t ws_bytes = gdn_prefill_sm100_workspace(B, T, Hq, Hv, kSv, kSv);
+    const size_t ws_bytes = gdn_prefill_sm100_workspace_ex(B, T, Hq, Hv, kSv, kSv, B200LAB_F32);
     void* ws = nullptr;
     CHECK_CUDA(cudaMalloc(&ws, ws_bytes));
 
     // token-serial variant: gdn_decode_sm100 per token on strided views needs contiguous
     // per-token tensors, so the inputs are regrouped [t][b][...] once.
-    __nv_bfloat16 *tq, *tk, *tv;
+    float *tq, *tk, *tv;
     float *tg, *tb, *tO;
-    CHECK_CUDA(cudaMalloc(&tq, nq * 2));
-    CHECK_CUDA(cudaMalloc(&tk, nq * 2));
-    CHECK_CUDA(cudaMalloc(&tv, nv * 2));
+    CHECK_CUDA(cudaMalloc(&tq, nq * 4));
+    CHECK_CUDA(cudaMalloc(&tk, nq * 4));
+    CHECK_CUDA(cudaMalloc(&tv, nv * 4));
     CHECK_CUDA(cudaMalloc(&tg, ng * 4));
     CHECK_CUDA(cudaMalloc(&tb, ng * 4));
     CHECK_CUDA(cudaMalloc(&tO, nv * 4));
     for (int bb = 0; bb < B; ++bb)
         for (int t = 0; t < T; ++t) {
             const size_t src = (size_t)bb * T + t, dst = (size_t)t * B + bb;
-            CHECK_CUDA(cudaMemcpy(tq + dst * Hq * kSv, dq + src * Hq * kSv, Hq * kSv * 2, cudaMemcpyDeviceToDevice));
-            CHECK_CUDA(cudaMemcpy(tk + dst * Hq * kSv, dk + src * Hq * kSv, Hq * kSv * 2, cudaMemcpyDeviceToDevice));
-            CHECK_CUDA(cudaMemcpy(tv + dst * Hv * kSv, dv + src * Hv * kSv, Hv * kSv * 2, cudaMemcpyDeviceToDevice));
+            CHECK_CUDA(cudaMemcpy(tq + dst * Hq * kSv, dq + src * Hq * kSv, Hq * kSv * 4, cudaMemcpyDeviceToDevice));
+            CHECK_CUDA(cudaMemcpy(tk + dst * Hq * kSv, dk + src * Hq * kSv, Hq * kSv * 4, cudaMemcpyDeviceToDevice));
+            CHECK_CUDA(cudaMemcpy(tv + dst * Hv * kSv, dv + src * Hv * kSv, Hv * kSv * 4, cudaMemcpyDeviceToDevice));
             CHECK_CUDA(cudaMemcpy(tg + dst * Hv, dg + src * Hv, Hv * 4, cudaMemcpyDeviceToDevice));
             CHECK_CUDA(cudaMemcpy(tb + dst * Hv, db + src * Hv, Hv * 4, cudaMemcpyDeviceToDevice));
         }
 
     auto prefill = [&]() {
         return gdn_prefill_sm100(dq, dk, dv, dg, db, dS, dO, B, T, Hq, Hv, kSv, kSv, 0, scale,
-                                 B200LAB_BF16, B200LAB_F32, ws, ws_bytes, nullptr);
+                                 B200LAB_F32, B200LAB_F32, ws, ws_bytes, nullptr);
     };
     auto serial = [&]() {
         int st = B200LAB_OK;
@@ -160,7 +156,7 @@ int main(int argc, char** argv) {
             st = gdn_decode_sm100(tq + (size_t)t * B * Hq * kSv, tk + (size_t)t * B * Hq * kSv,
                                   tv + (size_t)t * B * Hv * kSv, tg + (size_t)t * B * Hv,
                                   tb + (size_t)t * B * Hv, dS, tO + (size_t)t * B * Hv * kSv, B, Hq,
-                                  Hv, kSv, kSv, 0, scale, B200LAB_BF16, B200LAB_F32, nullptr);
+                                  Hv, kSv, kSv, 0, scale, B200LAB_F32, B200LAB_F32, nullptr);
         return st;
     };
 
