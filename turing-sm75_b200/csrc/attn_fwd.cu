@@ -357,6 +357,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         float m = -INFINITY;  // running max of scaled scores, log2 units
         float l = 0.f;
         bool ok = true;
+        // a warp whose 32 rows all lie past the queries (short or GQA-packed queries) writes no
+        // P: it only keeps step with the tiles, so that its arrival is counted for the right one
+        const bool warp_rows = __any_sync(0xffffffffu, qrow < Sq);
         for (int j = 0; j < nkv; ++j) {
             // S_0(j): commit j on s_full0.  S_1(j): the prologue's s1_pro, then step j-1's
             // commit on done[(j-1)&1] (its ((j-1)>>1)-th)
@@ -367,6 +370,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
             tc_fence_after();
+            if (!warp_rows) {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars->p_full[t]);
+                continue;
+            }
             uint32_t sr[BN];
 #pragma unroll
             for (int c = 0; c < BN / 32; ++c)
@@ -620,7 +629,7 @@ SplitPlan plan_splits(int B, int Hq, int Sq, int Skv) {
     const int nkv = (Skv + BN - 1) / BN;
     SplitPlan sp{1, nkv};
     if (base >= sms || nkv < 4) return sp;
-    long long want_ll = (sms + base - 1) / base;
+    long long want_ll = sms / base;  // one wave: at most one CTA an SM
     if (want_ll > 64) want_ll = 64;
     int want = (int)want_ll;
     want = min(want, nkv / 2);
