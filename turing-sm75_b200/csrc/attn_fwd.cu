@@ -196,6 +196,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     const int j0 = split * p.tiles_per_split;
     const int nkv = max(0, min(nkv_need - j0, p.tiles_per_split));
+    // the second query tile holds rows (false only for short queries: its products are skipped)
+    const bool tile1 = q0 + BM < Sq;
 
     if (threadIdx.x == 0) {
         mbar_init(&bars->q_full, 1);
@@ -316,7 +318,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tc_fence_after();
                     qk(0, 0);
                     mma_commit(&bars->s_full0);
-                    qk(1, 0);
+                    if (tile1) qk(1, 0);
                     mma_commit(&bars->s1_pro);
                 }
             }
@@ -333,10 +335,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mma_commit(&bars->s_full0);
                 }
                 // tile 1
-                if (!mbar_wait(&bars->p_full[1], j & 1, abort, &g_err_attn)) break;
-                tc_fence_after();
-                pv(1, j);
-                if (jn < nkv) qk(1, jn);
+                if (tile1) {
+                    if (!mbar_wait(&bars->p_full[1], j & 1, abort, &g_err_attn)) break;
+                    tc_fence_after();
+                    pv(1, j);
+                    if (jn < nkv) qk(1, jn);
+                }
                 mma_commit(&bars->done[st]);
             }
             mma_commit(&bars->o_final);
@@ -358,9 +362,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         float l = 0.f;
         bool ok = true;
         // a warp whose 32 rows all lie past the queries (short or GQA-packed queries) writes no
-        // P: it only keeps step with the tiles, so that its arrival is counted for the right one
+        // P: it only keeps step with the tiles, so that its arrival is counted for the right one.
+        // A second tile with no rows at all is not computed: its warps skip the key loop.
         const bool warp_rows = __any_sync(0xffffffffu, qrow < Sq);
-        for (int j = 0; j < nkv; ++j) {
+        const int nkv_t = (t == 1 && !tile1) ? 0 : nkv;
+        for (int j = 0; j < nkv_t; ++j) {
             // S_0(j): commit j on s_full0.  S_1(j): the prologue's s1_pro, then step j-1's
             // commit on done[(j-1)&1] (its ((j-1)>>1)-th)
             uint64_t* s_bar = t == 0 ? &bars->s_full0 : (j == 0 ? &bars->s1_pro : &bars->done[(j - 1) & 1]);
