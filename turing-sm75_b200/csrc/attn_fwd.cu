@@ -97,6 +97,7 @@ struct Params {
     int nsplit, tiles_per_split;
     int total_q, total_k, max_sq;  // varlen: the buffers' token counts and the grid's sizing
     int pack_sq;  // > 0: GQA-packed rows (row r is query r % pack_sq); 0: row = query
+    int tail_groups;  // causal: groups whose query pairs are dispatched level-major
     float scale_log2;
 };
 
@@ -158,10 +159,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int split = (int)blockIdx.x % p.nsplit;
-    const int cta_lin = (int)blockIdx.x / p.nsplit;
-    const int hq = blockIdx.y;
-    const int b = blockIdx.z;
+    // Causal CTAs differ in work (a pair's key tiles grow with its row index): the linear
+    // block index follows causal_unit_order (common.cuh), the last groups level-major so the
+    // last wave holds the shortest CTAs.  Splits of one pair stay adjacent.  Packed sequences
+    // keep the plain order (blockIdx.z is the sequence).
+    int split, cta_lin, hq, b;
+    if (p.causal && !kVarlen) {
+        const int lin = (int)(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z));
+        split = lin % p.nsplit;
+        int g;
+        causal_unit_order(lin / p.nsplit, p.n_ctas, (int)(gridDim.y * gridDim.z), p.tail_groups, cta_lin, g);
+        hq = g % (int)gridDim.y;
+        b = g / (int)gridDim.y;
+    } else {
+        split = (int)blockIdx.x % p.nsplit;
+        cta_lin = (int)blockIdx.x / p.nsplit;
+        hq = blockIdx.y;
+        b = blockIdx.z;
+    }
     int Sq = p.Sq, Skv = p.Skv, n_ctas = p.n_ctas;  // this sequence's lengths
     int q_tok0 = 0, k_tok0 = 0;                      // varlen: its first token in Q/O, K/V
     if constexpr (kVarlen) {
@@ -625,12 +640,7 @@ struct SplitPlan {
     int nsplit, tiles_per_split;
 };
 SplitPlan plan_splits(int B, int Hq, int Sq, int Skv) {
-    int sms = 148;
-    int dev = 0;
-    if (cudaGetDevice(&dev) == cudaSuccess) {
-        int v = 0;
-        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0) sms = v;
-    }
+    const int sms = device_sm_count();
     const long long base = (long long)((Sq + kQTiles * BM - 1) / (kQTiles * BM)) * Hq * B;
     const int nkv = (Skv + BN - 1) / BN;
     SplitPlan sp{1, nkv};
@@ -698,6 +708,7 @@ int launch(const void* Q, const void* K, const void* V, void* O, int B, int Hq, 
     if (sp.nsplit > 1 && (ws == nullptr || ws_bytes < need)) sp = SplitPlan{1, (Skv + BN - 1) / BN};
     p.nsplit = sp.nsplit;
     p.tiles_per_split = sp.tiles_per_split;
+    p.tail_groups = causal_tail_groups(p.n_ctas * p.nsplit, B * Hq);
     const size_t rows = (size_t)B * Hq * Sq;
     p.part_o = nullptr;
     p.part_ml = nullptr;

@@ -73,6 +73,7 @@ struct Params {
     const void* G;  // gate [B][Hq][Sq][D] or null
     void* O;
     int Hq, Sq, Skv, group, n_ctas, causal;
+    int tail_groups;  // causal: groups whose query tiles are dispatched level-major
     float scale_log2;
 };
 
@@ -94,9 +95,21 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int cta = p.causal ? (p.n_ctas - 1 - (int)blockIdx.x) : (int)blockIdx.x;
-    const int hq = blockIdx.y;
-    const int b = blockIdx.z;
+    // causal: the linear block index follows causal_unit_order (common.cuh), heaviest query
+    // tile of a group first and the last groups level-major, so the last wave is the lightest
+    int cta, hq, b;
+    if (p.causal) {
+        const int lin = (int)(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z));
+        int unit, g;
+        causal_unit_order(lin, p.n_ctas, (int)(gridDim.y * gridDim.z), p.tail_groups, unit, g);
+        cta = p.n_ctas - 1 - unit;
+        hq = g % (int)gridDim.y;
+        b = g / (int)gridDim.y;
+    } else {
+        cta = (int)blockIdx.x;
+        hq = blockIdx.y;
+        b = blockIdx.z;
+    }
     const int q0 = cta * BM;
     const int off = p.Skv - p.Sq;
     const int nkv_all = (p.Skv + BN - 1) / BN;
@@ -417,6 +430,7 @@ int launch(const void* Q, const void* K, const void* V, const void* G, void* O, 
     p.group = Hq / Hkv;
     p.n_ctas = (Sq + BM - 1) / BM;
     p.causal = causal;
+    p.tail_groups = causal_tail_groups(p.n_ctas, B * Hq);
     p.scale_log2 = scale * 1.4426950408889634f;
     auto kern = attn_gated_kernel<T>;
     B200_TRY_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kAlloc));

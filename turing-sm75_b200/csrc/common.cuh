@@ -35,6 +35,32 @@ void count_launch(int n);
 // Returns B200LAB_OK when the current device is an sm_100 part.
 int check_device_sm100();
 
+// The current device's SM count (148 when the query fails).
+int device_sm_count();
+
+// Causal attention grids: the units (query tiles) of one (head, batch) group differ in work,
+// heaviest first.  Blocks are dispatched in linear index order, so a plain group-major order
+// leaves the heavy units of the last groups in the last wave.  The units of the last
+// `tail_groups` groups are therefore ordered level-major (every group's heaviest unit, then
+// every group's next ...), which keeps the last wave to the lightest units, while the groups
+// before them stay group-major, their K/V read by neighbouring blocks out of L2.
+// tail_groups covers about eight waves of one block an SM.
+int causal_tail_groups(int units_per_group, int groups);
+
+// Maps a linear unit index onto (unit within its group, group) under that order.
+__host__ __device__ __forceinline__ void causal_unit_order(int rest, int units, int groups,
+                                                           int tail_groups, int& unit, int& group) {
+    const int plain = (groups - tail_groups) * units;
+    if (rest < plain) {
+        group = rest / units;
+        unit = rest % units;
+    } else {
+        const int r2 = rest - plain;
+        unit = r2 / tail_groups;
+        group = groups - tail_groups + r2 % tail_groups;
+    }
+}
+
 // Encodes a 3-D tiled TMA descriptor over a row-major [d2][d1][d0] tensor of
 // `elem_bytes`-wide elements with a (box0, box1, 1) box and the given swizzle.
 int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,

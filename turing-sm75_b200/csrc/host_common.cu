@@ -18,6 +18,20 @@ int check_device_sm100() {
     return B200LAB_OK;
 }
 
+int device_sm_count() {
+    int dev = 0, v = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0)
+        return v;
+    return 148;
+}
+
+int causal_tail_groups(int units_per_group, int groups) {
+    if (units_per_group <= 0 || groups <= 0) return 0;
+    const long long want = (8LL * device_sm_count() + units_per_group - 1) / units_per_group;
+    return (int)(want < groups ? want : groups);
+}
+
 // cuTensorMapEncodeTiled reached through the runtime's driver entry point, so
 // the library does not link libcuda directly.
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
