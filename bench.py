@@ -59,13 +59,15 @@ def _scaled(x, f):
     return None if x is None else x * f
 
 
-def profile_traffic(name):
+def profile_traffic(name, key=None):
     """Per-launch DRAM bytes of the dominant kernel, read from the committed ncu
-    summary profiles/<name>.md (line `traffic_bytes_per_launch: <float>`)."""
+    summary profiles/<name>.md (line `traffic_bytes_per_launch: <float>`, or
+    `traffic_bytes_per_launch[<key>]: <float>` in a summary that covers several workloads)."""
     path = os.path.join(ROOT, "profiles", f"{name}.md")
+    tag = "traffic_bytes_per_launch:" if key is None else f"traffic_bytes_per_launch[{key}]:"
     try:
         for line in open(path):
-            if line.strip().startswith("traffic_bytes_per_launch:"):
+            if line.strip().startswith(tag):
                 return float(line.split(":", 1)[1].strip().split()[0])
     except OSError:
         pass
@@ -450,7 +452,10 @@ def bench_attn_case(name, shp, args, dist, peaks):
         roof = {"bound": "hbm", "achieved": bytes_local / (ms_local * 1e-3) / 1e9,
                 "peak": peaks["hbm_gbs"], "unit": "GB/s"}
     roof["frac"] = roof["achieved"] / roof["peak"]
-    roof["traffic"] = None
+    # profiles/ records the DRAM bytes of one full-shape call (both kernels for split-KV);
+    # a shard of (batch, kv-head) units moves its share, a replica the whole
+    traffic = profile_traffic("attn_fwd_cases", name)
+    roof["traffic"] = _scaled(traffic, (Bl * Hkvl) / (B * Hkv))
     res = {"metric": f"attn fwd TFLOP/s ({name})", "value": total_flops / (ms * 1e-3) / 1e12,
            "unit": "TFLOP/s", "us_per_step": ms * 1e3, "steps": steps,
            "flop_convention": "visible (query, key) pairs x 4 D (causal: bottom-right aligned)",
@@ -789,7 +794,8 @@ def run_reference(args):
     import workloads
     if int(os.environ.get("RANK", "0")) != 0:
         return None
-    cfg = workloads.CONFIGS[args.workload if args.workload.startswith("attn") else "attn_c5"]
+    cfg = workloads.CONFIGS.get(args.workload) if args.workload.startswith("attn") else None
+    cfg = cfg or workloads.CONFIGS["attn_c5"]
     budget = max(0.5, args.cpu_budget_s / max(1, args.steps + args.warmup))
     vals = []
     desc = cores = None
@@ -820,14 +826,21 @@ def run_ours(args):
     dist.init()
     peaks, peaks_src = load_peaks()
     name = args.workload
-    cfgname = {"attn_c2": "attn_c2_d128", "gdn_decode": "gdn_decode_c4", "gdn_decode_state16": "gdn_decode_c4",
-               "gdn_prefill": "gdn_prefill_c3"}.get(name, name)
+    if name in ATTN_CASES and name != "attn_c1":
+        # one secondary attention shape alone, as its bench line measures it
+        cfgname = "attn_c5"
+    else:
+        cfgname = None
+    cfgname = cfgname or {"attn_c2": "attn_c2_d128", "gdn_decode": "gdn_decode_c4", "gdn_decode_state16": "gdn_decode_c4",
+               "gdn_prefill": "gdn_prefill_c3", "gdn_prefill_fused": "gdn_prefill_c3"}.get(name, name)
     cfg = dict(workloads.CONFIGS[cfgname])
     if args.attn_shape:
         # smaller instance of the same kernel, for ncu captures that must stay small
         cfg["B"], cfg["Hq"], cfg["Hkv"], cfg["S"], cfg["D"] = (int(x) for x in args.attn_shape.split(","))
         name = name + "_custom"
-    if name.startswith("attn_gated"):
+    if name in ATTN_CASES and name != "attn_c1":
+        main = bench_attn_case(name, ATTN_CASES[name], args, dist, peaks)
+    elif name.startswith("attn_gated"):
         main = bench_gated_attention(cfg, args, dist, peaks)
     elif name.startswith("attn"):
         main = bench_attention(name, cfg, args, dist, peaks)
@@ -835,6 +848,8 @@ def run_ours(args):
         main = bench_gdn_decode(cfg, args, dist, peaks)
     elif name == "gdn_decode_state16":
         main = bench_gdn_decode(cfg, args, dist, peaks, state_dtype=torch.float16)
+    elif name == "gdn_prefill_fused":
+        main = bench_gdn_prefill(cfg, args, dist, peaks, fused=True)
     else:
         main = bench_gdn_prefill(cfg, args, dist, peaks)
 
@@ -927,7 +942,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="attn_c5",
                     choices=["attn_c5", "attn_c1", "attn_c2", "attn_gated_d256", "gdn_decode",
-                             "gdn_decode_state16", "gdn_prefill"])
+                             "gdn_decode_state16", "gdn_prefill", "gdn_prefill_fused"] + [
+                                 k for k in ATTN_CASES if k not in ("attn_c1",)],
+                    help="the headline (attn_c5) or one secondary workload alone (for profiling)")
     ap.add_argument("--no-secondary", dest="secondary", action="store_false")
     ap.add_argument("--attn-shape", default=None, metavar="B,Hq,Hkv,S,D",
                     help="override the attention shape (profiling a smaller case)")

@@ -35,6 +35,7 @@
 #include "common.cuh"
 #include "errwords.h"
 
+#include <type_traits>
 #include <vector>
 
 namespace b200 {
@@ -213,6 +214,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int nkv = max(0, min(nkv_need - j0, p.tiles_per_split));
     // the second query tile holds rows (false only for short queries: its products are skipped)
     const bool tile1 = q0 + BM < Sq;
+    // the combine kernel that follows a split grid may be scheduled now: it waits for this
+    // grid to complete before reading the partials (griddepcontrol.wait)
+    if constexpr (kSplit) allow_dependent_launch();
 
     if (threadIdx.x == 0) {
         mbar_init(&bars->q_full, 1);
@@ -552,40 +556,93 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-// Split-KV combine: one warp per query row merges the nsplit partials,
+// Split-KV combine: the nsplit (<= 64) partials of a query row are merged as
 //   M = max_s m_s,  O = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s   (0 if no key seen).
+// A row gets wpr = 2^wpr_log2 warps (wpr >= nsplit / 8); warp `sub` of the row owns the
+// splits sub, sub + wpr, ... (at most 8) and issues all of their O loads before anything
+// else, so a row costs one memory round trip; the row's (max, sum) pairs are staged in
+// shared memory, reduced with shuffles, and the wpr warps' weighted sums are added in shared
+// memory.  Launched as a programmatic dependent of the split kernel: it waits for that grid
+// to complete (griddepcontrol.wait) before reading the partials.
 template <int D, typename T>
 __global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restrict__ part_o,
                                                            const float* __restrict__ part_ml,
-                                                           T* __restrict__ O, long long rows, int nsplit) {
-    const long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    if (row >= rows) return;
-    const float2* ml = reinterpret_cast<const float2*>(part_ml) + row * nsplit;
-    float M = -INFINITY;
-    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, ml[s].x);
+                                                           T* __restrict__ O, long long rows, int nsplit,
+                                                           int wpr_log2) {
     constexpr int kPer = D / 32;  // values per lane (4 or 2)
-    float acc[kPer];
+    static_assert(kPer == 4 || kPer == 2, "head dim 64 or 128");
+    using Vec = typename std::conditional<kPer == 4, float4, float2>::type;
+    __shared__ float2 s_ml[8][64];
+    __shared__ float s_acc[8][D];
+    grid_dependency_wait();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int wpr = 1 << wpr_log2;
+    const int rpb = 8 >> wpr_log2;  // rows per block
+    const int slot = warp >> wpr_log2, sub = warp & (wpr - 1);
+    const long long row0 = (long long)blockIdx.x * rpb;
+    const long long row = row0 + slot;
+    const bool live = row < rows;
+
+    Vec v[8];
 #pragma unroll
-    for (int u = 0; u < kPer; ++u) acc[u] = 0.f;
+    for (int i = 0; i < 8; ++i) {
+        const int sp = sub + i * wpr;
+        v[i] = Vec{};
+        if (live && sp < nsplit)
+            v[i] = *reinterpret_cast<const Vec*>(part_o + (row * nsplit + sp) * D + lane * kPer);
+    }
+    const float2* ml = reinterpret_cast<const float2*>(part_ml);
+    for (int i = threadIdx.x; i < rpb * nsplit; i += blockDim.x) {
+        const int r = i / nsplit, sp = i % nsplit;
+        float2 e = make_float2(-INFINITY, 0.f);
+        if (row0 + r < rows) e = ml[(row0 + r) * nsplit + sp];
+        if (!(e.y > 0.f)) e = make_float2(-INFINITY, 0.f);  // an empty split takes no part
+        s_ml[r][sp] = e;
+    }
+    __syncthreads();
+
+    const float2 e0 = lane < nsplit ? s_ml[slot][lane] : make_float2(-INFINITY, 0.f);
+    const float2 e1 = lane + 32 < nsplit ? s_ml[slot][lane + 32] : make_float2(-INFINITY, 0.f);
+    float M = fmaxf(e0.x, e1.x);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
     float L = 0.f;
     if (M != -INFINITY) {
-        for (int s = 0; s < nsplit; ++s) {
-            const float2 e = ml[s];
-            if (!(e.y > 0.f)) continue;
-            const float w = ex2(e.x - M);
-            L = fmaf(w, e.y, L);
-            const float* po = part_o + (row * nsplit + s) * D + lane * kPer;
+        L = (e0.y > 0.f ? ex2(e0.x - M) * e0.y : 0.f) + (e1.y > 0.f ? ex2(e1.x - M) * e1.y : 0.f);
 #pragma unroll
-            for (int u = 0; u < kPer; ++u) acc[u] = fmaf(w, po[u], acc[u]);
+        for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+    }
+    float acc[kPer];
+#pragma unroll
+    for (int c = 0; c < kPer; ++c) acc[c] = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int sp = sub + i * wpr;
+        if (sp < nsplit && M != -INFINITY) {
+            const float2 e = s_ml[slot][sp];
+            if (e.y > 0.f) {
+                const float w = ex2(e.x - M);
+                const float* pv = reinterpret_cast<const float*>(&v[i]);
+#pragma unroll
+                for (int c = 0; c < kPer; ++c) acc[c] = fmaf(w, pv[c], acc[c]);
+            }
         }
     }
-    const float inv = L > 0.f ? 1.f / L : 0.f;
-    T* orow = O + row * D + lane * kPer;
 #pragma unroll
-    for (int u = 0; u < kPer; u += 2) {
-        const uint32_t pk = Elem<T>::pack2(acc[u] * inv, acc[u + 1] * inv);
-        *reinterpret_cast<uint32_t*>(orow + u) = pk;
+    for (int c = 0; c < kPer; ++c) s_acc[warp][lane * kPer + c] = acc[c];
+    __syncthreads();
+
+    if (live) {
+        const float inv = L > 0.f ? 1.f / L : 0.f;
+        T* orow = O + row * D;
+        for (int pr = sub * 32 + lane; pr < D / 2; pr += wpr * 32) {  // column pairs
+            float a0 = 0.f, a1 = 0.f;
+            for (int k = 0; k < wpr; ++k) {
+                a0 += s_acc[slot * wpr + k][2 * pr];
+                a1 += s_acc[slot * wpr + k][2 * pr + 1];
+            }
+            *reinterpret_cast<uint32_t*>(orow + 2 * pr) = Elem<T>::pack2(a0 * inv, a1 * inv);
+        }
     }
 }
 
@@ -723,8 +780,28 @@ int launch(const void* Q, const void* K, const void* V, void* O, int B, int Hq, 
     count_launch(1);
     B200_TRY_CUDA(cudaGetLastError());
     if (sp.nsplit > 1) {
-        attn_combine_kernel<D, T><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(
-            p.part_o, p.part_ml, static_cast<T*>(O), (long long)rows, sp.nsplit);
+        // a programmatic dependent of the split kernel: its launch overlaps that grid's
+        // drain, and griddepcontrol.wait in the kernel orders its reads after the partials
+        cudaLaunchConfig_t cc = {};
+        // warps per row: enough that a warp owns at most 8 splits, then more (up to
+        // min(nsplit, 8)) while the grid has fewer than ~16 warps an SM
+        int wpr_log2 = 0;
+        while ((8 << wpr_log2) < sp.nsplit) ++wpr_log2;
+        while (wpr_log2 < 3 && (1 << wpr_log2) < sp.nsplit &&
+               (long long)rows * (1 << wpr_log2) < 16LL * device_sm_count())
+            ++wpr_log2;
+        const int rpb = 8 >> wpr_log2;
+        cc.gridDim = dim3((unsigned)((rows + rpb - 1) / rpb));
+        cc.blockDim = dim3(256);
+        cc.stream = st;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[0].val.programmaticStreamSerializationAllowed = 1;
+        cc.attrs = at;
+        cc.numAttrs = 1;
+        B200_TRY_CUDA(cudaLaunchKernelEx(&cc, attn_combine_kernel<D, T>, (const float*)p.part_o,
+                                         (const float*)p.part_ml, static_cast<T*>(O), (long long)rows,
+                                         sp.nsplit, wpr_log2));
         count_launch(1);
         B200_TRY_CUDA(cudaGetLastError());
     }
