@@ -2,7 +2,8 @@
 """Benchmark of the B200-native attention / Gated DeltaNet hot path.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload attn_c5|attn_c1|attn_c2|attn_gated_d256|gdn_decode|gdn_decode_state16|gdn_prefill]
+                    [--workload attn_c5|attn_c1|attn_c2|attn_gated_d256|gdn_decode|gdn_decode_state16|gdn_prefill
+                                |gdn_prefill_fused|<any secondary attention shape, e.g. attn_splitkv_q1>]
 
 One JSON line on stdout (rank 0).  The headline workload is the long-context
 causal GQA attention config (B4 Hq32 Hkv8 S16384 D128 bf16), the config the
