@@ -138,7 +138,13 @@ int attn_gated_fwd_sm100(const void* Q, const void* K, const void* V, const void
  *   dk = dv = 128.  workspace: gdn_prefill_sm100_workspace_ex(..., in_dtype)
  *   bytes (gdn_prefill_sm100_workspace() for 16-bit inputs).  fp32 q, k, v
  *   (the reference kernels' const float*) are converted once to bf16 copies in
- *   the workspace; the tensor-core operands are 16-bit for every in_dtype. */
+ *   the workspace; the tensor-core operands are 16-bit for every in_dtype.
+ *   With few sequences x v-heads (fewer state-pass CTAs than SMs, as on each GPU
+ *   of a multi-GPU split) the chunk chain is cut into segments that run side by
+ *   side and are then linked (two more kernels); the queried size includes their
+ *   buffers.  Any workspace of at least gdn_prefill_sm100_workspace_min() bytes
+ *   is accepted: one too small for the segment buffers runs the unsegmented
+ *   chain (same results up to rounding). */
 int gdn_prefill_sm100(const void* q, const void* k, const void* v,
                       const float* g_log, const float* beta, float* state, void* o,
                       int B, int T, int Hqk, int Hv, int dk, int dv, int head_map,
@@ -149,6 +155,9 @@ size_t gdn_prefill_sm100_workspace(int B, int T, int Hqk, int Hv, int dk, int dv
  * bf16 copies of q, k, v (B*T*(2*Hqk + Hv)*dk*2 bytes, rounded up).  Packed
  * sequences (the varlen entries) use B and max_seqlen, as for the 16-bit size. */
 size_t gdn_prefill_sm100_workspace_ex(int B, int T, int Hqk, int Hv, int dk, int dv, int in_dtype);
+/* The smallest workspace the prefill entries accept (the chunk items, plus the
+ * fp32 copies for B200LAB_F32 inputs): the unsegmented chain. */
+size_t gdn_prefill_sm100_workspace_min(int B, int T, int Hqk, int Hv, int dk, int dv, int in_dtype);
 
 /* Packed variable-length sequences (no counterpart in the reference, whose
  * prefill runs one sequence, src/gdn_sm75.cu:1246-1412): q, k [total][Hqk][dk],
@@ -178,8 +187,9 @@ int gdn_prefill_sm100_varlen(const void* q, const void* k, const void* v,
  * Same arguments and results as gdn_prefill_sm100, minus the workspace: the
  * scratch is a file-scope device array of B200LAB_NOALLOC_SCRATCH_BYTES
  * (64 MiB) that every GPU loading the prefill kernels holds until the process
- * exits.  A problem whose gdn_prefill_sm100_workspace_ex() exceeds that size is
- * rejected with B200LAB_ERR_WORKSPACE before anything is launched (about
+ * exits.  A problem whose gdn_prefill_sm100_workspace_min() exceeds that size is
+ * rejected with B200LAB_ERR_WORKSPACE before anything is launched (the
+ * segmented chain runs when gdn_prefill_sm100_workspace_ex() fits; about
  * 50 KB per (sequence, v-head, 64-token chunk): B*Hv*ceil(T/64) <= 1344,
  * e.g. Hv=48 up to T=1792, Hv=32 up to T=2688).
  * Every call looks up the array's device address with the caller's device

@@ -86,3 +86,21 @@ def test_state16_decode_rules_rejected_before_launch():
     # state not 16-byte aligned
     odd = ctypes.c_void_p(24)
     assert f(p, p, p, p, p, odd, b200lab.F16, p, 1, 1, 1, 128, 128, 0, 0.1, 1, 1, n) == b200lab.ERR_INVALID
+
+
+def test_prefill_segment_plan_in_workspace_sizes():
+    """Host-side plan of the segmented chain, seen through the workspace queries (no GPU
+    call: the SM count falls back to 148 without a device).  One GPU's share of C3 on 8 GPUs
+    (Hv 4) is segmented; C3 itself (Hv 32, 128 state CTAs) and short sequences are not."""
+    import b200lab
+    L = b200lab.lib()
+    full = lambda *a: L.gdn_prefill_sm100_workspace_ex(*a, 128, 128, b200lab.BF16)  # noqa: E731
+    small = lambda *a: L.gdn_prefill_sm100_workspace_min(*a, 128, 128, b200lab.BF16)  # noqa: E731
+    assert full(1, 4096, 16, 32) == small(1, 4096, 16, 32)
+    assert full(1, 300, 2, 4) == small(1, 300, 2, 4)
+    # 4 segments of 16 chunks, a head: end states 4 x 256 x 128 fp32, zero-state outputs
+    # 4096 x 128 fp32, R 4096 x 128 bf16, segment starts 4 x 128 x 128 bf16
+    extra = 4 * (4 * 256 * 128 * 4 + 4096 * 128 * 4 + 4096 * 128 * 2 + 4 * 128 * 128 * 2)
+    assert full(1, 4096, 16, 4) == small(1, 4096, 16, 4) + extra
+    assert L.gdn_prefill_sm100_workspace_ex(1, 4096, 16, 4, 128, 128, b200lab.F32) == \
+        L.gdn_prefill_sm100_workspace_min(1, 4096, 16, 4, 128, 128, b200lab.F32) + extra

@@ -45,7 +45,7 @@ def _pre(q, k, a, b, A_log, dt_bias):
     return _norm(q), _norm(k), g, beta
 
 
-@pytest.mark.parametrize("T", [1, 64, 200])
+@pytest.mark.parametrize("T", [1, 64, 200, 1000])  # 1000: a segmented chain (2 segments)
 @pytest.mark.parametrize("with_params", [True, False])
 def test_prefill_fused(cuda, T, with_params):
     dev = torch.device("cuda:0")

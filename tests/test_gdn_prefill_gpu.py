@@ -134,3 +134,59 @@ def test_workspace_and_dtype_rules(cuda):
     assert L.gdn_prefill_sm100(*args, 2, 1, p(ws), need, st) == b200lab.ERR_WORKSPACE
     assert L.gdn_prefill_sm100(*args, 1, 1, p(ws), need, st) == b200lab.OK
     assert b200lab.device_status() == b200lab.OK
+
+
+# Few sequences x v-heads leave most SMs idle in the one-chain-per-head state pass, so the
+# chunk chain is cut into segments run side by side and linked afterwards (the workspace
+# query then exceeds the minimum).  (1, 1000, 2, 4): 4 segments of 4 chunks; (2, 700, 2, 4):
+# 2 segments, a partial last chunk; (1, 4096, 16, 4): 4 segments of 16 (one GPU's share of
+# C3 on 8 GPUs).
+SEG_CASES = [(1, 1000, 2, 4, 0), (2, 700, 2, 4, 1), (1, 4096, 16, 4, 0)]
+
+
+@pytest.mark.parametrize("B,T,Hqk,Hv,head_map", SEG_CASES)
+def test_segmented_chain(cuda, B, T, Hqk, Hv, head_map):
+    assert b200lab.gdn_prefill_workspace_bytes(B, T, Hqk, Hv) > \
+        b200lab.gdn_prefill_workspace_min_bytes(B, T, Hqk, Hv)
+    o, S, o_ref, S_ref = _case(B, T, Hqk, Hv, head_map=head_map, state_std=0.05, seed=50 + T)
+    assert_close(o, o_ref, f"segmented out T{T}")
+    assert_close(S, S_ref, f"segmented state T{T}")
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
+def test_segmented_equals_unsegmented(cuda, out_dtype):
+    """The same call with the full workspace (segmented) and the minimum one (one chain)."""
+    dev = torch.device("cuda:0")
+    B, T, Hqk, Hv = 1, 2000, 4, 8
+    q, k, v, g, b = (t.to(dev) for t in workloads.gdn_inputs(B, T, Hqk, Hv, 128, torch.bfloat16, seed=9))
+    S0 = workloads.gdn_state(B, Hv, 128, std=0.05, seed=10).to(dev)
+    full = b200lab.gdn_prefill_workspace_bytes(B, T, Hqk, Hv)
+    small = b200lab.gdn_prefill_workspace_min_bytes(B, T, Hqk, Hv)
+    assert full > small
+    res = []
+    for nbytes in (full, small):
+        S = S0.clone()
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        o = b200lab.gdn_prefill(q, k, v, g, b, S, out_dtype=out_dtype, workspace=ws)
+        assert b200lab.device_status() == b200lab.OK
+        res.append((to_np(o), to_np(S)))
+    assert_close(res[0][0], res[1][0], "segmented vs one chain: out")
+    assert_close(res[0][1], res[1][1], "segmented vs one chain: state")
+
+
+def test_segmented_prefill_then_decode(cuda):
+    """A segmented prefill's state continues a decode step like the recurrence's."""
+    dev = torch.device("cuda:0")
+    B, T, Hqk, Hv = 1, 1100, 2, 4
+    q, k, v, g, b = workloads.gdn_inputs(B, T + 1, Hqk, Hv, 128, torch.bfloat16, seed=12)
+    assert b200lab.gdn_prefill_workspace_bytes(B, T, Hqk, Hv) > \
+        b200lab.gdn_prefill_workspace_min_bytes(B, T, Hqk, Hv)
+    S = torch.zeros((B, Hv, 128, 128), device=dev)
+    b200lab.gdn_prefill(*[t[:, :T].contiguous().to(dev) for t in (q, k, v, g, b)], S)
+    o = b200lab.gdn_decode(*[t[:, T].contiguous().to(dev) for t in (q, k, v, g, b)], S,
+                           out_dtype=torch.float32)
+    assert b200lab.device_status() == b200lab.OK
+    o_ref, S_ref = oracle.gdn_recurrent(to_np(q), to_np(k), to_np(v), to_np(g), to_np(b),
+                                        np.zeros((B, Hv, 128, 128)), 1.0 / np.sqrt(128), 0)
+    assert_close(to_np(o), o_ref[:, T], "decode after segmented prefill")
+    assert_close(to_np(S), S_ref, "state")

@@ -35,6 +35,7 @@ EXPORTED = (
     "attn_fwd_sm100", "attn_fwd_sm100_workspace", "attn_gated_fwd_sm100", "attn_fwd_sm100_varlen",
     "attn_fwd_sm100_host",
     "gdn_prefill_sm100", "gdn_prefill_sm100_workspace", "gdn_prefill_sm100_workspace_ex",
+    "gdn_prefill_sm100_workspace_min",
     "gdn_prefill_sm100_noalloc",
     "gdn_prefill_sm100_fused", "gdn_prefill_sm100_varlen", "gdn_prefill_sm100_fused_varlen",
     "gdn_decode_sm100", "gdn_decode_sm100_state16", "gdn_decode_sm100_fused",
@@ -84,6 +85,8 @@ def lib() -> ctypes.CDLL:
         L.gdn_prefill_sm100_workspace.argtypes = [ci] * 6
         L.gdn_prefill_sm100_workspace_ex.restype = sz
         L.gdn_prefill_sm100_workspace_ex.argtypes = [ci] * 7
+        L.gdn_prefill_sm100_workspace_min.restype = sz
+        L.gdn_prefill_sm100_workspace_min.argtypes = [ci] * 7
         L.gdn_prefill_sm100_noalloc.restype = ci
         L.gdn_prefill_sm100_noalloc.argtypes = [vp] * 7 + [ci] * 7 + [cf, ci, ci, vp]
         L.gdn_decode_sm100.restype = ci
@@ -255,8 +258,14 @@ def attn_fwd_varlen(Q, K, V, cu_seqlens_q, cu_seqlens_k, max_seqlen_q: int, *, s
 
 
 def gdn_prefill_workspace_bytes(B, T, Hqk, Hv, dk=128, dv=128, in_dtype=BF16) -> int:
-    """Workspace bytes of the prefill entries for inputs of type in_dtype (F16 / BF16 / F32)."""
+    """Workspace bytes of the prefill entries for inputs of type in_dtype (F16 / BF16 / F32),
+    including the segmented chain's buffers when the shape uses it."""
     return int(lib().gdn_prefill_sm100_workspace_ex(B, T, Hqk, Hv, dk, dv, int(in_dtype)))
+
+
+def gdn_prefill_workspace_min_bytes(B, T, Hqk, Hv, dk=128, dv=128, in_dtype=BF16) -> int:
+    """The smallest workspace the prefill entries accept (the unsegmented chain)."""
+    return int(lib().gdn_prefill_sm100_workspace_min(B, T, Hqk, Hv, dk, dv, int(in_dtype)))
 
 
 def gdn_prefill(q, k, v, g_log, beta, state, *, scale: float | None = None, head_map: int = 0,

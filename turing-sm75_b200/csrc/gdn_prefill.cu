@@ -750,6 +750,19 @@ struct StateParams {
     int T, Hqk, Hv, nch, head_map;
     int ntok;
     float scale;
+    // Segmented chain (nseg > 1, dense sequences only): segment g covers chunks
+    // [g seg_len, (g + 1) seg_len).  Segment 0 runs from the caller's state as usual; later
+    // segments run from a zero state and carry 128 more state columns (slices 4-7) that start
+    // as the identity with zero values, so that their end state is the segment's transition
+    // product P_g and their outputs are R = (the output map) P.  End states go to seg_x
+    // ([B][Hv][nseg][256 v][128 k], segment 0's real columns its true end state); outputs of
+    // segments g >= 1 go to seg_o (zero-state outputs, fp32 [tokens][Hv][128]) and seg_r (R,
+    // bf16 [tokens][Hv][128], an MMA operand).  gdn_seg_link_kernel and gdn_seg_fix_kernel
+    // then chain the segment starts and add R S_start.
+    int seg_len, nseg;
+    float* seg_x;
+    float* seg_o;
+    __nv_bfloat16* seg_r;
 };
 
 // 32 consecutive outputs of one thread as 16-byte vector stores
@@ -787,16 +800,27 @@ __global__ void __launch_bounds__(st::kThreads, 1)
 
     const int slice = blockIdx.x;
     const int h = blockIdx.y;
-    const int b = blockIdx.z;
+    const int b = blockIdx.z / p.nseg;
+    const int g = blockIdx.z % p.nseg;          // segment
+    const bool aug = slice >= kD / kSlice;      // transition columns of a later segment
+    if (aug && g == 0) return;
     const SeqSpan seq = seq_span(p.cu, p.T, b);
     if (!seq_ok(seq, p.T, p.ntok)) return;    // recorded by the prep grid; state left as it is
-    const int nch = (seq.len + kC - 1) / kC;  // this sequence's chunks (p.nch for the longest)
-    if (nch == 0) return;                     // an empty sequence: its state stays as it is
+    const int cs = g * p.seg_len;             // the segment's first chunk
+    // this segment's chunks (the sequence's chunks, p.nch for the longest, when nseg == 1)
+    const int nch = min(p.seg_len, (seq.len + kC - 1) / kC - cs);
+    if (nch <= 0) return;                     // an empty sequence: its state stays as it is
+    // segmented: the link kernel, launched as a programmatic dependent, may be scheduled now
+    // (it waits for this grid to complete before reading the end states)
+    if (p.nseg > 1) allow_dependent_launch();
+    const int tok0 = seq.start + cs * kC;     // the segment's first token
+    const int seq_left = seq.len - cs * kC;   // tokens of the sequence from there on
     const int c0 = slice * kSlice;
     const int hq = qk_head(h, p.Hqk, p.Hv, p.head_map);
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
     const size_t bh = (size_t)b * p.Hv + h;  // workspace slots: p.nch chunks a (sequence, head)
+    const size_t bhcs = bh * p.nch + cs;     // the segment's first chunk slot
 
     if (tid == 0) {
         for (int i = 0; i < kStages; ++i) {
@@ -832,7 +856,7 @@ __global__ void __launch_bounds__(st::kThreads, 1)
     if (warp == kWarpProducer) {
         if (lane == 0) {
             const float* gcs_all = reinterpret_cast<const float*>(p.ws + p.ws_gcs);
-            const int bhc0 = (int)(bh * p.nch);
+            const int bhc0 = (int)bhcs;
             grid_dependency_wait();  // W, U, Aqk, M, gcs come from the prep grid
             // prologue: W_0 into the W rows of stage 2's A1 tile
             uint8_t* pro = smem + (kStages - 1) * kStage + kA1;
@@ -849,16 +873,17 @@ __global__ void __launch_bounds__(st::kThreads, 1)
                 const int bhc = bhc0 + c;
                 // W_{c+1}, M_{c+1} of the last chunk read the next sequence's first chunk (or
                 // zero fill past the end): those rows of the products are not used
-                mbar_arrive_expect_tx(bar, kStageTx);
-                tma_load_4d(stg + kA1 + 0, &tmQ, bar, 0, hq, seq.start + c * kC, 0);
+                // (transition columns have zero values: no U tile)
+                mbar_arrive_expect_tx(bar, aug ? kStageTx - 4096 : kStageTx);
+                tma_load_4d(stg + kA1 + 0, &tmQ, bar, 0, hq, tok0 + c * kC, 0);
                 tma_load_3d(stg + kA1 + 8192, &tmW, bar, 0, 0, bhc + 1);
-                tma_load_4d(stg + kA1 + 16384, &tmQ, bar, 64, hq, seq.start + c * kC, 0);
+                tma_load_4d(stg + kA1 + 16384, &tmQ, bar, 64, hq, tok0 + c * kC, 0);
                 tma_load_3d(stg + kA1 + 24576, &tmW, bar, 64, 0, bhc + 1);
-                tma_load_4d(stg + kKt, &tmK, bar, 0, hq, seq.start + c * kC, 0);
-                tma_load_4d(stg + kKt + 8192, &tmK, bar, 64, hq, seq.start + c * kC, 0);
+                tma_load_4d(stg + kKt, &tmK, bar, 0, hq, tok0 + c * kC, 0);
+                tma_load_4d(stg + kKt + 8192, &tmK, bar, 64, hq, tok0 + c * kC, 0);
                 tma_load_3d(stg + kAM, &tmAqk, bar, 0, 0, bhc);
                 tma_load_3d(stg + kAM + 8192, &tmM, bar, 0, 0, bhc + 1);
-                tma_load_3d(stg + kU, &tmU, bar, c0, 0, bhc);
+                if (!aug) tma_load_3d(stg + kU, &tmU, bar, c0, 0, bhc);
                 bulk_load_1d(stg + kG, gcs_all + (size_t)bhc * kC, kC * 4, bar);
                 issued = c + 1;
             }
@@ -942,7 +967,7 @@ __global__ void __launch_bounds__(st::kThreads, 1)
         // ---------------- compute warps: three roles, each on its own chain -------
         const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
         const float* gcs_all = reinterpret_cast<const float*>(p.ws + p.ws_gcs);
-        const size_t bhc0 = bh * p.nch;
+        const size_t bhc0 = bhcs;
         if (warp >= kWarpOut) grid_dependency_wait();  // gcs comes from the prep grid
         auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
             return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, &g_err_gdn_prefill));
@@ -964,8 +989,13 @@ __global__ void __launch_bounds__(st::kThreads, 1)
             const int i = tid;
             float S[kSlice];
             float* Sg = p.state + (bh * kD + c0) * kD + i;
+            if (g == 0) {
 #pragma unroll
-            for (int cc = 0; cc < kSlice; ++cc) S[cc] = Sg[(size_t)cc * kD];
+                for (int cc = 0; cc < kSlice; ++cc) S[cc] = Sg[(size_t)cc * kD];
+            } else {  // a later segment: zero state, the transition columns the identity
+#pragma unroll
+                for (int cc = 0; cc < kSlice; ++cc) S[cc] = (aug && i == c0 - kD + cc) ? 1.f : 0.f;
+            }
             grid_dependency_wait();  // (the state itself is an input, not a prep result)
             uint8_t* sS = smem + kSt;
             // S (16-bit) -> shared (B operand of the RQ product), then S_c is announced
@@ -996,9 +1026,13 @@ __global__ void __launch_bounds__(st::kThreads, 1)
                     publish_S(c + 1);
                 }
             }
-            if (ok) {
+            if (ok && p.nseg == 1) {
 #pragma unroll
                 for (int cc = 0; cc < kSlice; ++cc) Sg[(size_t)cc * kD] = S[cc];
+            } else if (ok) {
+                float* X = p.seg_x + ((bh * p.nseg + g) * 2 * kD + c0) * kD + i;
+#pragma unroll
+                for (int cc = 0; cc < kSlice; ++cc) X[(size_t)cc * kD] = S[cc];
             }
         } else if (warp < kWarpVn) {
             // ---- outputs: o_c = scale (e^{gcs} Q_c S_c^T + Aqk_c Vn_c), token row ----
@@ -1023,14 +1057,20 @@ __global__ void __launch_bounds__(st::kThreads, 1)
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&ms->o_done[c & 1]);
-                const int tt = c * kC + row;
-                if (tt < seq.len) {
+                const int tt = c * kC + row;  // token from the segment's start
+                if (tt < seq_left) {
                     const float eg = __expf(gcs_t) * rq_t;
                     float ov[kSlice];
 #pragma unroll
                     for (int cc = 0; cc < kSlice; ++cc)
                         ov[cc] = p.scale * fmaf(eg, __uint_as_float(pq[cc]), __uint_as_float(oi[cc]));
-                    store_row32(static_cast<TOut*>(p.o) + (((size_t)seq.start + tt) * p.Hv + h) * kD + c0, ov);
+                    const size_t orow = ((size_t)tok0 + tt) * p.Hv + h;
+                    if (g == 0)
+                        store_row32(static_cast<TOut*>(p.o) + orow * kD + c0, ov);
+                    else if (!aug)
+                        store_row32(p.seg_o + orow * kD + c0, ov);
+                    else
+                        store_row32(p.seg_r + orow * kD + (c0 - kD), ov);
                 }
             }
         } else {
@@ -1053,7 +1093,8 @@ __global__ void __launch_bounds__(st::kThreads, 1)
                 float u[kSlice];
 #pragma unroll
                 for (int q8 = 0; q8 < kSlice / 8; ++q8) {
-                    const uint4 raw = *reinterpret_cast<const uint4*>(stg + kU + sw64_chunk(row, q8));
+                    uint4 raw = make_uint4(0u, 0u, 0u, 0u);  // transition columns: zero values
+                    if (!aug) raw = *reinterpret_cast<const uint4*>(stg + kU + sw64_chunk(row, q8));
                     const T16* e = reinterpret_cast<const T16*>(&raw);
 #pragma unroll
                     for (int u8 = 0; u8 < 8; ++u8) u[q8 * 8 + u8] = Elem<T16>::to_f(e[u8]);
@@ -1101,6 +1142,200 @@ __global__ void __launch_bounds__(st::kThreads, 1)
 }
 
 // ===========================================================================
+// Segmented chain: linking the segments and correcting their outputs
+// ===========================================================================
+// Every state column evolves on its own and linearly in (its values, its initial column), so
+// a segment run from a zero state has the true end state S_zero_g + P_g S_start(g) and the
+// true outputs O_zero + R S_start(g), with P_g and R from the identity-started columns.
+
+// 16-byte asynchronous copies global -> shared (no register staging); a thread's copies
+// are complete after cp_wait<n> leaves at most n of its newest groups in flight.
+__device__ __forceinline__ void cp16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// S_start(1) = segment 0's end state; S_start(g + 1) = S_zero_g + P_g S_start(g).  One CTA
+// per (8 state columns j, v-head, sequence), thread = key row k; the starts of segments
+// 1 .. nseg-1 go to sst ([B][Hv][nseg][k][j], bf16: the correction's MMA operand), the last
+// segment's end state to the caller's state ([v][k] as everywhere else).  P_g (64 KiB, the
+// transition columns' end states, contiguous in seg_x) is double-buffered in shared memory:
+// P_{g+1} streams in while P_g is used.
+namespace seglink {
+constexpr int kSmem = 2 * kD * kD * 4 + kD * 8 * 4;
+}  // namespace seglink
+__global__ void __launch_bounds__(kD) gdn_seg_link_kernel(const float* __restrict__ seg_x,
+                                                          __nv_bfloat16* __restrict__ sst,
+                                                          float* __restrict__ state, int Hv, int nseg) {
+    extern __shared__ __align__(16) float lsm[];
+    float (*cur)[8] = reinterpret_cast<float (*)[8]>(lsm + 2 * kD * kD);  // S_start(g)[k'][j0 .. j0+7]
+    grid_dependency_wait();    // the state pass's end states (a programmatic dependent launch)
+    allow_dependent_launch();  // the correction kernel waits for this grid in turn
+    const int j0 = blockIdx.x * 8, h = blockIdx.y, b = blockIdx.z, k = threadIdx.x;
+    const size_t bh = (size_t)b * Hv + h;
+    auto fetch_P = [&](int g, int buf) {  // P_g^T (row kp = column kp's end state) -> buffer
+        const float4* src = reinterpret_cast<const float4*>(seg_x + ((bh * nseg + g) * 2 + 1) * kD * kD);
+        float4* dst = reinterpret_cast<float4*>(lsm + buf * kD * kD);
+#pragma unroll
+        for (int m = 0; m < kD * kD / 4 / kD; ++m) cp16(dst + m * kD + k, src + m * kD + k);
+        cp_commit();
+    };
+    fetch_P(1, 0);
+    const float* X0 = seg_x + bh * nseg * 2 * kD * kD;  // X^T rows v, columns k
+    float sv[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) sv[u] = X0[(size_t)(j0 + u) * kD + k];
+    for (int g = 1; g < nseg; ++g) {
+        const int buf = (g - 1) & 1;
+        if (g + 1 < nseg) fetch_P(g + 1, buf ^ 1);
+        else cp_commit();  // an empty group keeps the count: P_g is then the second newest
+        const float* Xg = seg_x + (bh * nseg + g) * 2 * kD * kD;
+        float acc[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) acc[u] = Xg[(size_t)(j0 + u) * kD + k];  // S_zero_g[k][j]
+#pragma unroll
+        for (int u = 0; u < 8; ++u) cur[k][u] = sv[u];
+        uint4 pk;
+        pk.x = Elem<__nv_bfloat16>::pack2(sv[0], sv[1]);
+        pk.y = Elem<__nv_bfloat16>::pack2(sv[2], sv[3]);
+        pk.z = Elem<__nv_bfloat16>::pack2(sv[4], sv[5]);
+        pk.w = Elem<__nv_bfloat16>::pack2(sv[6], sv[7]);
+        *reinterpret_cast<uint4*>(sst + ((bh * nseg + g) * kD + k) * kD + j0) = pk;
+        cp_wait<1>();
+        __syncthreads();  // every thread's copies of P_g and its row of cur are visible
+        const float* sP = lsm + buf * kD * kD;
+#pragma unroll 8
+        for (int kp = 0; kp < kD; ++kp) {
+            const float pk = sP[kp * kD + k];  // P_g[k][kp]
+            const float4 c0 = *reinterpret_cast<const float4*>(&cur[kp][0]);
+            const float4 c1 = *reinterpret_cast<const float4*>(&cur[kp][4]);
+            acc[0] = fmaf(pk, c0.x, acc[0]); acc[1] = fmaf(pk, c0.y, acc[1]);
+            acc[2] = fmaf(pk, c0.z, acc[2]); acc[3] = fmaf(pk, c0.w, acc[3]);
+            acc[4] = fmaf(pk, c1.x, acc[4]); acc[5] = fmaf(pk, c1.y, acc[5]);
+            acc[6] = fmaf(pk, c1.z, acc[6]); acc[7] = fmaf(pk, c1.w, acc[7]);
+        }
+        __syncthreads();  // this buffer and cur are rewritten next round
+#pragma unroll
+        for (int u = 0; u < 8; ++u) sv[u] = acc[u];
+    }
+    cp_wait<0>();
+#pragma unroll
+    for (int u = 0; u < 8; ++u) state[(bh * kD + j0 + u) * kD + k] = sv[u];
+}
+
+// o = O_zero + R S_start(g) for a tile of 128 tokens (two chunks) of a segment g >= 1 and one
+// v-head (dense sequences, T tokens each), on the tensor core: A = R (bf16 [token][k],
+// K-major, two 64-column boxes), B = S_start(g) (bf16 [k][j], MN-major, two 64-column boxes
+// 16 KiB apart), D = 128 lanes x 128 fp32 columns of TMEM; thread = token row then adds
+// O_zero (fp32) and stores.  Rows past the segment (an odd segment length) or past T are
+// computed but not stored.  128 threads; every wait is bounded.
+namespace segfix {
+constexpr int kThreads = 128;
+constexpr int kA = 0, kB = 32768, kBar = 65536;
+constexpr int kAlloc = kBar + 64 + 1024;
+}  // namespace segfix
+template <typename TOut>
+__global__ void __launch_bounds__(segfix::kThreads) gdn_seg_fix_kernel(const __grid_constant__ CUtensorMap tmR,
+                                                                       const __grid_constant__ CUtensorMap tmS,
+                                                                       const float* __restrict__ seg_o,
+                                                                       TOut* __restrict__ o, int T, int Hv,
+                                                                       int seg_len, int nseg) {
+    using namespace segfix;
+    extern __shared__ uint8_t xsm_raw[];
+    grid_dependency_wait();  // R, O_zero (state pass) and the segment starts (link kernel)
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(xsm_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bar_ld = reinterpret_cast<uint64_t*>(smem + kBar);
+    uint64_t* bar_mma = bar_ld + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_ld + 2);
+    volatile int* abort = reinterpret_cast<volatile int*>(bar_ld + 3);
+    const int h = blockIdx.y;
+    const int b = blockIdx.z / (nseg - 1);
+    const int g = 1 + blockIdx.z % (nseg - 1);
+    const int cs = g * seg_len;                                   // the segment's first chunk
+    const int c_end = min((g + 1) * seg_len, (T + kC - 1) / kC);  // one past its last
+    const int c_tile = cs + 2 * (int)blockIdx.x;                  // the tile's first chunk
+    if (c_tile >= c_end) return;
+    const int rows = min(2 * kC, min(c_end * kC, T) - c_tile * kC);  // tokens of the tile to store
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const size_t bh = (size_t)b * Hv + h;
+    if (tid == 0) {
+        mbar_init(bar_ld, 1);
+        mbar_init(bar_mma, 1);
+        *abort = 0;
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, 128);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    bool ok = true;
+    if (tid == 0) {
+        const int tok = b * T + c_tile * kC;
+        const int sg = (int)(bh * nseg + g);
+        mbar_arrive_expect_tx(bar_ld, 4 * 16384);
+        tma_load_4d(smem + kA, &tmR, bar_ld, 0, h, tok, 0);
+        tma_load_4d(smem + kA + 16384, &tmR, bar_ld, 64, h, tok, 0);
+        tma_load_3d(smem + kB, &tmS, bar_ld, 0, 0, sg);
+        tma_load_3d(smem + kB + 16384, &tmS, bar_ld, 64, 0, sg);
+        ok = mbar_wait(bar_ld, 0, abort, &g_err_gdn_prefill);
+        if (ok) {
+            tc_fence_after();
+            constexpr uint32_t idesc = make_idesc(Elem<__nv_bfloat16>::kFmt, 128, 128, false, true);
+            const uint64_t da = smem_desc(smem_u32(smem + kA), 16, 1024, kLayoutSW128);
+            const uint64_t db = smem_desc(smem_u32(smem + kB), 16384, 1024, kLayoutSW128);
+#pragma unroll
+            for (int kk = 0; kk < kD / 16; ++kk)
+                mma_f16_ss(tmem, da + (uint64_t)((((kk >> 2) * 16384) + (kk & 3) * 32) >> 4),
+                           db + (uint64_t)((kk * 2048) >> 4), idesc, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(bar_mma);  // also after a failed load wait: the epilogue's wait then ends
+    }
+    // (a load that timed out set the abort flag: then nothing is stored)
+    ok = __all_sync(0xffffffffu, mbar_wait(bar_mma, 0, abort, &g_err_gdn_prefill) && *abort == 0);
+    tc_fence_after();
+    const int r = tid;  // token row = TMEM lane
+    if (ok) {  // (warp-uniform: every lane takes part in the TMEM loads, only rows < rows store)
+        const bool live = r < rows;
+        const size_t row = ((size_t)b * T + (size_t)c_tile * kC + r) * Hv + h;
+        const float4* z = reinterpret_cast<const float4*>(seg_o + row * kD);
+        TOut* dst = o + row * kD;
+        const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+#pragma unroll
+        for (int cc = 0; cc < kD / 32; ++cc) {
+            uint32_t v[32];
+            tmem_ld32(tmem + lane_base + cc * 32, v);
+            tmem_ld_wait();
+            if (live) {
+                float ov[32];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const float4 zz = z[cc * 8 + q];
+                    ov[4 * q + 0] = __uint_as_float(v[4 * q + 0]) + zz.x;
+                    ov[4 * q + 1] = __uint_as_float(v[4 * q + 1]) + zz.y;
+                    ov[4 * q + 2] = __uint_as_float(v[4 * q + 2]) + zz.z;
+                    ov[4 * q + 3] = __uint_as_float(v[4 * q + 3]) + zz.w;
+                }
+                store_row32(dst + cc * 32, ov);
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 128);
+    }
+}
+
+// ===========================================================================
 // host side
 // ===========================================================================
 // Pre-processing options of the fused entry (A_log, dt_bias may be null)
@@ -1110,12 +1345,66 @@ struct Fuse {
     const float* dt_bias;
 };
 
+// The segmented chain (StateParams): segment length and count, and the workspace area of its
+// buffers (end states, fp32 outputs, segment starts).  nseg == 1: the plain chain.
+struct Seg {
+    int seg_len, nseg;
+    uint8_t* area;
+};
+
+// Segments pay when the plain chain leaves SMs idle (few sequences x v-heads, as on each GPU
+// of a multi-GPU split).  Costs are counted in chain steps (~1.2 us each): a state pass of
+// one wave costs its chain length plus ~4 steps of prologue and epilogue; a segmented plan
+// must fit in one wave (a second wave repays everything) and adds the link kernel (~1.5
+// steps a segment) and the output correction (~3 steps).  Packed sequences keep the plain
+// chain.
+Seg seg_plan(int B, int Hv, int nch, bool packed) {
+    Seg best{nch, 1, nullptr};
+    if (packed || nch < 8) return best;
+    const long long sms = device_sm_count();
+    const long long plain_ctas = (long long)B * Hv * (kD / kSlice);
+    double best_cost = (double)((plain_ctas + sms - 1) / sms) * (nch + 4);
+    for (int G = 2; G <= 8; G *= 2) {
+        const int L = (nch + G - 1) / G;
+        if (L < 4) break;
+        const int nseg = (nch + L - 1) / L;
+        if ((long long)B * nseg > 65535) break;
+        // segment 0: the usual 4 slice-CTAs a head; later segments 8 (the transition columns)
+        const long long ctas = (long long)B * Hv * (2LL * (kD / kSlice) * nseg - kD / kSlice);
+        if (ctas > sms) break;
+        const double cost = L + 4 + 1.5 * (nseg - 1) + 3;
+        if (cost < best_cost) {
+            best = Seg{L, nseg, nullptr};
+            best_cost = cost;
+        }
+    }
+    return best;
+}
+
+// The segment buffers, in this order: end states [B][Hv][nseg][256][128] fp32, zero-state
+// outputs [ntok][Hv][128] fp32, R [ntok][Hv][128] bf16, segment starts [B][Hv][nseg][128][128]
+// bf16.
+struct SegLayout {
+    size_t x, o, r, s, total;
+};
+SegLayout seg_layout(int nseg, int B, size_t ntok, int Hv) {
+    SegLayout L{};
+    if (nseg <= 1) return L;
+    L.x = 0;
+    L.o = align_up((size_t)B * Hv * nseg * 2 * kD * kD * 4, 1024);
+    L.r = L.o + align_up(ntok * Hv * kD * 4, 1024);
+    L.s = L.r + align_up(ntok * Hv * kD * 2, 1024);
+    L.total = L.s + align_up((size_t)B * Hv * nseg * kD * kD * 2, 1024);
+    return L;
+}
+size_t seg_bytes(const Seg& sg, int B, size_t ntok, int Hv) { return seg_layout(sg.nseg, B, ntok, Hv).total; }
+
 // Packed sequences: cu is the device [B+1] token-offset array and ntok its last entry; dense
 // B x T: cu = null, ntok = B * T.  T is the (longest) sequence length.
 template <typename T16, typename TOut>
 int launch(const void* q, const void* k, const void* v, const float* g_log, const float* beta,
            float* state, void* o, int B, int T, int Hqk, int Hv, int head_map, float scale,
-           void* ws, cudaStream_t stream, Fuse fuse, const int* cu, int ntok) {
+           void* ws, cudaStream_t stream, Fuse fuse, const int* cu, int ntok, Seg sg) {
     const int nch = (T + kC - 1) / kC;
     const size_t nbhc = (size_t)B * Hv * nch;
     const WsLayout L = ws_layout(nbhc);
@@ -1173,12 +1462,31 @@ int launch(const void* q, const void* k, const void* v, const float* g_log, cons
     sp.nch = nch;
     sp.head_map = head_map;
     sp.scale = scale;
+    sp.seg_len = sg.nseg > 1 ? sg.seg_len : nch;
+    sp.nseg = sg.nseg > 1 ? sg.nseg : 1;
+    const SegLayout SL = seg_layout(sp.nseg, B, (size_t)ntok, Hv);
+    float* seg_x = sp.nseg > 1 ? reinterpret_cast<float*>(sg.area + SL.x) : nullptr;
+    float* seg_o = sp.nseg > 1 ? reinterpret_cast<float*>(sg.area + SL.o) : nullptr;
+    __nv_bfloat16* seg_r = sp.nseg > 1 ? reinterpret_cast<__nv_bfloat16*>(sg.area + SL.r) : nullptr;
+    __nv_bfloat16* seg_s = sp.nseg > 1 ? reinterpret_cast<__nv_bfloat16*>(sg.area + SL.s) : nullptr;
+    CUtensorMap tr, tss;
+    if (sp.nseg > 1) {
+        if ((rc = make_tmap_4d(&tr, seg_r, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, kD, Hv, ntok, 1, 64, 1, 2 * kC,
+                               CU_TENSOR_MAP_SWIZZLE_128B)))
+            return rc;
+        if ((rc = make_tmap_3d(&tss, seg_s, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, kD, kD, (uint64_t)B * Hv * sp.nseg,
+                               64, kD, CU_TENSOR_MAP_SWIZZLE_128B)))
+            return rc;
+    }
+    sp.seg_x = seg_x;
+    sp.seg_o = seg_o;
+    sp.seg_r = seg_r;
     auto k2 = fuse.on ? gdn_state_kernel<T16, TOut, true> : gdn_state_kernel<T16, TOut, false>;
     B200_TRY_CUDA(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, st::kAlloc));
     // launched with programmatic stream serialisation: its prologue (barriers, TMEM, the
     // initial state) overlaps the prep grid's last CTAs
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(kD / kSlice, Hv, B);
+    cfg.gridDim = dim3(sp.nseg > 1 ? 2 * kD / kSlice : kD / kSlice, Hv, B * sp.nseg);
     cfg.blockDim = dim3(st::kThreads);
     cfg.dynamicSmemBytes = st::kAlloc;
     cfg.stream = stream;
@@ -1189,7 +1497,36 @@ int launch(const void* q, const void* k, const void* v, const float* g_log, cons
     cfg.numAttrs = 1;
     B200_TRY_CUDA(cudaLaunchKernelEx(&cfg, k2, tq, tk, tw, ta, tm, tus, sp));
     count_launch(2);
-    return cudaGetLastError() == cudaSuccess ? B200LAB_OK : B200LAB_ERR_CUDA;
+    B200_TRY_CUDA(cudaGetLastError());
+    if (sp.nseg > 1) {
+        // both as programmatic dependents of the kernel before them (each waits for it with
+        // griddepcontrol.wait before reading its results), so their launches overlap its drain
+        B200_TRY_CUDA(cudaFuncSetAttribute(gdn_seg_link_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           seglink::kSmem));
+        cudaLaunchConfig_t lc = {};
+        lc.gridDim = dim3(kD / 8, Hv, B);
+        lc.blockDim = dim3(kD);
+        lc.dynamicSmemBytes = seglink::kSmem;
+        lc.stream = stream;
+        lc.attrs = attr;
+        lc.numAttrs = 1;
+        B200_TRY_CUDA(cudaLaunchKernelEx(&lc, gdn_seg_link_kernel, (const float*)seg_x, seg_s, state, Hv, sp.nseg));
+        B200_TRY_CUDA(cudaGetLastError());
+        auto k4 = gdn_seg_fix_kernel<TOut>;
+        B200_TRY_CUDA(cudaFuncSetAttribute(k4, cudaFuncAttributeMaxDynamicSharedMemorySize, segfix::kAlloc));
+        cudaLaunchConfig_t fc = {};
+        fc.gridDim = dim3((sp.seg_len + 1) / 2, Hv, B * (sp.nseg - 1));
+        fc.blockDim = dim3(segfix::kThreads);
+        fc.dynamicSmemBytes = segfix::kAlloc;
+        fc.stream = stream;
+        fc.attrs = attr;
+        fc.numAttrs = 1;
+        B200_TRY_CUDA(cudaLaunchKernelEx(&fc, k4, tr, tss, (const float*)seg_o, static_cast<TOut*>(o), T, Hv,
+                                         sp.seg_len, sp.nseg));
+        count_launch(2);
+        B200_TRY_CUDA(cudaGetLastError());
+    }
+    return B200LAB_OK;
 }
 
 // fp32 q / k / v: one pass converts them to bf16 copies in the workspace, which the chunked
@@ -1224,15 +1561,15 @@ size_t f32_copy_bytes(size_t ntok, int Hqk, int Hv) {
 template <typename T16>
 int dispatch_out(int out_dtype, const void* q, const void* k, const void* v, const float* g,
                  const float* be, float* state, void* o, int B, int T, int Hqk, int Hv, int hm,
-                 float scale, void* ws, cudaStream_t s, Fuse f, const int* cu, int ntok) {
+                 float scale, void* ws, cudaStream_t s, Fuse f, const int* cu, int ntok, Seg sg) {
     switch (out_dtype) {
         case B200LAB_F16:
-            return launch<T16, __half>(q, k, v, g, be, state, o, B, T, Hqk, Hv, hm, scale, ws, s, f, cu, ntok);
+            return launch<T16, __half>(q, k, v, g, be, state, o, B, T, Hqk, Hv, hm, scale, ws, s, f, cu, ntok, sg);
         case B200LAB_BF16:
             return launch<T16, __nv_bfloat16>(q, k, v, g, be, state, o, B, T, Hqk, Hv, hm, scale, ws, s, f, cu,
-                                              ntok);
+                                              ntok, sg);
         case B200LAB_F32:
-            return launch<T16, float>(q, k, v, g, be, state, o, B, T, Hqk, Hv, hm, scale, ws, s, f, cu, ntok);
+            return launch<T16, float>(q, k, v, g, be, state, o, B, T, Hqk, Hv, hm, scale, ws, s, f, cu, ntok, sg);
     }
     return B200LAB_ERR_UNSUPPORTED;
 }
@@ -1244,19 +1581,46 @@ bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p
 
 B200_DEFINE_ERR_TAKER(gdn_prefill, b200::g_err_gdn_prefill)
 
+namespace b200 {
+namespace {
+// the chunk items of the prep pass (the smallest workspace the entries accept, with the fp32
+// copies for fp32 inputs); the segmented chain's buffers follow them
+size_t prefill_base_bytes(int B, int T, int Hv) {
+    if (B < 1 || T < 1 || Hv < 1) return 0;
+    const size_t nch = ((size_t)T + kC - 1) / kC;
+    return ws_layout((size_t)B * Hv * nch).total;
+}
+size_t prefill_min_bytes(int B, int T, int Hqk, int Hv, int in_dtype) {
+    const size_t base = prefill_base_bytes(B, T, Hv);
+    if (base == 0 || in_dtype != B200LAB_F32 || Hqk < 1) return base;
+    return base + f32_copy_bytes((size_t)B * T, Hqk, Hv);
+}
+size_t prefill_seg_bytes(int B, int T, int Hv) {
+    if (B < 1 || T < 1 || Hv < 1) return 0;
+    const int nch = (T + kC - 1) / kC;
+    return seg_bytes(seg_plan(B, Hv, nch, false), B, (size_t)B * T, Hv);
+}
+}  // namespace
+}  // namespace b200
+
 extern "C" size_t gdn_prefill_sm100_workspace(int B, int T, int Hqk, int Hv, int dk, int dv) {
-    (void)Hqk;
     (void)dk;
     (void)dv;
-    if (B < 1 || T < 1 || Hv < 1) return 0;
-    const size_t nch = ((size_t)T + b200::kC - 1) / b200::kC;
-    return b200::ws_layout((size_t)B * Hv * nch).total;
+    const size_t base = b200::prefill_min_bytes(B, T, Hqk, Hv, B200LAB_BF16);
+    return base == 0 ? 0 : base + b200::prefill_seg_bytes(B, T, Hv);
 }
 
 extern "C" size_t gdn_prefill_sm100_workspace_ex(int B, int T, int Hqk, int Hv, int dk, int dv, int in_dtype) {
-    const size_t base = gdn_prefill_sm100_workspace(B, T, Hqk, Hv, dk, dv);
-    if (base == 0 || in_dtype != B200LAB_F32 || Hqk < 1) return base;
-    return base + b200::f32_copy_bytes((size_t)B * T, Hqk, Hv);
+    (void)dk;
+    (void)dv;
+    const size_t base = b200::prefill_min_bytes(B, T, Hqk, Hv, in_dtype);
+    return base == 0 ? 0 : base + b200::prefill_seg_bytes(B, T, Hv);
+}
+
+extern "C" size_t gdn_prefill_sm100_workspace_min(int B, int T, int Hqk, int Hv, int dk, int dv, int in_dtype) {
+    (void)dk;
+    (void)dv;
+    return b200::prefill_min_bytes(B, T, Hqk, Hv, in_dtype);
 }
 
 namespace b200 {
@@ -1282,15 +1646,20 @@ int prefill_entry(const void* q, const void* k, const void* v, const float* g_lo
         return B200LAB_ERR_INVALID;
     // fp32 inputs: the bf16 copies are sized by B * max_seqlen tokens, which bounds total_tokens
     if (in_dtype == B200LAB_F32 && cu && (long long)ntok > (long long)B * T) return B200LAB_ERR_INVALID;
-    const size_t need = gdn_prefill_sm100_workspace_ex(B, T, Hqk, Hv, dk, dv, in_dtype);
+    // the chunk items (and fp32 copies) are required; the segmented chain's buffers are used
+    // when the workspace also holds them (the size gdn_prefill_sm100_workspace reports)
+    const size_t need = prefill_min_bytes(B, T, Hqk, Hv, in_dtype);
     if (!workspace || ws_bytes < need || !aligned(workspace, 256)) return B200LAB_ERR_WORKSPACE;
     int rc = check_device_sm100();
     if (rc != B200LAB_OK) return rc;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (!cu) ntok = B * T;
+    Seg sg = seg_plan(B, Hv, (T + kC - 1) / kC, cu != nullptr);
+    if (ws_bytes - need < seg_bytes(sg, B, (size_t)ntok, Hv)) sg = Seg{(T + kC - 1) / kC, 1, nullptr};
+    sg.area = static_cast<uint8_t*>(workspace) + need;
     if (in_dtype == B200LAB_F32) {
         // bf16 copies after the chunk items, then the 16-bit path on them
-        uint8_t* conv = static_cast<uint8_t*>(workspace) + gdn_prefill_sm100_workspace(B, T, Hqk, Hv, dk, dv);
+        uint8_t* conv = static_cast<uint8_t*>(workspace) + prefill_base_bytes(B, T, Hv);
         const size_t nqk = (size_t)ntok * Hqk * kD, nv = (size_t)ntok * Hv * kD;
         F32Copies cp;
         cp.src[0] = static_cast<const float*>(q);
@@ -1307,13 +1676,13 @@ int prefill_entry(const void* q, const void* k, const void* v, const float* g_lo
         B200_TRY_CUDA(cudaGetLastError());
         count_launch(1);
         return dispatch_out<__nv_bfloat16>(out_dtype, cp.dst[0], cp.dst[1], cp.dst[2], g_log, beta, state, o, B,
-                                           T, Hqk, Hv, head_map, scale, workspace, s, fuse, cu, ntok);
+                                           T, Hqk, Hv, head_map, scale, workspace, s, fuse, cu, ntok, sg);
     }
     if (in_dtype == B200LAB_BF16)
         return dispatch_out<__nv_bfloat16>(out_dtype, q, k, v, g_log, beta, state, o, B, T, Hqk, Hv,
-                                           head_map, scale, workspace, s, fuse, cu, ntok);
+                                           head_map, scale, workspace, s, fuse, cu, ntok, sg);
     return dispatch_out<__half>(out_dtype, q, k, v, g_log, beta, state, o, B, T, Hqk, Hv, head_map,
-                                scale, workspace, s, fuse, cu, ntok);
+                                scale, workspace, s, fuse, cu, ntok, sg);
 }
 }  // namespace
 }  // namespace b200
