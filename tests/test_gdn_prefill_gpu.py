@@ -190,3 +190,15 @@ def test_segmented_prefill_then_decode(cuda):
                                         np.zeros((B, Hv, 128, 128)), 1.0 / np.sqrt(128), 0)
     assert_close(to_np(o), o_ref[:, T], "decode after segmented prefill")
     assert_close(to_np(S), S_ref, "state")
+
+
+def test_segmented_chain_fp32_inputs(cuda):
+    """fp32 q/k/v on a segmented shape: the bf16 copies sit between the chunk items and the
+    segment buffers in the workspace."""
+    B, T, Hqk, Hv = 1, 1000, 2, 4
+    assert b200lab.gdn_prefill_workspace_bytes(B, T, Hqk, Hv, in_dtype=b200lab.F32) > \
+        b200lab.gdn_prefill_workspace_min_bytes(B, T, Hqk, Hv, in_dtype=b200lab.F32)
+    o, S, o_ref, S_ref = _case(B, T, Hqk, Hv, dtype=torch.float32, out_dtype=torch.float32,
+                               state_std=0.05, seed=77)
+    assert_close(o, o_ref, "segmented fp32-in out")
+    assert_close(S, S_ref, "segmented fp32-in state")
