@@ -785,7 +785,8 @@ __device__ __forceinline__ void store_row32(TOut* dst, const float (&v)[32]) {
     }
 }
 
-template <typename T16, typename TOut, bool kFused>
+// kSeg: the segmented chain (StateParams); the plain instantiation compiles without any of it
+template <typename T16, typename TOut, bool kFused, bool kSeg>
 __global__ void __launch_bounds__(st::kThreads, 1)
     gdn_state_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmAqk,
@@ -800,19 +801,19 @@ __global__ void __launch_bounds__(st::kThreads, 1)
 
     const int slice = blockIdx.x;
     const int h = blockIdx.y;
-    const int b = blockIdx.z / p.nseg;
-    const int g = blockIdx.z % p.nseg;          // segment
-    const bool aug = slice >= kD / kSlice;      // transition columns of a later segment
+    const int b = kSeg ? (int)blockIdx.z / p.nseg : (int)blockIdx.z;
+    const int g = kSeg ? (int)blockIdx.z % p.nseg : 0;  // segment
+    const bool aug = kSeg && slice >= kD / kSlice;      // transition columns of a later segment
     if (aug && g == 0) return;
     const SeqSpan seq = seq_span(p.cu, p.T, b);
     if (!seq_ok(seq, p.T, p.ntok)) return;    // recorded by the prep grid; state left as it is
-    const int cs = g * p.seg_len;             // the segment's first chunk
-    // this segment's chunks (the sequence's chunks, p.nch for the longest, when nseg == 1)
-    const int nch = min(p.seg_len, (seq.len + kC - 1) / kC - cs);
+    const int cs = kSeg ? g * p.seg_len : 0;  // the segment's first chunk
+    // this segment's chunks (the sequence's chunks, p.nch for the longest, when plain)
+    const int nch = kSeg ? min(p.seg_len, (seq.len + kC - 1) / kC - cs) : (seq.len + kC - 1) / kC;
     if (nch <= 0) return;                     // an empty sequence: its state stays as it is
     // segmented: the link kernel, launched as a programmatic dependent, may be scheduled now
     // (it waits for this grid to complete before reading the end states)
-    if (p.nseg > 1) allow_dependent_launch();
+    if constexpr (kSeg) allow_dependent_launch();
     const int tok0 = seq.start + cs * kC;     // the segment's first token
     const int seq_left = seq.len - cs * kC;   // tokens of the sequence from there on
     const int c0 = slice * kSlice;
@@ -1026,7 +1027,7 @@ __global__ void __launch_bounds__(st::kThreads, 1)
                     publish_S(c + 1);
                 }
             }
-            if (ok && p.nseg == 1) {
+            if (ok && !kSeg) {
 #pragma unroll
                 for (int cc = 0; cc < kSlice; ++cc) Sg[(size_t)cc * kD] = S[cc];
             } else if (ok) {
@@ -1481,7 +1482,8 @@ int launch(const void* q, const void* k, const void* v, const float* g_log, cons
     sp.seg_x = seg_x;
     sp.seg_o = seg_o;
     sp.seg_r = seg_r;
-    auto k2 = fuse.on ? gdn_state_kernel<T16, TOut, true> : gdn_state_kernel<T16, TOut, false>;
+    auto k2 = sp.nseg > 1 ? (fuse.on ? gdn_state_kernel<T16, TOut, true, true> : gdn_state_kernel<T16, TOut, false, true>)
+                          : (fuse.on ? gdn_state_kernel<T16, TOut, true, false> : gdn_state_kernel<T16, TOut, false, false>);
     B200_TRY_CUDA(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, st::kAlloc));
     // launched with programmatic stream serialisation: its prologue (barriers, TMEM, the
     // initial state) overlaps the prep grid's last CTAs
