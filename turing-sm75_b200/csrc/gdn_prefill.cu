@@ -1161,28 +1161,35 @@ __device__ __forceinline__ void cp_wait() {
 }
 
 // S_start(1) = segment 0's end state; S_start(g + 1) = S_zero_g + P_g S_start(g).  One CTA
-// per (8 state columns j, v-head, sequence), thread = key row k; the starts of segments
+// per (8 state columns j, v-head, sequence) of 256 threads: key row k = tid % 128, and the
+// two halves of the threads take the product's inner index kp in [0, 64) and [64, 128),
+// their sums added through shared memory; packed f32x2 FMAs.  The starts of segments
 // 1 .. nseg-1 go to sst ([B][Hv][nseg][k][j], bf16: the correction's MMA operand), the last
 // segment's end state to the caller's state ([v][k] as everywhere else).  P_g (64 KiB, the
 // transition columns' end states, contiguous in seg_x) is double-buffered in shared memory:
 // P_{g+1} streams in while P_g is used.
 namespace seglink {
-constexpr int kSmem = 2 * kD * kD * 4 + kD * 8 * 4;
+constexpr int kThreads = 2 * kD;
+constexpr int kSmem = 2 * kD * kD * 4 + kD * 8 * 4 + kD * 8 * 4;
 }  // namespace seglink
-__global__ void __launch_bounds__(kD) gdn_seg_link_kernel(const float* __restrict__ seg_x,
-                                                          __nv_bfloat16* __restrict__ sst,
-                                                          float* __restrict__ state, int Hv, int nseg) {
+__global__ void __launch_bounds__(seglink::kThreads) gdn_seg_link_kernel(const float* __restrict__ seg_x,
+                                                                         __nv_bfloat16* __restrict__ sst,
+                                                                         float* __restrict__ state, int Hv,
+                                                                         int nseg) {
     extern __shared__ __align__(16) float lsm[];
-    float (*cur)[8] = reinterpret_cast<float (*)[8]>(lsm + 2 * kD * kD);  // S_start(g)[k'][j0 .. j0+7]
+    float (*cur)[8] = reinterpret_cast<float (*)[8]>(lsm + 2 * kD * kD);          // S_start(g)[k'][j0 ..]
+    float (*part)[8] = reinterpret_cast<float (*)[8]>(lsm + 2 * kD * kD + kD * 8);  // second half's sums
     grid_dependency_wait();    // the state pass's end states (a programmatic dependent launch)
     allow_dependent_launch();  // the correction kernel waits for this grid in turn
-    const int j0 = blockIdx.x * 8, h = blockIdx.y, b = blockIdx.z, k = threadIdx.x;
+    const int j0 = blockIdx.x * 8, h = blockIdx.y, b = blockIdx.z;
+    const int tid = threadIdx.x, k = tid & (kD - 1), half = tid >> 7;
     const size_t bh = (size_t)b * Hv + h;
     auto fetch_P = [&](int g, int buf) {  // P_g^T (row kp = column kp's end state) -> buffer
         const float4* src = reinterpret_cast<const float4*>(seg_x + ((bh * nseg + g) * 2 + 1) * kD * kD);
         float4* dst = reinterpret_cast<float4*>(lsm + buf * kD * kD);
 #pragma unroll
-        for (int m = 0; m < kD * kD / 4 / kD; ++m) cp16(dst + m * kD + k, src + m * kD + k);
+        for (int m = 0; m < kD * kD / 4 / seglink::kThreads; ++m)
+            cp16(dst + m * seglink::kThreads + tid, src + m * seglink::kThreads + tid);
         cp_commit();
     };
     fetch_P(1, 0);
@@ -1195,37 +1202,58 @@ __global__ void __launch_bounds__(kD) gdn_seg_link_kernel(const float* __restric
         if (g + 1 < nseg) fetch_P(g + 1, buf ^ 1);
         else cp_commit();  // an empty group keeps the count: P_g is then the second newest
         const float* Xg = seg_x + (bh * nseg + g) * 2 * kD * kD;
-        float acc[8];
+        float2 acc[4];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) acc[u] = Xg[(size_t)(j0 + u) * kD + k];  // S_zero_g[k][j]
+        for (int u = 0; u < 4; ++u) acc[u] = make_float2(0.f, 0.f);
+        if (half == 0) {
 #pragma unroll
-        for (int u = 0; u < 8; ++u) cur[k][u] = sv[u];
-        uint4 pk;
-        pk.x = Elem<__nv_bfloat16>::pack2(sv[0], sv[1]);
-        pk.y = Elem<__nv_bfloat16>::pack2(sv[2], sv[3]);
-        pk.z = Elem<__nv_bfloat16>::pack2(sv[4], sv[5]);
-        pk.w = Elem<__nv_bfloat16>::pack2(sv[6], sv[7]);
-        *reinterpret_cast<uint4*>(sst + ((bh * nseg + g) * kD + k) * kD + j0) = pk;
+            for (int u = 0; u < 4; ++u)  // S_zero_g[k][j]
+                acc[u] = make_float2(Xg[(size_t)(j0 + 2 * u) * kD + k], Xg[(size_t)(j0 + 2 * u + 1) * kD + k]);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) cur[k][u] = sv[u];
+            uint4 pk;
+            pk.x = Elem<__nv_bfloat16>::pack2(sv[0], sv[1]);
+            pk.y = Elem<__nv_bfloat16>::pack2(sv[2], sv[3]);
+            pk.z = Elem<__nv_bfloat16>::pack2(sv[4], sv[5]);
+            pk.w = Elem<__nv_bfloat16>::pack2(sv[6], sv[7]);
+            *reinterpret_cast<uint4*>(sst + ((bh * nseg + g) * kD + k) * kD + j0) = pk;
+        }
         cp_wait<1>();
-        __syncthreads();  // every thread's copies of P_g and its row of cur are visible
+        __syncthreads();  // every thread's copies of P_g and the rows of cur are visible
         const float* sP = lsm + buf * kD * kD;
+        const int kp0 = half * (kD / 2);
 #pragma unroll 8
-        for (int kp = 0; kp < kD; ++kp) {
+        for (int kp = kp0; kp < kp0 + kD / 2; ++kp) {
             const float pk = sP[kp * kD + k];  // P_g[k][kp]
+            const float2 p2 = make_float2(pk, pk);
             const float4 c0 = *reinterpret_cast<const float4*>(&cur[kp][0]);
             const float4 c1 = *reinterpret_cast<const float4*>(&cur[kp][4]);
-            acc[0] = fmaf(pk, c0.x, acc[0]); acc[1] = fmaf(pk, c0.y, acc[1]);
-            acc[2] = fmaf(pk, c0.z, acc[2]); acc[3] = fmaf(pk, c0.w, acc[3]);
-            acc[4] = fmaf(pk, c1.x, acc[4]); acc[5] = fmaf(pk, c1.y, acc[5]);
-            acc[6] = fmaf(pk, c1.z, acc[6]); acc[7] = fmaf(pk, c1.w, acc[7]);
+            acc[0] = __ffma2_rn(p2, make_float2(c0.x, c0.y), acc[0]);
+            acc[1] = __ffma2_rn(p2, make_float2(c0.z, c0.w), acc[1]);
+            acc[2] = __ffma2_rn(p2, make_float2(c1.x, c1.y), acc[2]);
+            acc[3] = __ffma2_rn(p2, make_float2(c1.z, c1.w), acc[3]);
         }
-        __syncthreads();  // this buffer and cur are rewritten next round
+        if (half == 1) {
 #pragma unroll
-        for (int u = 0; u < 8; ++u) sv[u] = acc[u];
+            for (int u = 0; u < 4; ++u) {
+                part[k][2 * u] = acc[u].x;
+                part[k][2 * u + 1] = acc[u].y;
+            }
+        }
+        __syncthreads();  // the second half's sums are in; this buffer and cur are rewritten next
+        if (half == 0) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                sv[2 * u] = acc[u].x + part[k][2 * u];
+                sv[2 * u + 1] = acc[u].y + part[k][2 * u + 1];
+            }
+        }
     }
     cp_wait<0>();
+    if (half == 0) {
 #pragma unroll
-    for (int u = 0; u < 8; ++u) state[(bh * kD + j0 + u) * kD + k] = sv[u];
+        for (int u = 0; u < 8; ++u) state[(bh * kD + j0 + u) * kD + k] = sv[u];
+    }
 }
 
 // o = O_zero + R S_start(g) for a tile of 128 tokens (two chunks) of a segment g >= 1 and one
@@ -1299,14 +1327,18 @@ __global__ void __launch_bounds__(segfix::kThreads) gdn_seg_fix_kernel(const __g
         }
         mma_commit(bar_mma);  // also after a failed load wait: the epilogue's wait then ends
     }
+    // this thread's O_zero row (token row = TMEM lane), every load issued while the MMAs run
+    const int r = tid;
+    const bool live = r < rows;
+    const size_t row = ((size_t)b * T + (size_t)c_tile * kC + r) * Hv + h;
+    float4 zr[kD / 4];
+#pragma unroll
+    for (int q = 0; q < kD / 4; ++q)
+        zr[q] = live ? reinterpret_cast<const float4*>(seg_o + row * kD)[q] : make_float4(0.f, 0.f, 0.f, 0.f);
     // (a load that timed out set the abort flag: then nothing is stored)
     ok = __all_sync(0xffffffffu, mbar_wait(bar_mma, 0, abort, &g_err_gdn_prefill) && *abort == 0);
     tc_fence_after();
-    const int r = tid;  // token row = TMEM lane
     if (ok) {  // (warp-uniform: every lane takes part in the TMEM loads, only rows < rows store)
-        const bool live = r < rows;
-        const size_t row = ((size_t)b * T + (size_t)c_tile * kC + r) * Hv + h;
-        const float4* z = reinterpret_cast<const float4*>(seg_o + row * kD);
         TOut* dst = o + row * kD;
         const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
 #pragma unroll
@@ -1318,7 +1350,7 @@ __global__ void __launch_bounds__(segfix::kThreads) gdn_seg_fix_kernel(const __g
                 float ov[32];
 #pragma unroll
                 for (int q = 0; q < 8; ++q) {
-                    const float4 zz = z[cc * 8 + q];
+                    const float4 zz = zr[cc * 8 + q];
                     ov[4 * q + 0] = __uint_as_float(v[4 * q + 0]) + zz.x;
                     ov[4 * q + 1] = __uint_as_float(v[4 * q + 1]) + zz.y;
                     ov[4 * q + 2] = __uint_as_float(v[4 * q + 2]) + zz.z;
@@ -1507,7 +1539,7 @@ int launch(const void* q, const void* k, const void* v, const float* g_log, cons
                                            seglink::kSmem));
         cudaLaunchConfig_t lc = {};
         lc.gridDim = dim3(kD / 8, Hv, B);
-        lc.blockDim = dim3(kD);
+        lc.blockDim = dim3(seglink::kThreads);
         lc.dynamicSmemBytes = seglink::kSmem;
         lc.stream = stream;
         lc.attrs = attr;
