@@ -684,13 +684,16 @@ def bench_gdn_prefill(cfg, args, dist, peaks, fused=False):
                      "includes": "all_gather_into_tensor + head permute"}
         del full
     wl = "gdn_prefill_c3" + ("_fused" if fused else "")
+    traffic = _scaled(profile_traffic(wl), Hv_l / Hv)
+    if cfg.get("custom"):  # a shape of its own: the C3 summaries do not describe it
+        wl, traffic = wl.replace("_c3", "") + "_custom", None
     res = {"metric": "GDN prefill tok/s", "value": T / (ms * 1e-3), "unit": "tok/s",
            "us_per_step": ms * 1e3,
            "config": {"workload": wl, "B": 1, "T": T, "Hqk": Hqk, "Hv": Hv, "d": d,
                       "chunk": 64, "sharding": "v-heads", "l2": "L2 flushed between launches"},
            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                         "frac": achieved / peaks["hbm_gbs"],
-                        "traffic": _scaled(profile_traffic(wl), Hv_l / Hv),
+                        "traffic": traffic,
                         "tensor_tflops": flops_local / (ms_local * 1e-3) / 1e12},
            "gpu_launches": int(launches), "clocks": clk.summary()}
     if allgather:
@@ -839,6 +842,9 @@ def run_ours(args):
         # smaller instance of the same kernel, for ncu captures that must stay small
         cfg["B"], cfg["Hq"], cfg["Hkv"], cfg["S"], cfg["D"] = (int(x) for x in args.attn_shape.split(","))
         name = name + "_custom"
+    if args.gdn_shape:
+        cfg["T"], cfg["Hqk"], cfg["Hv"] = (int(x) for x in args.gdn_shape.split(","))
+        cfg["custom"] = True
     if name in ATTN_CASES and name != "attn_c1":
         main = bench_attn_case(name, ATTN_CASES[name], args, dist, peaks)
     elif name.startswith("attn_gated"):
@@ -949,6 +955,9 @@ def main():
     ap.add_argument("--no-secondary", dest="secondary", action="store_false")
     ap.add_argument("--attn-shape", default=None, metavar="B,Hq,Hkv,S,D",
                     help="override the attention shape (profiling a smaller case)")
+    ap.add_argument("--gdn-shape", default=None, metavar="T,Hqk,Hv",
+                    help="override the GDN prefill shape (e.g. one GPU's share of C3 on 8 GPUs: "
+                         "4096,2,4)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline legs")
     ap.add_argument("--cpu-budget-s", type=float, default=60.0,
                     help="approximate CPU seconds for the reference arm / cpu_baseline")
