@@ -556,8 +556,9 @@ def bench_gdn_decode(cfg, args, dist, peaks, state_dtype=None, weak=False):
     dist.barrier()
     torch.cuda.synchronize()
     n0 = b200lab.launch_count()
-    if ssz == 4:
-        # the fp32 state (134 MB at N=1) is larger than L2: 256 steps back to back
+    state_bytes = state.numel() * ssz
+    if state_bytes > 126e6:
+        # a state larger than L2 (fp32 at 64 sequences: 134 MB): 256 steps back to back
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with ClockSampler(dev) as clk:
             e0.record(stream)
@@ -566,8 +567,8 @@ def bench_gdn_decode(cfg, args, dist, peaks, state_dtype=None, weak=False):
             torch.cuda.synchronize()
         ms_local = e0.elapsed_time(e1) / T
     else:
-        # a 16-bit state (67 MB at N=1) would stay in L2 between steps: flush L2 before
-        # every step and time each step alone
+        # a state that fits in L2 (16-bit, or a GPU's share of the sequences) would stay there
+        # between steps: flush L2 before every step and time each step alone
         flush = L2Flush(dev)
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                for _ in range(T)]
@@ -595,8 +596,9 @@ def bench_gdn_decode(cfg, args, dist, peaks, state_dtype=None, weak=False):
                       "B": Bl * dist.world if weak else cfg["B"], "Hqk": Hqk, "Hv": Hv, "d": d,
                       "state": f"{sname} [B,Hv,128,128] in place",
                       "sharding": f"sequences, {Bl} per GPU (weak scaling)" if weak else "sequences",
-                      "l2": "state larger than L2 (134 MB at N=1), 256 consecutive steps" if ssz == 4
-                      else "L2 flushed before every step (16-bit state 67 MB at N=1)"},
+                      "l2": f"state larger than L2 ({state_bytes / 1e6:.0f} MB a GPU), 256 consecutive steps"
+                      if state_bytes > 126e6
+                      else f"L2 flushed before every step (state {state_bytes / 1e6:.0f} MB a GPU)"},
            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                         "frac": achieved / peaks["hbm_gbs"], "traffic": traffic},
            "gpu_launches": int(launches), "clocks": clk.summary()}
@@ -871,8 +873,11 @@ def run_ours(args):
                 ("attn_gated_d256", bench_gated_attention, workloads.CONFIGS["attn_gated_d256"]),
                 ("gdn_prefill", bench_gdn_prefill, workloads.CONFIGS["gdn_prefill_c3"]),
                 ("gdn_prefill_fused", fused, workloads.CONFIGS["gdn_prefill_c3"])]
-        if dist.world > 1:  # at N = 1 the weak-scaling decode is the gdn_decode line itself
+        if dist.world > 1:  # at N = 1 the weak-scaling decodes are the decode lines themselves
             todo.insert(1, ("gdn_decode_weak", weak, workloads.CONFIGS["gdn_decode_c4"]))
+            weak16 = lambda c, a, d_, p: bench_gdn_decode(c, a, d_, p, state_dtype=torch.float16,  # noqa: E731
+                                                          weak=True)
+            todo.insert(3, ("gdn_decode_state16_weak", weak16, workloads.CONFIGS["gdn_decode_c4"]))
         for key, shp in ATTN_CASES.items():
             todo.append((key, lambda c, a, d_, p, key=key: bench_attn_case(key, c, a, d_, p), shp))
         for key, fn, c in todo:
