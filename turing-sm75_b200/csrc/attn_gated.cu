@@ -8,26 +8,26 @@
 // and the gate after the softmax are the model's gated-attention layer (24 q-heads / 4
 // kv-heads, head dim 256, docs/qwen38-27b.md:13), which the reference does not build.
 //
-// Design: one CTA per (128-row query tile, q-head, batch), 192 threads.
-//   TMEM (512 columns): S in two 64-column buffers (64 keys a tile), O in 256, and Q in
-//   128 (copied there once by the softmax warps, so QK^T reads only K from shared memory).
-//   Two query tiles would need 768 columns, so the overlap comes from S instead: the
-//   tensor core computes S(j+1) while the softmax works on S(j), and PV(j) runs as soon
-//   as P(j) is in TMEM.  Per 64-key tile the tensor work (QK^T and PV, 8.4 MFLOP) is
-//   ~1320 cycles (the N = 64 QK^T instructions run at two thirds of the full rate)
-//   against ~1000 of softmax.
-//   warp 4: TMA producer (Q once; K(0), K(1); then per tile the stage {V(j), K(j+2)} into
-//           slot j & 1 of two rings of 128-byte-swizzled 64-column boxes).
-//   warp 5: TMEM owner and MMA issuer: QK(0), QK(1), then per tile PV(j), QK(j+2).
+// Design: one CTA per (128-row query tile, q-head, batch), 192 threads, 128-key tiles.
+//   TMEM (512 columns): S in two 128-column buffers, O in 256.  Q, K and V sit in shared
+//   memory (64 KiB each, one slot each); both QK^T operands come from shared memory, so the
+//   QK^T products run at N = 128 (the full rate; 64-key tiles with Q in TMEM ran them at
+//   N = 64, two thirds of it).  Two query tiles would need 768 TMEM columns, so the overlap
+//   comes from S: the tensor core computes S(j+1) while the softmax works on S(j), then
+//   PV(j).  Per key tile: QK^T and PV 16.8 MFLOP, ~2048 cycles of tensor work.
+//   warp 4: TMA producer -- lane 0: Q once, then K(j) as soon as QK(j-1) has read K(j-1);
+//           lane 1: V(j) as soon as PV(j-1) has read V(j-1) (128-byte-swizzled 64-column
+//           boxes of 128 rows).
+//   warp 5: TMEM owner and MMA issuer: QK(0), then per tile QK(j+1) (once K(j+1) landed)
+//           and PV(j) (once P(j) is published).
 //   warps 0-3: softmax, thread = query row = TMEM lane; P(j) packed to 16 bits over the
-//           first 32 columns of its S buffer; lazy O rescale (max grows by > 2^8) after
+//           first 64 columns of its S buffer; lazy O rescale (max grows by > 2^8) after
 //           waiting for PV(j-1); epilogue O / l * sigmoid(G).
 // The issuing thread keeps the tensor pipe busy only while it is issuing: every barrier
 // wait or commit it makes between MMAs idles the pipe for ~50-150 cycles, wherever it is
-// placed.  Per tile the MMA thread therefore waits once (P(j), which the softmax warps
-// publish only after they have seen stage j land) and commits once: done[j & 1] marks
-// PV(j) and QK(j+2) complete, which is at once "S(j+2) ready" for the softmax, "slots of
-// V(j) and K(j+2) free" for the producer, and "PV(j) done" for a rescale of O.
+// placed.  Per 128-key tile it waits twice (K(j+1) landed; P(j), which the softmax warps
+// publish only after they have seen V(j) land) and commits twice (S(j+1) ready, which also
+// frees the K slot; PV(j) done, which frees the V slot and lets O be rescaled).
 // Every mbarrier wait is bounded (common.cuh).
 #include "common.cuh"
 #include "errwords.h"
@@ -39,29 +39,27 @@ __device__ int g_err_attn_gated = 0;
 
 constexpr int D = 256;
 constexpr int BM = 128;   // query rows per CTA
-constexpr int BN = 64;    // keys per tile
+constexpr int BN = 128;   // keys per tile
 constexpr int kThreads = 192;
 constexpr int kWarpProducer = 4, kWarpMma = 5;
 constexpr uint32_t kTmemCols = 512;
-// S buffers at 0 and 64, O at 128..383, Q at 384..511 (two 16-bit values a column): the
-// QK^T products take Q from TMEM, so per key tile shared memory carries only K and V
-constexpr uint32_t kColS = 0, kColO = 128, kColQ = 384;
+// S in two 128-column buffers (columns 0 and 128), O at 256..511; Q stays in shared memory
+constexpr uint32_t kColS = 0, kColO = 256;
 constexpr float kRescaleThreshold = 8.0f;
 
-// shared layout: Q [4 boxes of 128 rows x 64 cols], K and V rings [2][4 boxes of 64 x 64]
-constexpr int kQBytes = BM * D * 2;      // 64 KiB
-constexpr int kKVBytes = BN * D * 2;     // 32 KiB a stage
-constexpr int kQ = 0, kK = kQ + kQBytes, kV = kK + 2 * kKVBytes, kBar = kV + 2 * kKVBytes;
+// shared layout: Q, K and V, each four 128-byte-swizzled boxes of 128 rows x 64 columns, one
+// slot each: K(j+1) streams in once QK(j) has read K(j), V(j+1) once PV(j) has read V(j)
+constexpr int kQBytes = BM * D * 2;    // 64 KiB
+constexpr int kKVBytes = BN * D * 2;   // 64 KiB
+constexpr int kQ = 0, kK = kQ + kQBytes, kV = kK + kKVBytes, kBar = kV + kKVBytes;
 
-// done[s] completes its n-th phase when QK(s + 2n) has completed, together with every MMA
-// issued before it (PV(s + 2n - 2) among them); the prologue commits QK(0) and QK(1).
 struct Bars {
     uint64_t q_full;
-    uint64_t k_pro;       // K(0) and K(1) landed
-    uint64_t kv_full[2];  // stage j: V(j) (and K(j+2)) landed in slot j & 1
-    uint64_t done[2];
-    uint64_t p_full[2];
-    uint64_t q_tmem;  // the softmax warps have copied Q into TMEM
+    uint64_t k_full;     // K(j) landed: phase j
+    uint64_t v_full;     // V(j) landed: phase j
+    uint64_t s_full[2];  // QK(j) complete (S(j) ready, K slot free): buffer j & 1, phase j >> 1
+    uint64_t pv_done;    // PV(j) complete (V slot free, O up to date): phase j
+    uint64_t p_full;     // P(j) written, V(j) seen landed: phase j
     uint64_t o_final, drain;
     uint32_t tmem_base;
     int abort;
@@ -80,6 +78,12 @@ struct Params {
 __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float y;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(y) : "f"(a), "f"(b), "f"(c));
     return y;
 }
 
@@ -121,13 +125,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (threadIdx.x == 0) {
         mbar_init(&bars->q_full, 1);
-        mbar_init(&bars->k_pro, 1);
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&bars->kv_full[i], 1);
-            mbar_init(&bars->done[i], 1);
-            mbar_init(&bars->p_full[i], 4);  // one arrival per softmax warp
-        }
-        mbar_init(&bars->q_tmem, 4);
+        mbar_init(&bars->k_full, 1);
+        mbar_init(&bars->v_full, 1);
+        mbar_init(&bars->s_full[0], 1);
+        mbar_init(&bars->s_full[1], 1);
+        mbar_init(&bars->pv_done, 1);
+        mbar_init(&bars->p_full, 4);  // one arrival per softmax warp
         mbar_init(&bars->o_final, 1);
         mbar_init(&bars->drain, 1);
         bars->abort = 0;
@@ -143,95 +146,84 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = bars->tmem_base;
 
     if (warp == kWarpProducer) {
+        // lane 0 streams Q and the K tiles, lane 1 the V tiles: each waits only for the
+        // product that frees its slot
+        const int bh_q = b * p.Hq + hq;
+        const int bh_kv = b * (p.Hq / p.group) + hq / p.group;
+        auto load4 = [&](uint8_t* dst, const CUtensorMap* map, uint64_t* bar, int row, int z) {
+#pragma unroll
+            for (int a = 0; a < D / 64; ++a) tma_load_3d(dst + a * BN * 128, map, bar, a * 64, row, z);
+        };
         if (lane == 0) {
             prefetch_tmap(&tmQ);
             prefetch_tmap(&tmK);
-            prefetch_tmap(&tmV);
-            const int bh_q = b * p.Hq + hq;
-            const int bh_kv = b * (p.Hq / p.group) + hq / p.group;
             mbar_arrive_expect_tx(&bars->q_full, kQBytes);
-#pragma unroll
-            for (int a = 0; a < D / 64; ++a)
-                tma_load_3d(smem + kQ + a * BM * 128, &tmQ, &bars->q_full, a * 64, q0, bh_q);
-            auto load_k = [&](int j, int slot, uint64_t* bar) {
-#pragma unroll
-                for (int a = 0; a < D / 64; ++a)
-                    tma_load_3d(smem + kK + slot * kKVBytes + a * BN * 128, &tmK, bar, a * 64, j * BN, bh_kv);
-            };
-            const int npro = min(2, nkv);
-            if (npro > 0) {
-                mbar_arrive_expect_tx(&bars->k_pro, npro * kKVBytes);
-                for (int j = 0; j < npro; ++j) load_k(j, j, &bars->k_pro);
-            }
-            int issued = 0;  // stages whose loads were issued
+            load4(smem + kQ, &tmQ, &bars->q_full, q0, bh_q);
+            int issued = 0;
             for (int j = 0; j < nkv; ++j) {
-                const int st = j & 1;
-                const bool with_k = j + 2 < nkv;
-                // slot st of V held V(j-2) (read by PV(j-2)) and slot st of K holds K(j)
-                // (read by QK(j)): both are free once done[st] has completed phase j >> 1
-                if (j >= 2 && !mbar_wait(&bars->done[st], (j >> 1) & 1, abort, &g_err_attn_gated)) break;
-                mbar_arrive_expect_tx(&bars->kv_full[st], with_k ? 2 * kKVBytes : kKVBytes);
-#pragma unroll
-                for (int a = 0; a < D / 64; ++a)
-                    tma_load_3d(smem + kV + st * kKVBytes + a * BN * 128, &tmV, &bars->kv_full[st], a * 64,
-                                j * BN, bh_kv);
+                // the K slot held K(j-1): free once QK(j-1) has completed
+                if (j > 0 && !mbar_wait(&bars->s_full[(j - 1) & 1], ((j - 1) >> 1) & 1, abort, &g_err_attn_gated))
+                    break;
+                mbar_arrive_expect_tx(&bars->k_full, kKVBytes);
+                load4(smem + kK, &tmK, &bars->k_full, j * BN, bh_kv);
                 issued = j + 1;
-                if (with_k) {
-                    if (j < 2 && !mbar_wait(&bars->done[st], 0, abort, &g_err_attn_gated)) break;
-                    load_k(j + 2, st, &bars->kv_full[st]);
-                }
             }
-            // drain: every TMA load issued has landed before exit (a stage whose K load was
-            // skipped by an abort never completes; its wait gives up on the abort flag)
+            // drain: every load issued has landed before exit (one K load is in flight at most)
             mbar_wait(&bars->q_full, 0, abort, &g_err_attn_gated);
-            if (npro > 0) mbar_wait(&bars->k_pro, 0, abort, &g_err_attn_gated);
-            for (int j = max(0, issued - 2); j < issued; ++j)
-                mbar_wait(&bars->kv_full[j & 1], (j >> 1) & 1, abort, &g_err_attn_gated);
+            if (issued > 0) mbar_wait(&bars->k_full, (issued - 1) & 1, abort, &g_err_attn_gated);
+        } else if (lane == 1) {
+            prefetch_tmap(&tmV);
+            int issued = 0;
+            for (int j = 0; j < nkv; ++j) {
+                // the V slot held V(j-1): free once PV(j-1) has completed
+                if (j > 0 && !mbar_wait(&bars->pv_done, (j - 1) & 1, abort, &g_err_attn_gated)) break;
+                mbar_arrive_expect_tx(&bars->v_full, kKVBytes);
+                load4(smem + kV, &tmV, &bars->v_full, j * BN, bh_kv);
+                issued = j + 1;
+            }
+            if (issued > 0) mbar_wait(&bars->v_full, (issued - 1) & 1, abort, &g_err_attn_gated);
         }
     } else if (warp == kWarpMma) {
         if (lane == 0) {
             constexpr uint32_t kFmt = Elem<T>::kFmt;
             constexpr uint32_t idesc_qk = make_idesc(kFmt, BM, BN, false, false);
             constexpr uint32_t idesc_pv = make_idesc(kFmt, BM, D, false, true);
+            const uint64_t dq = smem_desc(smem_u32(smem + kQ), 16, 1024, kLayoutSW128);
             const uint64_t dk = smem_desc(smem_u32(smem + kK), 16, 1024, kLayoutSW128);
             const uint64_t dv = smem_desc(smem_u32(smem + kV), BN * 128, 1024, kLayoutSW128);
-            auto qk = [&](int j) {  // S[j & 1] = Q K_j^T  (M=128, N=64, K=256), Q from TMEM
-                const uint64_t ka = dk + (((j & 1) * kKVBytes) >> 4);
+            auto qk = [&](int j) {  // S[j & 1] = Q K_j^T  (M=128, N=128, K=256), both from shared
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
-                    const uint32_t ko = ((kk >> 2) * (BN * 128) + (kk & 3) * 32) >> 4;
-                    mma_f16_ts(tmem + kColS + (j & 1) * BN, tmem + kColQ + kk * 8, ka + ko, idesc_qk,
-                               kk > 0 ? 1u : 0u);
+                    const uint32_t o = ((kk >> 2) * (BM * 128) + (kk & 3) * 32) >> 4;  // BM == BN
+                    mma_f16_ss(tmem + kColS + (j & 1) * BN, dq + o, dk + o, idesc_qk, kk > 0 ? 1u : 0u);
                 }
             };
-            // (no key tile: the softmax warps copy no Q and nothing waits for it)
-            bool ok = nkv == 0 || (mbar_wait(&bars->q_tmem, 0, abort, &g_err_attn_gated) &&
-                                   mbar_wait(&bars->k_pro, 0, abort, &g_err_attn_gated));
+            bool ok = nkv == 0 || (mbar_wait(&bars->q_full, 0, abort, &g_err_attn_gated) &&
+                                   mbar_wait(&bars->k_full, 0, abort, &g_err_attn_gated));
             if (ok && nkv > 0) {
                 tc_fence_after();
                 qk(0);
-                mma_commit(&bars->done[0]);
-                if (nkv > 1) {
-                    qk(1);
-                    mma_commit(&bars->done[1]);
-                }
+                mma_commit(&bars->s_full[0]);
             }
             for (int j = 0; ok && j < nkv; ++j) {
-                const int st = j & 1;
-                const uint32_t ph = (j >> 1) & 1;
-                // P(j) implies stage j: the softmax warps saw it land before publishing P(j)
-                if (!mbar_wait(&bars->p_full[st], ph, abort, &g_err_attn_gated)) break;
+                if (j + 1 < nkv) {
+                    // S buffer (j+1) & 1 held P(j-1), which PV(j-1), issued before, has read
+                    if (!mbar_wait(&bars->k_full, (j + 1) & 1, abort, &g_err_attn_gated)) break;
+                    tc_fence_after();
+                    qk(j + 1);
+                    mma_commit(&bars->s_full[(j + 1) & 1]);
+                }
+                // P(j) implies V(j): the softmax warps saw it land before publishing P(j)
+                if (!mbar_wait(&bars->p_full, j & 1, abort, &g_err_attn_gated)) break;
                 tc_fence_after();
                 // O += P(j) V_j: P from TMEM (16 keys = 8 packed columns a step), V MN-major,
                 // its four 64-column boxes BN*128 bytes apart
-                const uint64_t va = dv + ((st * kKVBytes) >> 4);
+                const uint32_t tP = tmem + kColS + (j & 1) * BN;
 #pragma unroll
                 for (int kk = 0; kk < BN / 16; ++kk)
-                    mma_f16_ts(tmem + kColO, tmem + kColS + st * BN + kk * 8, va + ((kk * 16 * 128) >> 4),
-                               idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
-                // S buffer st is free once PV(j) has read P(j); the tensor pipe runs in order
-                if (j + 2 < nkv) qk(j + 2);
-                mma_commit(&bars->done[st]);
+                    mma_f16_ts(tmem + kColO, tP + kk * 8, dv + ((kk * 16 * 128) >> 4), idesc_pv,
+                               (j > 0 || kk > 0) ? 1u : 0u);
+                mma_commit(&bars->pv_done);
             }
             mma_commit(&bars->o_final);
             mma_commit(&bars->drain);
@@ -246,41 +238,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float sl2 = p.scale_log2;
         float m = -INFINITY, l = 0.f;
         bool ok = true;
-        if (nkv > 0) {
-            // Q row r (four 128B-swizzled 64-column boxes) -> TMEM columns kColQ.., two 16-bit
-            // values a column (low half = even k), the A layout of the QK^T MMAs
-            ok = __all_sync(0xffffffffu, mbar_wait(&bars->q_full, 0, abort, &g_err_attn_gated));
-#pragma unroll
-            for (int a = 0; a < D / 64; ++a) {
-                uint32_t w[32];
-                const uint8_t* qrow_s = smem + kQ + a * BM * 128 + r * 128;
-#pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    const uint4 v4 = *reinterpret_cast<const uint4*>(qrow_s + ((c ^ (r & 7)) << 4));
-                    w[4 * c + 0] = v4.x;
-                    w[4 * c + 1] = v4.y;
-                    w[4 * c + 2] = v4.z;
-                    w[4 * c + 3] = v4.w;
-                }
-                tmem_st32(tmem + lane_base + kColQ + a * 32, w);
-            }
-            tmem_st_wait();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->q_tmem);
-        }
         for (int j = 0; ok && j < nkv; ++j) {
             const int st = j & 1;
-            // S(j) = QK(j) complete: phase j >> 1 of done[st]
-            if (!__all_sync(0xffffffffu, mbar_wait(&bars->done[st], (j >> 1) & 1, abort, &g_err_attn_gated))) {
+            // S(j) = QK(j) complete: phase j >> 1 of s_full[st]
+            if (!__all_sync(0xffffffffu, mbar_wait(&bars->s_full[st], (j >> 1) & 1, abort, &g_err_attn_gated))) {
                 ok = false;
                 break;
             }
             tc_fence_after();
             const uint32_t tS = tmem + lane_base + kColS + st * BN;
             uint32_t sr[BN];
-            tmem_ld32(tS, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-            tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+#pragma unroll
+            for (int c = 0; c < BN / 32; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
             tmem_ld_wait();
             const int k0 = j * BN;
             if (k0 + BN - 1 > key_lim) {
@@ -288,12 +257,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int c = 0; c < BN; ++c)
                     if (k0 + c > key_lim) sr[c] = __float_as_uint(-INFINITY);
             }
-            float mx[4];
+            // row max: three-input max, eight independent chains (8 deep)
+            float mx[8];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) mx[u] = -INFINITY;
+            for (int u = 0; u < 8; ++u) mx[u] = -INFINITY;
 #pragma unroll
-            for (int c = 0; c < BN; ++c) mx[c & 3] = fmaxf(mx[c & 3], __uint_as_float(sr[c]));
-            const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * sl2;
+            for (int c = 0; c < BN; c += 16)
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    mx[u] = fmax3(mx[u], __uint_as_float(sr[c + 2 * u]), __uint_as_float(sr[c + 2 * u + 1]));
+            const float mt =
+                fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7])) * sl2;
             float alpha = 1.f;
             bool rescale = false;
             if (mt > m + kRescaleThreshold) {
@@ -304,23 +278,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                 m = mt;
             }
             const float neg_mb = (m == -INFINITY) ? 0.f : -m;
-            float2 rs[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};  // packed f32x2 partials
-            uint32_t pk[32];
+            float2 rs[4];  // row-sum partials, packed f32x2 adds
 #pragma unroll
-            for (int c2 = 0; c2 < BN / 2; ++c2) {
-                const float2 x = __ffma2_rn(make_float2(__uint_as_float(sr[2 * c2]), __uint_as_float(sr[2 * c2 + 1])),
-                                            make_float2(sl2, sl2), make_float2(neg_mb, neg_mb));
-                const float2 e = make_float2(ex2(x.x), ex2(x.y));
-                rs[c2 & 1] = __fadd2_rn(rs[c2 & 1], e);
-                pk[c2] = Elem<T>::pack2(e.x, e.y);
+            for (int u = 0; u < 4; ++u) rs[u] = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {  // 64 keys -> 32 packed columns at a time
+                uint32_t pk[32];
+#pragma unroll
+                for (int c2 = 0; c2 < 32; ++c2) {
+                    const int c = half * 64 + 2 * c2;
+                    const float2 x = __ffma2_rn(make_float2(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])),
+                                                make_float2(sl2, sl2), make_float2(neg_mb, neg_mb));
+                    const float2 e = make_float2(ex2(x.x), ex2(x.y));
+                    rs[c2 & 3] = __fadd2_rn(rs[c2 & 3], e);
+                    pk[c2] = Elem<T>::pack2(e.x, e.y);
+                }
+                tmem_st32(tS + half * 32, pk);
             }
-            tmem_st32(tS, pk);
-            // O may be rescaled only once PV(j-1) has finished (S(j) was computed earlier)
+            // O may be rescaled only once PV(j-1) has finished
             if (j > 0 && __any_sync(0xffffffffu, rescale)) {
-                // PV(j-1) complete: phase ((j - 1) >> 1) + 1 of done[(j - 1) & 1]
-                const int jp = j - 1;
-                if (!__all_sync(0xffffffffu, mbar_wait(&bars->done[jp & 1], ((jp >> 1) + 1) & 1, abort,
-                                                       &g_err_attn_gated))) {
+                if (!__all_sync(0xffffffffu, mbar_wait(&bars->pv_done, (j - 1) & 1, abort, &g_err_attn_gated))) {
                     ok = false;
                     break;
                 }
@@ -337,16 +314,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             tmem_st_wait();
-            l = l * alpha + ((rs[0].x + rs[0].y) + (rs[1].x + rs[1].y));
-            // P(j) is published only once stage j (V(j), K(j+2)) has landed, so the MMA thread
-            // waits once a tile (each wait it makes idles the tensor pipe)
-            if (!__all_sync(0xffffffffu, mbar_wait(&bars->kv_full[st], (j >> 1) & 1, abort, &g_err_attn_gated))) {
+            l = l * alpha + (((rs[0].x + rs[0].y) + (rs[1].x + rs[1].y)) + ((rs[2].x + rs[2].y) + (rs[3].x + rs[3].y)));
+            // P(j) is published only once V(j) has landed, so the MMA thread waits once for PV(j)
+            if (!__all_sync(0xffffffffu, mbar_wait(&bars->v_full, j & 1, abort, &g_err_attn_gated))) {
                 ok = false;
                 break;
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&bars->p_full[st]);
+            if (lane == 0) mbar_arrive(&bars->p_full);
         }
 
         // ---------------- epilogue: O / l * sigmoid(G) -------------------------------
