@@ -140,17 +140,19 @@ constexpr int kThreads = 128;
 // first MMA has read Q (so the first TMA wait covers K and Q only)
 constexpr int kTiles = 0;
 constexpr int kK0 = 0, kQ0 = 8192, kK1 = 16384, kQ1 = 24576, kV0 = kQ0, kV1 = kQ1;
-constexpr int kAT = 32768;         // [T diag(beta Gam); T diag(beta)] 128 x 64, 16 KiB
 constexpr int kLd = 68;            // fp32 row pitch of A and T (16-byte aligned, fewer conflicts)
-constexpr int kAs = 49152;         // A, then T = (I + A)^-1 in place, fp32 64 x kLd
+// One region, in turn: A, then T = (I + A)^-1 in place (fp32 64 x kLd; the block inverse's
+// 32 x 32 scratch sits in its upper-right block, zero in A and in T); then, once every thread
+// holds its row of T in registers, AT = [T diag(beta Gam); T diag(beta)] (16-bit 128 x 64, the
+// A operand of the W and U products); after those, the previous chunk's K (for M); last, M
+// staged for its store.
+constexpr int kAs = 32768;
+constexpr int kAT = kAs;
 constexpr int kMisc = kAs + kC * kLd * 4;
-constexpr int kXs = kMisc + 3072;  // 32 x 36 fp32 scratch of the block inverse (its own
-                                   // slot: AT is still being read by the Aqk store then)
-constexpr int kBytes = kXs + 32 * 36 * 4;
+constexpr int kBytes = kMisc + 3072;
 constexpr int kAlloc = kBytes + 1024;
-static_assert(3 * (kAlloc + 1024) <= 233472, "three prep CTAs per SM");
-static_assert(kAlloc <= 232448, "state kernel shared memory above the 227 KiB per-CTA limit");
-// 128 columns: three CTAs per SM fit the 512 TMEM columns without one waiting in
+static_assert(4 * (kAlloc + 1024) <= 233472, "four prep CTAs per SM");
+// 128 columns: four CTAs per SM fit the 512 TMEM columns without one waiting in
 // tcgen05.alloc for another to exit (W and U are produced one after the other)
 constexpr uint32_t kTmemCols = 128;
 
@@ -167,7 +169,7 @@ struct Misc {
     uint32_t tmem_base;
     int abort;
 };
-static_assert(sizeof(Misc) <= kXs - kMisc, "prep Misc overflows its slot");
+static_assert(sizeof(Misc) <= kBytes - kMisc, "prep Misc overflows its slot");
 }  // namespace prep
 
 __device__ __forceinline__ float ex2f(float x) {
@@ -226,7 +228,7 @@ __device__ __forceinline__ void diag_block_inverse(float* As, int warp, int lane
 
 // T21 = -T22 (A21 T11) once both diagonal blocks are inverted (all 128 threads; the caller
 // has synchronised the CTA after diag_block_inverse).
-__device__ __forceinline__ void offdiag_block_inverse(float* As, float* X, int tid) {
+__device__ __forceinline__ void offdiag_block_inverse(float* As, float* X, int xld, int tid) {
     using prep::kLd;
     float* Ts = As;
     // 128 threads x 8 outputs: row r = tid / 4, columns c0 .. c0 + 7 with c0 = (tid % 4) * 8
@@ -245,8 +247,8 @@ __device__ __forceinline__ void offdiag_block_inverse(float* As, float* X, int t
             acc[4] = fmaf(a, t1.x, acc[4]); acc[5] = fmaf(a, t1.y, acc[5]);
             acc[6] = fmaf(a, t1.z, acc[6]); acc[7] = fmaf(a, t1.w, acc[7]);
         }
-        *reinterpret_cast<float4*>(X + r * 36 + c0) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-        *reinterpret_cast<float4*>(X + r * 36 + c0 + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+        *reinterpret_cast<float4*>(X + r * xld + c0) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        *reinterpret_cast<float4*>(X + r * xld + c0 + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
     }
     __syncthreads();
     {   // T21 = -T22 X
@@ -256,8 +258,8 @@ __device__ __forceinline__ void offdiag_block_inverse(float* As, float* X, int t
 #pragma unroll
         for (int s = 0; s < 32; ++s) {
             const float a = Ts[(32 + r) * kLd + 32 + s];
-            const float4 x0 = *reinterpret_cast<const float4*>(X + s * 36 + c0);
-            const float4 x1 = *reinterpret_cast<const float4*>(X + s * 36 + c0 + 4);
+            const float4 x0 = *reinterpret_cast<const float4*>(X + s * xld + c0);
+            const float4 x1 = *reinterpret_cast<const float4*>(X + s * xld + c0 + 4);
             acc[0] = fmaf(a, x0.x, acc[0]); acc[1] = fmaf(a, x0.y, acc[1]);
             acc[2] = fmaf(a, x0.z, acc[2]); acc[3] = fmaf(a, x0.w, acc[3]);
             acc[4] = fmaf(a, x1.x, acc[4]); acc[5] = fmaf(a, x1.y, acc[5]);
@@ -270,7 +272,7 @@ __device__ __forceinline__ void offdiag_block_inverse(float* As, float* X, int t
 }
 
 template <typename T16, bool kFused>
-__global__ void __launch_bounds__(prep::kThreads, 3)
+__global__ void __launch_bounds__(prep::kThreads, 4)
     gdn_prep_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmW,
                     const __grid_constant__ CUtensorMap tmU, const __grid_constant__ CUtensorMap tmAqk,
@@ -282,7 +284,6 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
     Misc* ms = reinterpret_cast<Misc*>(smem + kMisc);
     float* As = reinterpret_cast<float*>(smem + kAs);
     const float* Ts = As;  // T replaces A in place
-    float* Xs = reinterpret_cast<float*>(smem + kXs);
     volatile int* abort = &ms->abort;
 
     const int c = blockIdx.x;   // chunk of the sequence
@@ -447,9 +448,9 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
             __syncwarp();  // this warp's 32 rows of A, which hold its whole diagonal block
             diag_block_inverse(As, warp, lane);
         } else {
-            // Aqk row (lower incl. diagonal), 16-bit, staged 128B-swizzled in the (not yet
-            // used) AT tile and written to the workspace by one TMA store
-            uint8_t* stg = smem + kAT + row * 128;
+            // Aqk row (lower incl. diagonal), 16-bit, straight to the workspace (row-major
+            // [64][64] a chunk item; the state pass loads it by TMA after this grid completes)
+            uint4* dst = reinterpret_cast<uint4*>(p.ws + p.ws_aqk + ((size_t)bhc * kC + row) * kC * 2);
 #pragma unroll
             for (int s = 0; s < kC; s += 8) {
                 uint4 pk;
@@ -465,16 +466,11 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
                     }
                     pw[u] = Elem<T16>::pack2(a0, a1);
                 }
-                *reinterpret_cast<uint4*>(stg + (((s >> 3) ^ (row & 7)) << 4)) = pk;
+                dst[s >> 3] = pk;
             }
-            fence_proxy_async_smem();
         }
     }
     __syncthreads();
-    if (tid == 64 && ok) {
-        tma_store_3d(&tmAqk, smem + kAT, 0, 0, (int)bhc);
-        bulk_commit();
-    }
 
     {
         const int j = tid & 63;
@@ -483,23 +479,27 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
             if (tid < kC) sc *= ms->rk[j];  // W = T diag(beta Gam / |k|) K
         ms->colscale[tid] = sc;
     }
-    offdiag_block_inverse(As, Xs, tid);  // contains __syncthreads: every thread calls it
-    if (tid == 64 && ok) {
-        bulk_wait_read();  // the Aqk store has read the AT tile, which is rewritten next
-    }
-    __syncthreads();
+    // the block inverse's scratch X is the upper-right 32 x 32 block (zero in A and in T)
+    offdiag_block_inverse(As, As + 32, kLd, tid);  // contains __syncthreads: every thread calls it
     {
-        // AT rows 0-63 <- T diag(beta Gam), rows 64-127 <- T diag(beta). Thread = AT row:
-        // eight 16-byte swizzled chunks of 8 columns each (conflict-free row reads of Ts,
-        // broadcast reads of the column scales)
+        // AT rows 0-63 <- T diag(beta Gam), rows 64-127 <- T diag(beta). Thread = AT row: its
+        // row of T (the upper-right block read as the zero it is in T) into registers, then,
+        // once every thread holds its row, eight 16-byte swizzled chunks of 8 columns over the
+        // same bytes (broadcast reads of the column scales)
         const int r = tid;
         const float* trow = Ts + (r & (kC - 1)) * kLd;
         const float* sc = ms->colscale + (r < kC ? 0 : kC);
+        float4 tr[kC / 4];
+#pragma unroll
+        for (int c4 = 0; c4 < kC / 4; ++c4)
+            tr[c4] = ((r & (kC - 1)) < 32 && c4 >= 8) ? make_float4(0.f, 0.f, 0.f, 0.f)
+                                                      : *reinterpret_cast<const float4*>(trow + c4 * 4);
+        __syncthreads();
         uint8_t* at = smem + kAT + r * 128;
 #pragma unroll
         for (int c8 = 0; c8 < 8; ++c8) {
-            const float4 a = *reinterpret_cast<const float4*>(trow + c8 * 8);
-            const float4 b = *reinterpret_cast<const float4*>(trow + c8 * 8 + 4);
+            const float4 a = tr[2 * c8];
+            const float4 b = tr[2 * c8 + 1];
             const float4 sa = *reinterpret_cast<const float4*>(sc + c8 * 8);
             const float4 sb = *reinterpret_cast<const float4*>(sc + c8 * 8 + 4);
             uint4 pk;
@@ -524,12 +524,6 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
     constexpr uint32_t idesc2 = make_idesc(Elem<T16>::kFmt, 128, 128, false, true);
     const uint32_t a0 = smem_u32(smem + kAT);
     if (tid == 0 && ok) {
-        if (c > 0) {
-            // K of the previous chunk into the (now dead) A tile, for M below
-            mbar_arrive_expect_tx(&ms->bar_kp, 2 * 8192);
-            tma_load_4d(smem + kAs, &tmK, &ms->bar_kp, 0, hq, tok0 - kC, 0);
-            tma_load_4d(smem + kAs + 8192, &tmK, &ms->bar_kp, 64, hq, tok0 - kC, 0);
-        }
         tc_fence_after();
         const uint32_t bk = smem_u32(smem + kK0);
 #pragma unroll
@@ -584,6 +578,13 @@ __global__ void __launch_bounds__(prep::kThreads, 3)
     }
     ok = __all_sync(0xffffffffu, mbar_wait(&ms->bar_mma2, 1, abort, &g_err_gdn_prefill)) && ok;
     tc_fence_after();
+    if (tid == 0 && ok && c > 0) {
+        // the W and U products have read AT: the previous chunk's K goes over it, for M below
+        // (in flight while warps 2-3 stage U)
+        mbar_arrive_expect_tx(&ms->bar_kp, 2 * 8192);
+        tma_load_4d(smem + kAs, &tmK, &ms->bar_kp, 0, hq, tok0 - kC, 0);
+        tma_load_4d(smem + kAs + 8192, &tmK, &ms->bar_kp, 64, hq, tok0 - kC, 0);
+    }
     if (ok && warp >= 2) stage_rows(smem + kV0);  // U -> [. | V0 | . | V1]
     tc_fence_before();
     __syncthreads();
