@@ -404,13 +404,27 @@ __global__ void __launch_bounds__(prep::kThreads, 4)
             mma_commit(&ms->bar_mma1);
         }
     }
-    ok = __all_sync(0xffffffffu, mbar_wait(&ms->bar_mma1, 0, abort, &g_err_gdn_prefill));
     if constexpr (kFused) {
-        // per-token 1/|k_t| and 1/|q_t| from the tiles, before V is loaded over Q
-        ok = __all_sync(0xffffffffu, mbar_wait(&ms->bar_tma, 0, abort, &g_err_gdn_prefill)) && ok;
-        if (tid < kC) ms->rk[tid] = row_rnorm<T16>(smem + kK0, smem + kK1, tid);
-        else ms->rq[tid - kC] = row_rnorm<T16>(smem + kQ0, smem + kQ1, tid - kC);
-        fence_proxy_async_smem();  // these reads of Q come before the V load's writes
+        // per-token 1/|q_t| from the Q tile while MMA1 runs (warps 2-3); these reads of Q come
+        // before the V load's writes over it
+        ok = __all_sync(0xffffffffu, mbar_wait(&ms->bar_tma, 0, abort, &g_err_gdn_prefill));
+        if (tid >= kC) ms->rq[tid - kC] = row_rnorm<T16>(smem + kQ0, smem + kQ1, tid - kC);
+        fence_proxy_async_smem();
+    }
+    ok = __all_sync(0xffffffffu, mbar_wait(&ms->bar_mma1, 0, abort, &g_err_gdn_prefill)) && ok;
+    if constexpr (kFused) {
+        // 1/|k_t| from the diagonal of K K^T, which MMA1 has just made (lanes 0-63): warp w holds
+        // rows 32w .. 32w + 31, so its diagonal lies in columns 32w .. 32w + 31
+        if (warp < 2) {
+            tc_fence_after();
+            uint32_t d[32];
+            tmem_ld32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + warp * 32, d);
+            tmem_ld_wait();
+            float kk = 0.f;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) kk = (i == lane) ? __uint_as_float(d[i]) : kk;
+            ms->rk[tid] = ok ? rsqrtf(kk + kNormEps) : 1.f;
+        }
         __syncthreads();
     }
     if (tid == 0 && ok) {
