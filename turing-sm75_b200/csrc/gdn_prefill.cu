@@ -1181,49 +1181,50 @@ __device__ __forceinline__ void cp_wait() {
 // their sums added through shared memory; packed f32x2 FMAs.  The starts of segments
 // 1 .. nseg-1 go to sst ([B][Hv][nseg][k][j], bf16: the correction's MMA operand), the last
 // segment's end state to the caller's state ([v][k] as everywhere else).  P_g (64 KiB, the
-// transition columns' end states, contiguous in seg_x) is double-buffered in shared memory:
-// P_{g+1} streams in while P_g is used.
+// transition columns' end states, contiguous in seg_x) and the CTA's 8 rows of S_zero_g (4 KiB)
+// are double-buffered in shared memory: step g+1's operands stream in while step g runs, so no
+// step waits on a global load.
 namespace seglink {
 constexpr int kThreads = 2 * kD;
-constexpr int kSmem = 2 * kD * kD * 4 + kD * 8 * 4 + kD * 8 * 4;
+constexpr int kZero = 2 * kD * kD;              // float offset of the S_zero rows, 2 x [8][kD]
+constexpr int kCur = kZero + 2 * 8 * kD;        // S_start(g) [kD][8]
+constexpr int kPart = kCur + kD * 8;            // second half's sums [kD][8]
+constexpr int kSmem = (kPart + kD * 8) * 4;
+static_assert(kThreads * 4 == 8 * kD, "one 16-byte copy a thread moves the 8 S_zero rows");
 }  // namespace seglink
 __global__ void __launch_bounds__(seglink::kThreads) gdn_seg_link_kernel(const float* __restrict__ seg_x,
                                                                          __nv_bfloat16* __restrict__ sst,
                                                                          float* __restrict__ state, int Hv,
                                                                          int nseg) {
     extern __shared__ __align__(16) float lsm[];
-    float (*cur)[8] = reinterpret_cast<float (*)[8]>(lsm + 2 * kD * kD);          // S_start(g)[k'][j0 ..]
-    float (*part)[8] = reinterpret_cast<float (*)[8]>(lsm + 2 * kD * kD + kD * 8);  // second half's sums
+    float (*cur)[8] = reinterpret_cast<float (*)[8]>(lsm + seglink::kCur);    // S_start(g)[k'][j0 ..]
+    float (*part)[8] = reinterpret_cast<float (*)[8]>(lsm + seglink::kPart);  // second half's sums
     grid_dependency_wait();    // the state pass's end states (a programmatic dependent launch)
     allow_dependent_launch();  // the correction kernel waits for this grid in turn
     const int j0 = blockIdx.x * 8, h = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x, k = tid & (kD - 1), half = tid >> 7;
     const size_t bh = (size_t)b * Hv + h;
-    auto fetch_P = [&](int g, int buf) {  // P_g^T (row kp = column kp's end state) -> buffer
+    auto fetch = [&](int g, int buf) {  // P_g^T (row kp = column kp's end state), S_zero_g rows j0 ..
         const float4* src = reinterpret_cast<const float4*>(seg_x + ((bh * nseg + g) * 2 + 1) * kD * kD);
         float4* dst = reinterpret_cast<float4*>(lsm + buf * kD * kD);
 #pragma unroll
         for (int m = 0; m < kD * kD / 4 / seglink::kThreads; ++m)
             cp16(dst + m * seglink::kThreads + tid, src + m * seglink::kThreads + tid);
+        const int zr = tid >> 5, zc = 4 * (tid & 31);  // row j0 + zr, keys zc .. zc + 3
+        cp16(lsm + seglink::kZero + buf * 8 * kD + zr * kD + zc,
+             seg_x + (bh * nseg + g) * 2 * kD * kD + (size_t)(j0 + zr) * kD + zc);
         cp_commit();
     };
-    fetch_P(1, 0);
+    fetch(1, 0);
     const float* X0 = seg_x + bh * nseg * 2 * kD * kD;  // X^T rows v, columns k
     float sv[8];
 #pragma unroll
     for (int u = 0; u < 8; ++u) sv[u] = X0[(size_t)(j0 + u) * kD + k];
     for (int g = 1; g < nseg; ++g) {
         const int buf = (g - 1) & 1;
-        if (g + 1 < nseg) fetch_P(g + 1, buf ^ 1);
-        else cp_commit();  // an empty group keeps the count: P_g is then the second newest
-        const float* Xg = seg_x + (bh * nseg + g) * 2 * kD * kD;
-        float2 acc[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) acc[u] = make_float2(0.f, 0.f);
+        if (g + 1 < nseg) fetch(g + 1, buf ^ 1);
+        else cp_commit();  // an empty group keeps the count: step g's group is then the second newest
         if (half == 0) {
-#pragma unroll
-            for (int u = 0; u < 4; ++u)  // S_zero_g[k][j]
-                acc[u] = make_float2(Xg[(size_t)(j0 + 2 * u) * kD + k], Xg[(size_t)(j0 + 2 * u + 1) * kD + k]);
 #pragma unroll
             for (int u = 0; u < 8; ++u) cur[k][u] = sv[u];
             uint4 pk;
@@ -1234,7 +1235,12 @@ __global__ void __launch_bounds__(seglink::kThreads) gdn_seg_link_kernel(const f
             *reinterpret_cast<uint4*>(sst + ((bh * nseg + g) * kD + k) * kD + j0) = pk;
         }
         cp_wait<1>();
-        __syncthreads();  // every thread's copies of P_g and the rows of cur are visible
+        __syncthreads();  // every thread's copies of P_g, S_zero_g and the rows of cur are visible
+        float2 acc[4];
+        const float* Z = lsm + seglink::kZero + buf * 8 * kD;
+#pragma unroll
+        for (int u = 0; u < 4; ++u)  // S_zero_g[k][j] seeds the first half's sums
+            acc[u] = half == 0 ? make_float2(Z[(2 * u) * kD + k], Z[(2 * u + 1) * kD + k]) : make_float2(0.f, 0.f);
         const float* sP = lsm + buf * kD * kD;
         const int kp0 = half * (kD / 2);
 #pragma unroll 8
@@ -1290,7 +1296,10 @@ __global__ void __launch_bounds__(segfix::kThreads) gdn_seg_fix_kernel(const __g
                                                                        int seg_len, int nseg) {
     using namespace segfix;
     extern __shared__ uint8_t xsm_raw[];
-    grid_dependency_wait();  // R, O_zero (state pass) and the segment starts (link kernel)
+    // Launched as a programmatic dependent of the link kernel, whose CTAs allow this launch only
+    // after their own griddepcontrol.wait on the state pass: the state pass has completed and
+    // flushed by the time any CTA here starts, so R and O_zero are read at once; the segment
+    // starts (the link kernel's results) only after this grid's own wait.
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(xsm_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bar_ld = reinterpret_cast<uint64_t*>(smem + kBar);
     uint64_t* bar_mma = bar_ld + 1;
@@ -1327,6 +1336,7 @@ __global__ void __launch_bounds__(segfix::kThreads) gdn_seg_fix_kernel(const __g
         mbar_arrive_expect_tx(bar_ld, 4 * 16384);
         tma_load_4d(smem + kA, &tmR, bar_ld, 0, h, tok, 0);
         tma_load_4d(smem + kA + 16384, &tmR, bar_ld, 64, h, tok, 0);
+        grid_dependency_wait();  // the segment starts
         tma_load_3d(smem + kB, &tmS, bar_ld, 0, 0, sg);
         tma_load_3d(smem + kB + 16384, &tmS, bar_ld, 64, 0, sg);
         ok = mbar_wait(bar_ld, 0, abort, &g_err_gdn_prefill);
@@ -1350,6 +1360,7 @@ __global__ void __launch_bounds__(segfix::kThreads) gdn_seg_fix_kernel(const __g
 #pragma unroll
     for (int q = 0; q < kD / 4; ++q)
         zr[q] = live ? reinterpret_cast<const float4*>(seg_o + row * kD)[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+    grid_dependency_wait();  // (thread 0 passed it above) nothing is stored before the link kernel ends
     // (a load that timed out set the abort flag: then nothing is stored)
     ok = __all_sync(0xffffffffu, mbar_wait(bar_mma, 0, abort, &g_err_gdn_prefill) && *abort == 0);
     tc_fence_after();
