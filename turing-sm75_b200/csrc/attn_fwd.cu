@@ -81,11 +81,22 @@ struct Layout {
     static constexpr int kQ = 0;
     static constexpr int kK = kQ + kQTiles * kQTileBytes;
     static constexpr int kV = kK + kStages * kKVBytes;
-    static constexpr int kBar = kV + kStages * kKVBytes;
+    // Head dim 64: the row sums of P come from the PV product itself, N = D + 16, whose
+    // columns D .. D+15 read a 64-column swizzle block of ones placed after the V stages (the
+    // descriptor's leading byte offset, one descriptor a stage); O_t column D is then the
+    // running sum, rescaled with O.  The MMAs have slack at D = 64, the softmax (issue-bound)
+    // drops its packed add a pair.  At D = 128 TMEM has no room for the extra columns.
+    static constexpr bool kRowSumMma = D == 64;
+    static constexpr int kOnes = kV + kStages * kKVBytes;
+    static constexpr int kOnesBytes = kRowSumMma ? BN * 128 : 0;
+    static constexpr int kBar = kOnes + kOnesBytes;
     static constexpr int kBytes = kBar + (int)sizeof(Bars);
     static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
     static_assert(kAlloc <= 232448, "shared memory budget");
-    static constexpr uint32_t kTmemO = 256;       // O_t at kTmemO + t*D
+    static constexpr int kOCols = kRowSumMma ? D + 16 : D;  // TMEM columns of an O tile
+    static constexpr uint32_t kTmemO = 256;                  // O_t at kTmemO + t*kOCols
+    static_assert(kTmemO + kQTiles * kOCols <= kTmemCols, "TMEM columns");
+    static_assert(kOnes % 1024 == 0, "swizzled operand base");
 };
 
 struct Params {
@@ -233,6 +244,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         bars->abort = 0;
         fence_barrier_init();
     }
+    if constexpr (L::kRowSumMma) {  // the tile of ones, made visible to the tensor core
+        const uint32_t one2 = Elem<T>::pack2(1.f, 1.f);
+        uint4* ones = reinterpret_cast<uint4*>(smem + L::kOnes);
+        for (int i = threadIdx.x; i < L::kOnesBytes / 16; i += kThreads) ones[i] = make_uint4(one2, one2, one2, one2);
+        fence_proxy_async_smem();
+    }
     if (warp == kWarpMma) {
         tmem_alloc(&bars->tmem_base, kTmemCols);
         tmem_relinquish();
@@ -305,12 +322,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             constexpr uint32_t kFmt = Elem<T>::kFmt;
             constexpr uint32_t idesc_qk = make_idesc(kFmt, BM, BN, false, false);
-            constexpr uint32_t idesc_pv = make_idesc(kFmt, BM, D, false, true);
+            constexpr uint32_t idesc_pv = make_idesc(kFmt, BM, L::kOCols, false, true);
             // Descriptors are built once; per K-step only the start-address field
             // (bits 0-13, address >> 4) advances, by a plain 64-bit add.
             const uint64_t dq0 = smem_desc(sQ, 16, 1024, kLayoutSW128);
             const uint64_t dk0 = smem_desc(sK0, 16, 1024, kLayoutSW128);
             const uint64_t dv0 = smem_desc(sV0, BN * 128, 1024, kLayoutSW128);
+            // D = 64: the block after each V stage's columns is the tile of ones
+            const uint64_t dv1s[2] = {smem_desc(sV0, L::kOnes - L::kV, 1024, kLayoutSW128),
+                                      smem_desc(sV0 + L::kKVBytes, L::kOnes - L::kV - L::kKVBytes, 1024,
+                                                kLayoutSW128)};
             auto qk = [&](int t, int j) {  // S_t = Q_t K_j^T
                 const uint64_t qa = dq0 + ((t * L::kQTileBytes) >> 4);
                 const uint64_t ka = dk0 + (((j & 1) * L::kKVBytes) >> 4);
@@ -323,11 +344,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             auto pv = [&](int t, int j) {  // O_t += P_t V_j, P from TMEM
                 // B = V tile [key][d], MN-major: 16 keys = two 8-row groups; 64-column
                 // boxes BN*128 bytes apart (the descriptor's leading byte offset).
-                const uint64_t va = dv0 + (((j & 1) * L::kKVBytes) >> 4);
+                const uint64_t va = L::kRowSumMma ? dv1s[j & 1] : dv0 + (((j & 1) * L::kKVBytes) >> 4);
 #pragma unroll
                 for (int kk = 0; kk < BN / 16; ++kk) {
-                    mma_f16_ts(tmem + L::kTmemO + t * D, tmem + t * BN + kk * 8, va + ((kk * 16 * 128) >> 4),
-                               idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+                    mma_f16_ts(tmem + L::kTmemO + t * L::kOCols, tmem + t * BN + kk * 8,
+                               va + ((kk * 16 * 128) >> 4), idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
                 }
             };
             bool ok = mbar_wait(&bars->q_full, 0, abort, &g_err_attn);
@@ -373,12 +394,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int r = (warp & 3) * 32 + lane;
         const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
         const uint32_t tS = tmem + lane_base + t * BN;
-        const uint32_t tO = tmem + lane_base + L::kTmemO + t * D;
+        const uint32_t tO = tmem + lane_base + L::kTmemO + t * L::kOCols;
         const int qrow = q0 + t * BM + r;
         const int key_lim = p.causal ? min(Skv - 1, (p.pack_sq ? qrow % p.pack_sq : qrow) + off) : (Skv - 1);
         const float sl2 = p.scale_log2;
         float m = -INFINITY;  // running max of scaled scores, log2 units
-        float l = 0.f;
+        float l = 0.f;  // (D = 64: O_t column D holds it, read in the epilogue)
         bool ok = true;
         // a warp whose 32 rows all lie past the queries (short or GQA-packed queries) writes no
         // P: it only keeps step with the tiles, so that its arrival is counted for the right one.
@@ -455,7 +476,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         e.x = ex2(x.x);
                         e.y = ex2(x.y);
                     }
-                    rs[c2 & 3] = __fadd2_rn(rs[c2 & 3], e);
+                    if constexpr (!L::kRowSumMma) rs[c2 & 3] = __fadd2_rn(rs[c2 & 3], e);
                     pk[c2] = Elem<T>::pack2(e.x, e.y);
                 }
                 tmem_st32(tS + half * 32, pk);
@@ -474,9 +495,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int u = 0; u < 32; ++u) o[u] = __float_as_uint(__uint_as_float(o[u]) * alpha);
                     tmem_st32(tO + c * 32, o);
                 }
+                if constexpr (L::kRowSumMma) {  // the running row sum in column D
+                    uint32_t lc;
+                    tmem_ld1(tO + D, lc);
+                    tmem_ld_wait();
+                    tmem_st1(tO + D, __float_as_uint(__uint_as_float(lc) * alpha));
+                }
             }
             tmem_st_wait();
-            l = l * alpha + rowsum;
+            if constexpr (!L::kRowSumMma) l = l * alpha + rowsum;
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars->p_full[t]);
@@ -486,6 +513,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ok && nkv > 0) {
             ok = __all_sync(0xffffffffu, mbar_wait(&bars->o_final, 0, abort, &g_err_attn));
             tc_fence_after();
+        }
+        if constexpr (L::kRowSumMma) {  // the row sum from O_t column D (warp-uniform condition)
+            if (ok && nkv > 0) {
+                uint32_t lc;
+                tmem_ld1(tO + D, lc);
+                tmem_ld_wait();
+                l = __uint_as_float(lc);
+            }
         }
         if constexpr (kSplit) {
             // split-KV partial: unnormalised O, running max and sum, fp32
